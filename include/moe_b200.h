@@ -1,0 +1,217 @@
+/*
+ * moe_b200.h -- C ABI of the B200 mixture-of-experts layer forward.
+ *
+ * Replaces the Python/NVRTC MoE FFN path of NightmareDesigns/Linuxnightmaresuite:
+ * moe_forward.py (MoERouter / ExpertFFN / MoELayer), the GGUF block decoders of
+ * dequant_fast.py and the per-expert GpuMM launches of qwen35_gpu.py that the
+ * streaming engines drive (nightmare_stream.py _moe_ffn_gpu / _moe_ffn_g4_gpu).
+ *
+ * Conventions
+ *   - Every function returns an int status: MOE_OK (0) or a negative MOE_ERR_*;
+ *     moe_last_error() returns the calling thread's last message.
+ *   - All tensor pointers are DEVICE pointers owned by the caller.  Nothing here
+ *     allocates device memory: scratch comes from a caller-provided workspace
+ *     whose size the matching *_workspace_bytes() reports.
+ *   - Work is enqueued asynchronously on the given stream (0 = legacy default).
+ *   - Weights enter as raw GGUF block bytes (Q4_0 = GGML type 2, Q8_0 = type 8),
+ *     expert-major, each matrix (rows, cols) row-major in the reference's
+ *     (out, in) orientation.  moe_pack_weights() rearranges them once, at load
+ *     time, into the tile order the expert kernels stream; the packed buffer
+ *     has exactly the size of the raw one and moe_unpack_weights() inverts it.
+ *   - Routing modes: MOE_ROUTE_TOPK_SOFTMAX follows MoERouter.route
+ *     (moe_forward.py:91-109); MOE_ROUTE_SOFTMAX_TOPK_RENORM follows
+ *     GPUStreamEngine._moe_ffn (nightmare_stream.py:3227-3238).  Ties between
+ *     equal scores go to the higher expert index first.
+ *   - Device-detected input errors (e.g. an out-of-range expert id) set bits in
+ *     the status word at the start of the workspace; moe_read_status() fetches it.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* moe_stream_t; /* same object as cudaStream_t */
+
+enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID = -1,     /* bad argument (null pointer, non-positive size, k > E) */
+  MOE_ERR_UNSUPPORTED = -2, /* quant type or shape this build does not handle */
+  MOE_ERR_WORKSPACE = -3,   /* workspace smaller than *_workspace_bytes() */
+  MOE_ERR_CUDA = -4,        /* a CUDA runtime call or kernel launch failed */
+  MOE_ERR_DEVICE = -5       /* moe_read_status found a device-side error bit */
+};
+
+enum { MOE_Q4_0 = 2, MOE_Q8_0 = 8 };  /* GGML type ids, dequant_fast.py:689-754 */
+
+enum { MOE_ROUTE_TOPK_SOFTMAX = 0, MOE_ROUTE_SOFTMAX_TOPK_RENORM = 1 };
+
+enum { MOE_ROUTER_D_E = 0, MOE_ROUTER_E_D = 1 }; /* router weight layout */
+
+/* device status bits */
+enum { MOE_STATUS_BAD_EXPERT_ID = 1, MOE_STATUS_ROW_OVERFLOW = 2, MOE_STATUS_TIMEOUT = 4 };
+
+/* ---- library ------------------------------------------------------------ */
+
+/* Library version, major*10000 + minor*100 + patch. */
+int moe_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated). */
+int moe_last_error(char* buf, size_t len);
+
+/* Weights per block and bytes per block of a GGML quant type.
+ * Replaces dequant_fast.BLOCK_SIZES (dequant_fast.py:723-754) for types 2 and 8. */
+int moe_block_geometry(int qtype, int* elems_per_block, int* bytes_per_block);
+
+/* Reads (and clears) the device status word a workspace carries. Synchronises
+ * the stream.  Returns MOE_ERR_DEVICE if any bit was set. */
+int moe_read_status(const void* workspace, int* status_out, moe_stream_t stream);
+
+/* ---- profiling (no counterpart in the reference) ---------------------------------
+ * When enabled, every kernel launch of the library is bracketed by a pair of
+ * CUDA events on its stream; moe_profile_collect() waits for them and returns,
+ * per kernel id, the summed device milliseconds and the number of launches,
+ * then resets.  Do not enable while capturing a CUDA graph. */
+enum {
+  MOE_K_ROUTER_PARTIAL = 0, MOE_K_ROUTER_SELECT, MOE_K_DISPATCH, MOE_K_PLAN, MOE_K_XPREP,
+  MOE_K_GATEUP, MOE_K_DOWN, MOE_K_COMBINE, MOE_K_RMS_NORM, MOE_K_PACK, MOE_K_DEQUANT,
+  MOE_K_AUX, MOE_K_COUNT
+};
+int moe_profile_enable(int on);
+int moe_profile_collect(float* ms, int* launches, int n);
+
+/* ---- weights ---------------------------------------------------------------- */
+
+/* Decodes n_elements weights of raw GGUF blocks to f32.  GPU counterpart of
+ * dequant_fast.dequantize_q4_0 / dequantize_q8_0 (dequant_fast.py:44-100) and of
+ * the dequant_q4_0 / dequant_q8_34 kernels (qwen35_gpu.py:610-648). */
+int moe_dequantize(const uint8_t* raw, float* out, int qtype, int64_t n_elements,
+                   moe_stream_t stream);
+
+/* Size in bytes of n_mats packed (rows, cols) matrices (== raw size). */
+int moe_packed_bytes(int qtype, int n_mats, int rows, int cols, size_t* bytes);
+
+/* Raw GGUF blocks of n_mats stacked (rows, cols) matrices -> packed tiles.
+ * Needs rows % 16 == 0 and cols % 64 == 0.  Replaces the raw expert upload of
+ * GpuMM.upload_raw (qwen35_gpu.py:1884-1924) / _load_expert_fast
+ * (nightmare_stream.py:3361-3441) as the load-time step. */
+int moe_pack_weights(const uint8_t* raw, uint8_t* packed, int qtype, int n_mats, int rows,
+                     int cols, moe_stream_t stream);
+
+/* Inverse of moe_pack_weights (bit-exact round trip). */
+int moe_unpack_weights(const uint8_t* packed, uint8_t* raw, int qtype, int n_mats, int rows,
+                       int cols, moe_stream_t stream);
+
+/* ---- router ------------------------------------------------------------------- */
+
+int moe_router_workspace_bytes(int T, int d, int E, size_t* bytes);
+
+/* Router logits, selection and weights for T tokens in one pass.
+ *   x        (T, d) f32
+ *   gate_w   (d, E) f32 for MOE_ROUTER_D_E (MoERouter.gate_weight, moe_forward.py:83)
+ *            or (E, d) for MOE_ROUTER_E_D (the production 'moe_router' tensor)
+ *   bias     (E,) f32 added to the logits, or NULL
+ *   ids      (T, k) int32 out, weights (T, k) f32 out, in the reference's order:
+ *            descending for MOE_ROUTE_TOPK_SOFTMAX, ascending for
+ *            MOE_ROUTE_SOFTMAX_TOPK_RENORM.
+ * Replaces MoERouter.route (moe_forward.py:91-109), the host softmax/argsort of
+ * nightmare_stream.py:3227-3238 / :3296-3306 and the router matvec_t launch
+ * (qwen35_gpu.py:39-47). */
+int moe_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
+               int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
+               size_t workspace_bytes, moe_stream_t stream);
+
+/* ---- dispatch ------------------------------------------------------------------ */
+
+int moe_dispatch_workspace_bytes(int T, int k, int E, size_t* bytes);
+
+/* Stable counting sort of the T*k (token, slot) pairs by expert id.
+ *   expert_offsets (E+1) out: rows of expert e are [off[e], off[e+1])
+ *   perm_rows (T*k) out: sorted row r holds pair perm_rows[r] = t*k + slot
+ *   inv_perm  (T*k) out: pair p sits at row inv_perm[p]
+ * Within an expert, pairs keep ascending (t, slot) order.  Ids outside [0,E)
+ * set MOE_STATUS_BAD_EXPERT_ID and are dropped (their inv_perm entry is -1).
+ * Replaces the per-token `for eid in top_idx` loops of moe_forward.py:166-168 and
+ * nightmare_stream.py:3240-3253. */
+int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offsets,
+                 int32_t* perm_rows, int32_t* inv_perm, void* workspace,
+                 size_t workspace_bytes, moe_stream_t stream);
+
+/* ---- experts --------------------------------------------------------------------- */
+
+int moe_experts_workspace_bytes(int rows, int E_local, int d, int F, size_t* bytes);
+
+/* Grouped SwiGLU experts over expert-sorted rows:
+ *   y[r] = W_down[e] (silu(W_gate[e] x[r]) * (W_up[e] x[r]))   for r in expert e's rows.
+ *   w_gate, w_up   packed (E_local, F, d) stacks, w_down packed (E_local, d, F)
+ *   expert_offsets (E_local+1) row offsets (as moe_dispatch writes them)
+ *   x              activations; sorted row r reads x row
+ *                  (x_rows ? x_rows[r] / x_rows_div : r)
+ *   y              (.., d) f32 out; sorted row r writes y row (y_rows ? y_rows[r] : r)
+ *   rows           number of sorted rows (== expert_offsets[E_local])
+ * Replaces ExpertFFN.forward (moe_forward.py:129-133) and the per-expert
+ * matvec_q4_0 / matvec_q8_34 / kernel_silu_mul launches (qwen35_gpu.py:55-104,
+ * :904-910) of _moe_ffn_gpu (nightmare_stream.py:3308-3331). */
+int moe_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                const int32_t* expert_offsets, int E_local, int rows, const float* x,
+                const int32_t* x_rows, int x_rows_div, int d, int F, float* y,
+                const int32_t* y_rows, void* workspace, size_t workspace_bytes,
+                moe_stream_t stream);
+
+/* ---- combine ----------------------------------------------------------------------- */
+
+/* out[t] = sum_slot weights[t,slot] * y[inv_perm[t*k+slot]]  (+ shared[t]) (+ residual[t]),
+ * summed in slot order in f32.  shared / residual may be NULL.  out may alias
+ * residual.  Replaces `output += w * expert_out` and the shared-expert add
+ * (moe_forward.py:165-172) and kernel_add_scaled (qwen35_gpu.py:920-924). */
+int moe_combine(const float* y, const int32_t* inv_perm, const float* weights,
+                const float* shared, const float* residual, int T, int k, int d, float* out,
+                moe_stream_t stream);
+
+/* RMSNorm of moe_forward.rms_norm (moe_forward.py:34-40):
+ * out[t] = x[t] / sqrt(mean(x[t]^2) + eps) * weight. */
+int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, float* out,
+                 moe_stream_t stream);
+
+/* ---- whole layer ----------------------------------------------------------------------- */
+
+typedef struct moe_layer_weights {
+  const float* gate_w;   /* router weight, layout per router_layout */
+  const float* bias;     /* (E,) or NULL */
+  const uint8_t* w_gate; /* packed (E, F, d) */
+  const uint8_t* w_up;   /* packed (E, F, d) */
+  const uint8_t* w_down; /* packed (E, d, F) */
+  const uint8_t* s_gate; /* packed shared expert (1, Fs, d) or NULL */
+  const uint8_t* s_up;
+  const uint8_t* s_down;
+  int router_layout;
+  int qtype;
+  int shared_qtype;
+  int E, k, d, F, Fs;
+  int mode;
+} moe_layer_weights;
+
+int moe_layer_workspace_bytes(const moe_layer_weights* w, int T, size_t* bytes);
+
+/* MoELayer.forward (moe_forward.py:154-174) for T tokens:
+ * router -> dispatch -> grouped experts -> combine (+ shared expert).
+ *   out (T, d) f32; must not alias x.
+ *   residual (T, d) or NULL: added to the output (the transformer residual,
+ *   moe_forward.py:359 `x = x + ffn_out`); may alias out.
+ *   ids_out / weights_out (T, k) or NULL: receive the routing decisions.
+ * Replaces MoELayer.forward and the GPU engine's _moe_ffn_gpu
+ * (nightmare_stream.py:3280-3334) / _moe_ffn_gpu_native
+ * (nightmare_gpu_native.py:1542-1590). */
+int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* out,
+                      const float* residual, int32_t* ids_out, float* weights_out,
+                      void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

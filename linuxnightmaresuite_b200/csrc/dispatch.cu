@@ -1,0 +1,151 @@
+// Dispatch: stable counting sort of (token, slot) pairs by expert id.
+//
+// Replaces the per-token expert loops of moe_forward.py:166-168 and
+// nightmare_stream.py:3240-3253 with one permutation of all T*k pairs.  Rows of
+// expert e are contiguous and, inside an expert, pairs keep ascending
+// (token, slot) order, so the result is a pure function of the ids.
+//
+// One CTA of 32 warps; warp w owns a contiguous range of pairs.  No atomics:
+// within a 32-pair round, __match_any_sync groups lanes by expert and the
+// lowest lane of each group updates the warp's private counter for that
+// expert; counters are then prefix-summed over warps (in warp order) and over
+// experts, and a second pass ranks each pair inside its round.
+#include "moe_common.cuh"
+
+namespace moe {
+
+constexpr int kDispThreads = 1024;
+constexpr int kDispWarps = kDispThreads / 32;
+
+__global__ void __launch_bounds__(kDispThreads)
+dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restrict__ offsets,
+                int32_t* __restrict__ perm_rows, int32_t* __restrict__ inv_perm,
+                int* __restrict__ status) {
+  extern __shared__ int sm[];
+  int* wcnt = sm;                          // [kDispWarps][E]
+  int* etot = sm + kDispWarps * E;         // [E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int chunk = ((P + kDispWarps - 1) / kDispWarps + 31) / 32 * 32;
+  const int p0 = warp * chunk;
+  const int p1 = min(P, p0 + chunk);
+
+  for (int i = threadIdx.x; i < kDispWarps * E; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+
+  // pass 1: per-warp counts
+  for (int base = p0; base < p1; base += 32) {
+    int p = base + lane;
+    int e = -1;
+    if (p < p1) {
+      e = ids[p];
+      if (e < 0 || e >= E) {
+        set_status(status, MOE_STATUS_BAD_EXPERT_ID);
+        inv_perm[p] = -1;
+        e = -1;
+      }
+    }
+    unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (peers & lt_mask) == 0) wcnt[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // per-expert exclusive prefix over warps, then totals
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kDispWarps; ++w) {
+      int c = wcnt[w * E + e];
+      wcnt[w * E + e] = run;
+      run += c;
+    }
+    etot[e] = run;
+  }
+  __syncthreads();
+  // exclusive scan of etot over experts (single warp; E is small)
+  if (warp == 0) {
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      int e = e0 + lane;
+      int v = e < E ? etot[e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (e < E) {
+        etot[e] = carry + incl - v;
+        offsets[e] = carry + incl - v;
+      }
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) offsets[E] = carry;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kDispWarps * E; i += blockDim.x) wcnt[i] += etot[i % E];
+  __syncthreads();
+
+  // pass 2: stable ranks and scatter
+  for (int base = p0; base < p1; base += 32) {
+    int p = base + lane;
+    int e = -1;
+    if (p < p1) {
+      e = ids[p];
+      if (e < 0 || e >= E) e = -1;
+    }
+    unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      int pos = wcnt[warp * E + e] + __popc(peers & lt_mask);
+      perm_rows[pos] = p;
+      inv_perm[p] = pos;
+    }
+    __syncwarp();
+    if (e >= 0 && (peers & lt_mask) == 0) wcnt[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_dispatch_workspace_bytes(int T, int k, int E, size_t* bytes) {
+  MOE_REQUIRE(bytes, MOE_ERR_INVALID, "null output pointer");
+  (void)T;
+  (void)k;
+  (void)E;
+  *bytes = 256;  // the status word
+  return MOE_OK;
+}
+
+int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offsets,
+                 int32_t* perm_rows, int32_t* inv_perm, void* workspace,
+                 size_t workspace_bytes, moe_stream_t stream) {
+  using namespace moe;
+  MOE_REQUIRE(T >= 0 && k > 0 && E > 0, MOE_ERR_INVALID, "bad shape T=%d k=%d E=%d", T, k, E);
+  MOE_REQUIRE(expert_offsets && workspace, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(workspace_bytes >= 256, MOE_ERR_WORKSPACE, "dispatch workspace too small");
+  MOE_REQUIRE(E <= 1024, MOE_ERR_UNSUPPORTED, "expert count %d above 1024", E);
+  int64_t P = (int64_t)T * k;
+  MOE_REQUIRE(P < (1LL << 30), MOE_ERR_UNSUPPORTED, "too many pairs");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (P == 0) {
+    MOE_CUDA(cudaMemsetAsync(expert_offsets, 0, sizeof(int32_t) * (E + 1), s));
+    return MOE_OK;
+  }
+  MOE_REQUIRE(ids && perm_rows && inv_perm, MOE_ERR_INVALID, "null pointer");
+  size_t smem = sizeof(int) * ((size_t)kDispWarps * E + E);
+  if (smem > 48 * 1024) {
+    MOE_CUDA(cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+  }
+  {
+    ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
+    dispatch_kernel<<<1, kDispThreads, smem, s>>>(ids, (int)P, E, expert_offsets, perm_rows,
+                                                  inv_perm, static_cast<int*>(workspace));
+  }
+  return check_launch("dispatch");
+}
+
+}  // extern "C"

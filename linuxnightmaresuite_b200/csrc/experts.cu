@@ -1,0 +1,602 @@
+// Grouped SwiGLU experts over expert-sorted rows (decode / small-group path).
+//
+// ExpertFFN.forward (moe_forward.py:129-133) for every routed row at once:
+//   h = silu(W_gate x) * (W_up x),  y = W_down h.
+//
+// Kernels, per call:
+//   plan_kernel    active-expert list and 4-row group offsets from expert_offsets
+//   xprep_kernel   gathers each expert's rows, scales each row by a power of two
+//                  and splits it into fp16 hi + lo parts, laid out as m16n8k16
+//                  B fragments (4 rows x {hi, lo} = the 8 MMA columns)
+//   gateup_kernel  streams packed W_gate / W_up tiles with 128-bit loads,
+//                  dequantises them in registers to exact fp16 integers, runs
+//                  one pair of MMAs per 32-weight block into a zeroed
+//                  accumulator and adds it, times the block's fp16 scale, to the
+//                  fp32 running sum (so the weights are exact and only the
+//                  activations are split); SiLU(gate) * up in the epilogue,
+//                  written as fragments for the next GEMV
+//   down_kernel    the same for W_down, writing f32 rows of y
+// The fp16 hi/lo split keeps ~22 bits of each activation, which is what the
+// reference's f32 tolerance needs; a single fp16 rounding does not.
+#include <math.h>
+
+#include "moe_common.cuh"
+
+namespace moe {
+
+constexpr int kMaxCG = 4;                 // column groups (4 rows each) per pass
+constexpr float kHScale = 1.0f / 256.0f;  // hidden activations are stored / 256
+constexpr int kPlanThreads = 1024;
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float half_lo(uint32_t v) {
+  return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu)));
+}
+__device__ __forceinline__ float half_hi(uint32_t v) {
+  return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
+}
+
+// element of a 32-block held at register slot i (0..7) of lane-column t
+template <int QT>
+__device__ __forceinline__ constexpr int frag_elem_c(int t, int i) {
+  return QT == MOE_Q4_0 ? ((i < 4 ? 0 : 16) + 4 * t + ((i & 3) == 1 ? 2 : ((i & 3) == 2 ? 1 : (i & 3))))
+                        : 8 * t + i;
+}
+// inverse: element e -> (t, i)
+template <int QT>
+__device__ __forceinline__ void frag_pos(int e, int& t, int& i) {
+  if (QT == MOE_Q4_0) {
+    int hi = e >= 16;
+    int r = e & 15;
+    t = r >> 2;
+    int m = r & 3;                       // 0,1,2,3 -> slot 0,2,1,3
+    i = (hi ? 4 : 0) + (m == 1 ? 2 : (m == 2 ? 1 : m));
+  } else {
+    t = e >> 3;
+    i = e & 7;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// plan: active experts, group offsets, group -> expert map
+// ---------------------------------------------------------------------------
+__device__ int block_excl_scan(int v, int* sh, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) sh[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    sh[lane] = wi - w;
+    if (lane == 31) sh[32] = wi;
+  }
+  __syncthreads();
+  int res = sh[warp] + incl - v;
+  total = sh[32];
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(kPlanThreads)
+plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups,
+            int* __restrict__ n_active, int* __restrict__ active, int* __restrict__ goff,
+            int* __restrict__ gexp, int* __restrict__ status) {
+  __shared__ int sh[33];
+  const int e = threadIdx.x;
+  int n = 0;
+  if (e < E) {
+    n = offsets[e + 1] - offsets[e];
+    if (n < 0 || offsets[e] < 0 || offsets[e + 1] > rows) {
+      set_status(status, MOE_STATUS_ROW_OVERFLOW);
+      n = 0;
+    }
+  }
+  int ng = (n + 3) / 4;
+  int tot_g, tot_a;
+  int g0 = block_excl_scan(ng, sh, tot_g);
+  int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
+  bool overflow = tot_g > max_groups;
+  if (overflow && e == 0) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+  if (e < E) {
+    goff[e] = g0;
+    if (n > 0) active[a0] = e;
+    if (!overflow)
+      for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
+  }
+  if (e == 0) {
+    goff[E] = tot_g;
+    *n_active = overflow ? 0 : tot_a;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// xprep: one CTA of 4 warps per 4-row group; warp w handles row w of the group
+// ---------------------------------------------------------------------------
+template <int QT>
+__global__ void __launch_bounds__(128)
+xprep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
+             const int32_t* __restrict__ offsets, const int* __restrict__ goff,
+             const int* __restrict__ gexp, int E, int d, float* __restrict__ row_scale,
+             uint8_t* __restrict__ xfrag) {
+  const int G = blockIdx.x;
+  if (G >= goff[E]) return;
+  const int e = gexp[G];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = offsets[e] + 4 * (G - goff[e]) + warp;
+  const bool valid = r < offsets[e + 1];
+  const int nb = d / 32;
+  uint8_t* gbase = xfrag + (size_t)G * nb * 512 + warp * 64;
+  if (!valid) {
+    for (int b = lane; b < nb; b += 32) {
+      uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)  // 2 parts x 4 lane-columns
+        *reinterpret_cast<uint4*>(gbase + (size_t)b * 512 + (q >> 2) * 256 + (q & 3) * 16) = z;
+    }
+    return;
+  }
+  const int src_row = x_rows ? x_rows[r] / x_div : r;
+  const float4* src = reinterpret_cast<const float4*>(x + (size_t)src_row * d);
+  float m = 0.f;
+  for (int i = lane; i < d / 4; i += 32) {
+    float4 v = __ldg(src + i);
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float scale = 1.f, inv = 1.f;
+  if (m > 0.f && isfinite(m)) {
+    int ex = ilogbf(m);
+    scale = ldexpf(1.f, 14 - ex);   // max |x| * scale in [2^14, 2^15)
+    inv = ldexpf(1.f, ex - 14);
+  }
+  if (lane == 0) row_scale[r] = inv;
+  for (int b = lane; b < nb; b += 32) {
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 f = __ldg(src + b * 8 + q);
+      v[4 * q + 0] = f.x * scale;
+      v[4 * q + 1] = f.y * scale;
+      v[4 * q + 2] = f.z * scale;
+      v[4 * q + 3] = f.w * scale;
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        float a = v[frag_elem_c<QT>(t, i)];
+        float c = v[frag_elem_c<QT>(t, i + 1)];
+        __half ha = __float2half_rn(a), hc = __float2half_rn(c);
+        __half la = __float2half_rn(a - __half2float(ha));
+        __half lc = __float2half_rn(c - __half2float(hc));
+        hi[i / 2] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hc) << 16);
+        lo[i / 2] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lc) << 16);
+      }
+      uint8_t* dst = gbase + (size_t)b * 512 + t * 16;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(dst + 256) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// one 64-wide tile of a 16-row strip against ncg column groups
+// ---------------------------------------------------------------------------
+template <int QT>
+struct TileRegs {
+  uint4 q[QT == MOE_Q4_0 ? 1 : 2];
+  uint2 sc;
+};
+
+template <int QT>
+__device__ __forceinline__ void load_tile(TileRegs<QT>& r, const uint8_t* tile, int lane) {
+  using Tr = QTraits<QT>;
+  const uint8_t* qp = tile + lane * Tr::kLaneBytes;
+  r.q[0] = ldg_stream_v4(qp);
+  if (QT == MOE_Q8_0) r.q[QT == MOE_Q4_0 ? 0 : 1] = ldg_stream_v4(qp + 16);
+  r.sc = ldg_stream_v2(tile + Tr::kTileQuant + (lane >> 2) * 8);
+}
+
+// A fragments of both k16 steps for block b (rows g and g+8)
+template <int QT>
+__device__ __forceinline__ void tile_afrags(const TileRegs<QT>& r, int b, uint32_t (&a0)[4],
+                                            uint32_t (&a1)[4], float& dg, float& dg8) {
+  if (QT == MOE_Q4_0) {
+    uint32_t wg = b ? r.q[0].y : r.q[0].x;
+    uint32_t w8 = b ? r.q[0].w : r.q[0].z;
+    uint32_t l01, l23, h01, h23, m01, m23, n01, n23;
+    dequant_q4(wg, l01, l23, h01, h23);
+    dequant_q4(w8, m01, m23, n01, n23);
+    a0[0] = l01; a0[1] = m01; a0[2] = l23; a0[3] = m23;
+    a1[0] = h01; a1[1] = n01; a1[2] = h23; a1[3] = n23;
+  } else {
+    const uint4& qa = r.q[0];
+    const uint4& qb = r.q[QT == MOE_Q4_0 ? 0 : 1];
+    uint32_t g0 = b ? qa.z : qa.x, g1 = b ? qa.w : qa.y;
+    uint32_t e0 = b ? qb.z : qb.x, e1 = b ? qb.w : qb.y;
+    uint32_t x01, x23, y01, y23;
+    dequant_q8(g0, x01, x23);
+    dequant_q8(e0, y01, y23);
+    a0[0] = x01; a0[1] = y01; a0[2] = x23; a0[3] = y23;
+    dequant_q8(g1, x01, x23);
+    dequant_q8(e1, y01, y23);
+    a1[0] = x01; a1[1] = y01; a1[2] = x23; a1[3] = y23;
+  }
+  dg = b ? half_hi(r.sc.x) : half_lo(r.sc.x);
+  dg8 = b ? half_hi(r.sc.y) : half_lo(r.sc.y);
+}
+
+__device__ __forceinline__ void block_mma(float (&acc)[4], const uint32_t (&a0)[4],
+                                          const uint32_t (&a1)[4], uint4 xf, float dg,
+                                          float dg8) {
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+  float tmp[4];
+  mma_16816(tmp, a0[0], a0[1], a0[2], a0[3], xf.x, xf.y, zero);
+  mma_16816(tmp, a1[0], a1[1], a1[2], a1[3], xf.z, xf.w, tmp);
+  acc[0] = fmaf(dg, tmp[0], acc[0]);
+  acc[1] = fmaf(dg, tmp[1], acc[1]);
+  acc[2] = fmaf(dg8, tmp[2], acc[2]);
+  acc[3] = fmaf(dg8, tmp[3], acc[3]);
+}
+
+// ---------------------------------------------------------------------------
+// gate / up: CTA = 8 warps = (8 / ks) strips x ks K-slices
+// ---------------------------------------------------------------------------
+template <int QT>
+__global__ void __launch_bounds__(256)
+gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t mat_bytes,
+              int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
+              const int* __restrict__ active, const int* __restrict__ goff,
+              const float* __restrict__ row_scale, const uint8_t* __restrict__ xfrag,
+              uint8_t* __restrict__ hfrag, int ks, int* __restrict__ status) {
+  using Tr = QTraits<QT>;
+  __shared__ float red[8][kMaxCG * 8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int spc = 8 / ks;
+  const int strips = F / 16;
+  const int cpe = (strips + spc - 1) / spc;
+  const int a = blockIdx.x / cpe;
+  if (a >= *n_active) return;
+  const int e = active[a];
+  const int sl = warp / ks, kp = warp % ks;
+  const int s = (blockIdx.x % cpe) * spc + sl;
+  const bool strip_ok = s < strips;
+  const int JT = d / 64;
+  const int jb = kp * JT / ks, je = (kp + 1) * JT / ks;
+  const int row0 = offsets[e];
+  const int n = offsets[e + 1] - row0;
+  const int G0 = goff[e];
+  const int nbx = d / 32, nbF = F / 32;
+  const uint8_t* gbase = wg + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * Tr::kTileBytes;
+  const uint8_t* ubase = wu + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * Tr::kTileBytes;
+
+  for (int c0 = 0; c0 < n; c0 += 4 * kMaxCG) {
+    const int ncg = min(kMaxCG, (n - c0 + 3) / 4);
+    float accg[kMaxCG][4], accu[kMaxCG][4];
+#pragma unroll
+    for (int c = 0; c < kMaxCG; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) accg[c][i] = accu[c][i] = 0.f;
+    if (strip_ok) {
+      const uint8_t* xg = xfrag + (size_t)(G0 + c0 / 4) * nbx * 512 + lane * 16;
+#pragma unroll 2
+      for (int j = jb; j < je; ++j) {
+        TileRegs<QT> tg, tu;
+        load_tile<QT>(tg, gbase + (size_t)j * Tr::kTileBytes, lane);
+        load_tile<QT>(tu, ubase + (size_t)j * Tr::kTileBytes, lane);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          uint32_t ga0[4], ga1[4], ua0[4], ua1[4];
+          float dg, dg8, du, du8;
+          tile_afrags<QT>(tg, b, ga0, ga1, dg, dg8);
+          tile_afrags<QT>(tu, b, ua0, ua1, du, du8);
+#pragma unroll
+          for (int c = 0; c < kMaxCG; ++c) {
+            if (c < ncg) {
+              uint4 xf = __ldg(reinterpret_cast<const uint4*>(
+                  xg + ((size_t)c * nbx + 2 * j + b) * 512));
+              block_mma(accg[c], ga0, ga1, xf, dg, dg8);
+              block_mma(accu[c], ua0, ua1, xf, du, du8);
+            }
+          }
+        }
+      }
+    }
+    if (ks > 1) {
+      __syncthreads();
+#pragma unroll
+      for (int c = 0; c < kMaxCG; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          red[warp][c * 8 + i][lane] = accg[c][i];
+          red[warp][c * 8 + 4 + i][lane] = accu[c][i];
+        }
+      __syncthreads();
+      if (kp == 0) {
+        for (int q = 1; q < ks; ++q)
+#pragma unroll
+          for (int c = 0; c < kMaxCG; ++c)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              accg[c][i] += red[warp + q][c * 8 + i][lane];
+              accu[c][i] += red[warp + q][c * 8 + 4 + i][lane];
+            }
+      }
+    }
+    if (kp == 0 && strip_ok) {
+#pragma unroll
+      for (int c = 0; c < kMaxCG; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          accg[c][i] += __shfl_xor_sync(0xffffffffu, accg[c][i], 2);
+          accu[c][i] += __shfl_xor_sync(0xffffffffu, accu[c][i], 2);
+        }
+      if (t < 2) {
+#pragma unroll
+        for (int c = 0; c < kMaxCG; ++c) {
+          if (c >= ncg) continue;
+          const int G = G0 + c0 / 4 + c;
+#pragma unroll
+          for (int ci = 0; ci < 2; ++ci) {
+            const int rig = 2 * t + ci;              // row inside the group
+            const int tok = c0 + 4 * c + rig;
+            if (tok >= n) continue;
+            const float rs = row_scale[row0 + tok];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              float gv = accg[c][rr * 2 + ci] * rs;
+              float uv = accu[c][rr * 2 + ci] * rs;
+              float h = silu_f(gv) * uv;
+              float hs = h * kHScale;
+              if (!(fabsf(hs) <= 65504.f)) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+              __half hh = __float2half_rn(hs);
+              __half hl = __float2half_rn(hs - __half2float(hh));
+              const int f = s * 16 + g + 8 * rr;
+              int tf, fi;
+              frag_pos<QT>(f & 31, tf, fi);
+              uint8_t* dst = hfrag + ((size_t)G * nbF + (f >> 5)) * 512 + rig * 64 + tf * 16 + fi * 2;
+              *reinterpret_cast<__half*>(dst) = hh;
+              *reinterpret_cast<__half*>(dst + 256) = hl;
+            }
+          }
+        }
+      }
+    }
+    if (ks > 1) __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// down: CTA = 8 warps = 8 strips of d; K = F is short, no split
+// ---------------------------------------------------------------------------
+template <int QT>
+__global__ void __launch_bounds__(256)
+down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
+            const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
+            const int* __restrict__ active, const int* __restrict__ goff,
+            const uint8_t* __restrict__ hfrag, float* __restrict__ y,
+            const int32_t* __restrict__ y_rows) {
+  using Tr = QTraits<QT>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int strips = d / 16;
+  const int cpe = (strips + 7) / 8;
+  const int a = blockIdx.x / cpe;
+  if (a >= *n_active) return;
+  const int s = (blockIdx.x % cpe) * 8 + warp;
+  if (s >= strips) return;
+  const int e = active[a];
+  const int JT = F / 64;
+  const int row0 = offsets[e];
+  const int n = offsets[e + 1] - row0;
+  const int G0 = goff[e];
+  const int nbF = F / 32;
+  const uint8_t* base = wd + (size_t)e * mat_bytes + (size_t)s * JT * Tr::kTileBytes;
+  for (int c0 = 0; c0 < n; c0 += 4 * kMaxCG) {
+    const int ncg = min(kMaxCG, (n - c0 + 3) / 4);
+    float acc[kMaxCG][4];
+#pragma unroll
+    for (int c = 0; c < kMaxCG; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[c][i] = 0.f;
+    const uint8_t* hg = hfrag + (size_t)(G0 + c0 / 4) * nbF * 512 + lane * 16;
+#pragma unroll 2
+    for (int j = 0; j < JT; ++j) {
+      TileRegs<QT> tw;
+      load_tile<QT>(tw, base + (size_t)j * Tr::kTileBytes, lane);
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        uint32_t a0[4], a1[4];
+        float dw, dw8;
+        tile_afrags<QT>(tw, b, a0, a1, dw, dw8);
+#pragma unroll
+        for (int c = 0; c < kMaxCG; ++c) {
+          if (c < ncg) {
+            uint4 xf = __ldg(reinterpret_cast<const uint4*>(hg + ((size_t)c * nbF + 2 * j + b) * 512));
+            block_mma(acc[c], a0, a1, xf, dw, dw8);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kMaxCG; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[c][i] += __shfl_xor_sync(0xffffffffu, acc[c][i], 2);
+    if (t < 2) {
+#pragma unroll
+      for (int c = 0; c < kMaxCG; ++c) {
+        if (c >= ncg) continue;
+#pragma unroll
+        for (int ci = 0; ci < 2; ++ci) {
+          const int tok = c0 + 4 * c + 2 * t + ci;
+          if (tok >= n) continue;
+          const int r = row0 + tok;
+          const int orow = y_rows ? y_rows[r] : r;
+          float* yr = y + (size_t)orow * d + s * 16 + g;
+          yr[0] = acc[c][ci] * (1.0f / kHScale);
+          yr[8] = acc[c][2 + ci] * (1.0f / kHScale);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct ExpertsWs {
+  int* status;
+  int* n_active;
+  int* active;
+  int* goff;
+  int* gexp;
+  float* row_scale;
+  uint8_t* xfrag;
+  uint8_t* hfrag;
+  size_t bytes;
+};
+
+static int max_groups(int rows, int E) { return (rows + 3) / 4 + E; }
+
+static ExpertsWs carve_experts(void* ws, int rows, int E, int d, int F) {
+  Carve c{static_cast<uint8_t*>(ws), 0, 0};
+  ExpertsWs w;
+  const int mg = max_groups(rows, E);
+  w.status = c.take<int>(64);
+  w.n_active = c.take<int>(64);
+  w.active = c.take<int>(E);
+  w.goff = c.take<int>(E + 1);
+  w.gexp = c.take<int>(mg);
+  w.row_scale = c.take<float>(rows > 0 ? rows : 1);
+  w.xfrag = c.take<uint8_t>((size_t)mg * d * 16);
+  w.hfrag = c.take<uint8_t>((size_t)mg * F * 16);
+  w.bytes = align_up(c.used, 256);
+  return w;
+}
+
+int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
+  *bytes = carve_experts(nullptr, rows, E, d, F).bytes;
+  return MOE_OK;
+}
+
+// Launches the grouped experts with an already-carved workspace.
+template <int QT>
+static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down,
+                          const int32_t* offsets, int E, int rows, const float* x,
+                          const int32_t* x_rows, int x_div, int d, int F, float* y,
+                          const int32_t* y_rows, const ExpertsWs& w, cudaStream_t s) {
+  using Tr = QTraits<QT>;
+  const int mg = max_groups(rows, E);
+  {
+    ::moe::ProfScope _prof(MOE_K_PLAN, s);
+    plan_kernel<<<1, kPlanThreads, 0, s>>>(offsets, E, rows, mg, w.n_active, w.active, w.goff,
+                                           w.gexp, w.status);
+  }
+  MOE_CHECK(check_launch("plan"));
+  {
+    ::moe::ProfScope _prof(MOE_K_XPREP, s);
+    xprep_kernel<QT><<<mg, 128, 0, s>>>(x, x_rows, x_div, offsets, w.goff, w.gexp, E, d,
+                                        w.row_scale, w.xfrag);
+  }
+  MOE_CHECK(check_launch("xprep"));
+  const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
+  const int est_active = rows < E ? rows : E;
+  const int strips_f = F / 16;
+  const int JT = d / 64;
+  const int target = sm_count() * 16;  // resident warps to aim for
+  int ks = 1;
+  while (ks < 8 && (long long)est_active * strips_f * ks < target && JT / (2 * ks) >= 2) ks *= 2;
+  const int spc = 8 / ks;
+  const int gu_grid = est_active * ((strips_f + spc - 1) / spc);
+  {
+    ::moe::ProfScope _prof(MOE_K_GATEUP, s);
+    gateup_kernel<QT><<<gu_grid, 256, 0, s>>>(w_gate, w_up, mat_bytes, d, F, offsets, w.n_active,
+                                             w.active, w.goff, w.row_scale, w.xfrag, w.hfrag, ks,
+                                             w.status);
+  }
+  MOE_CHECK(check_launch("gateup"));
+  const int strips_d = d / 16;
+  const int dn_grid = est_active * ((strips_d + 7) / 8);
+  {
+    ::moe::ProfScope _prof(MOE_K_DOWN, s);
+    down_kernel<QT><<<dn_grid, 256, 0, s>>>(w_down, mat_bytes, d, F, offsets, w.n_active,
+                                            w.active, w.goff, w.hfrag, y, y_rows);
+  }
+  return check_launch("down");
+}
+
+int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
+                int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
+                size_t ws_bytes, cudaStream_t s, int* status) {
+  MOE_REQUIRE(qtype_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
+  MOE_REQUIRE(E > 0 && E <= kPlanThreads, MOE_ERR_UNSUPPORTED, "local expert count %d", E);
+  MOE_REQUIRE(d > 0 && F > 0 && d % 64 == 0 && F % 64 == 0, MOE_ERR_UNSUPPORTED,
+              "d=%d and F=%d must be multiples of 64", d, F);
+  MOE_REQUIRE(rows >= 0, MOE_ERR_INVALID, "rows must be >= 0");
+  if (rows == 0) return MOE_OK;
+  MOE_REQUIRE(w_gate && w_up && w_down && offsets && x && y && ws, MOE_ERR_INVALID,
+              "null pointer");
+  MOE_REQUIRE(x_div > 0, MOE_ERR_INVALID, "x_rows_div must be positive");
+  MOE_REQUIRE(((uintptr_t)w_gate | (uintptr_t)w_up | (uintptr_t)w_down | (uintptr_t)x) % 16 == 0,
+              MOE_ERR_INVALID, "weights and activations must be 16-byte aligned");
+  ExpertsWs w = carve_experts(ws, rows, E, d, F);
+  if (status) w.status = status;
+  MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "experts workspace %zu < %zu", ws_bytes,
+              w.bytes);
+  if (qtype == MOE_Q4_0)
+    return launch_experts<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div, d,
+                                    F, y, y_rows, w, s);
+  return launch_experts<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div, d,
+                                  F, y, y_rows, w, s);
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_experts_workspace_bytes(int rows, int E_local, int d, int F, size_t* bytes) {
+  MOE_REQUIRE(bytes, MOE_ERR_INVALID, "null output pointer");
+  MOE_REQUIRE(rows >= 0 && E_local > 0 && d > 0 && F > 0, MOE_ERR_INVALID, "bad shape");
+  return moe::experts_workspace(rows, E_local, d, F, bytes);
+}
+
+int moe_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                const int32_t* expert_offsets, int E_local, int rows, const float* x,
+                const int32_t* x_rows, int x_rows_div, int d, int F, float* y,
+                const int32_t* y_rows, void* workspace, size_t workspace_bytes,
+                moe_stream_t stream) {
+  return moe::run_experts(w_gate, w_up, w_down, qtype, expert_offsets, E_local, rows, x, x_rows,
+                          x_rows_div, d, F, y, y_rows, workspace, workspace_bytes,
+                          reinterpret_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // extern "C"

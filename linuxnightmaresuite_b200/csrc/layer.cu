@@ -1,0 +1,113 @@
+// Whole MoE layer: router -> dispatch -> grouped experts -> combine.
+// MoELayer.forward (moe_forward.py:154-174) for a batch of tokens.
+#include "moe_common.cuh"
+
+namespace moe {
+
+int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
+                int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
+                size_t ws_bytes, cudaStream_t s, int* status);
+int experts_workspace(int rows, int E, int d, int F, size_t* bytes);
+int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
+                   const float* residual, int T, int k, int d, float* out, cudaStream_t s);
+
+__global__ void fill_two_offsets(int32_t* off, int n) {
+  if (threadIdx.x == 0) {
+    off[0] = 0;
+    off[1] = n;
+  }
+}
+
+struct LayerWs {
+  int* status;
+  uint8_t* router_ws;
+  size_t router_bytes;
+  int32_t* ids;
+  float* wts;
+  int32_t* offsets;
+  int32_t* perm;
+  int32_t* inv;
+  uint8_t* exp_ws;
+  size_t exp_bytes;
+  float* y;
+  int32_t* s_off;
+  float* s_y;
+  size_t bytes;
+};
+
+static LayerWs carve_layer(void* ws, const moe_layer_weights* w, int T) {
+  Carve c{static_cast<uint8_t*>(ws), 0, 0};
+  LayerWs L;
+  const size_t P = (size_t)T * w->k;
+  L.status = c.take<int>(64);
+  moe_router_workspace_bytes(T, w->d, w->E, &L.router_bytes);
+  L.router_ws = c.take<uint8_t>(L.router_bytes);
+  L.ids = c.take<int32_t>(P);
+  L.wts = c.take<float>(P);
+  L.offsets = c.take<int32_t>(w->E + 1);
+  L.perm = c.take<int32_t>(P);
+  L.inv = c.take<int32_t>(P);
+  size_t eb = 0, sb = 0;
+  experts_workspace((int)P, w->E, w->d, w->F, &eb);
+  if (w->s_gate) experts_workspace(T, 1, w->d, w->Fs, &sb);
+  L.exp_bytes = eb > sb ? eb : sb;
+  L.exp_ws = c.take<uint8_t>(L.exp_bytes);
+  L.y = c.take<float>(P * w->d);
+  L.s_off = c.take<int32_t>(2);
+  L.s_y = w->s_gate ? c.take<float>((size_t)T * w->d) : nullptr;
+  L.bytes = align_up(c.used, 256);
+  return L;
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_layer_workspace_bytes(const moe_layer_weights* w, int T, size_t* bytes) {
+  MOE_REQUIRE(w && bytes, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(T >= 0 && w->E > 0 && w->k > 0 && w->d > 0 && w->F > 0, MOE_ERR_INVALID,
+              "bad shape");
+  *bytes = moe::carve_layer(nullptr, w, T).bytes;
+  return MOE_OK;
+}
+
+int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* out,
+                      const float* residual, int32_t* ids_out, float* weights_out,
+                      void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  using namespace moe;
+  MOE_REQUIRE(w, MOE_ERR_INVALID, "null weights");
+  MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
+  if (T == 0) return MOE_OK;
+  MOE_REQUIRE(x && out && workspace && w->gate_w && w->w_gate && w->w_up && w->w_down,
+              MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(x != out, MOE_ERR_INVALID, "out must not alias x");
+  MOE_REQUIRE(w->k > 0 && w->k <= w->E, MOE_ERR_INVALID, "top_k %d vs %d experts", w->k, w->E);
+  MOE_REQUIRE(!w->s_gate || (w->s_up && w->s_down && w->Fs > 0), MOE_ERR_INVALID,
+              "incomplete shared expert");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  LayerWs L = carve_layer(workspace, w, T);
+  MOE_REQUIRE(workspace_bytes >= L.bytes, MOE_ERR_WORKSPACE, "layer workspace %zu < %zu",
+              workspace_bytes, L.bytes);
+  int32_t* ids = ids_out ? ids_out : L.ids;
+  float* wts = weights_out ? weights_out : L.wts;
+  const int P = T * w->k;
+  MOE_CHECK(moe_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
+                       ids, wts, L.router_ws, L.router_bytes, stream));
+  MOE_CHECK(moe_dispatch(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status, 256, stream));
+  MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
+                        w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status));
+  if (w->s_gate) {
+    {
+      ::moe::ProfScope _prof(MOE_K_AUX, s);
+      fill_two_offsets<<<1, 32, 0, s>>>(L.s_off, T);
+    }
+    MOE_CHECK(check_launch("fill_offsets"));
+    MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
+                          nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.exp_ws, L.exp_bytes, s,
+                          L.status));
+  }
+  return launch_combine(L.y, L.inv, wts, L.s_y, residual, T, w->k, w->d, out, s);
+}
+
+}  // extern "C"

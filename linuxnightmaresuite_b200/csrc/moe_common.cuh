@@ -1,0 +1,220 @@
+// Shared device/host helpers for the MoE layer kernels (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "moe_b200.h"
+
+namespace moe {
+
+// ---------------------------------------------------------------------------
+// host-side error reporting: every C entry point returns a status and leaves a
+// message retrievable with moe_last_error().
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+int fail(int status, const char* fmt, ...);
+int check_launch(const char* what);
+
+#define MOE_REQUIRE(cond, status, ...)            \
+  do {                                            \
+    if (!(cond)) return ::moe::fail(status, __VA_ARGS__); \
+  } while (0)
+
+#define MOE_CUDA(call)                                                        \
+  do {                                                                        \
+    cudaError_t _e = (call);                                                  \
+    if (_e != cudaSuccess)                                                    \
+      return ::moe::fail(MOE_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(_e)); \
+  } while (0)
+
+#define MOE_CHECK(call)             \
+  do {                              \
+    int _s = (call);                \
+    if (_s != MOE_OK) return _s;    \
+  } while (0)
+
+int sm_count();
+
+// Per-kernel event profiling (see moe_profile_enable).
+void prof_begin(int kernel_id, cudaStream_t s);
+void prof_end(cudaStream_t s);
+
+// Brackets one kernel launch with the profiler's events.
+struct ProfScope {
+  cudaStream_t s;
+  ProfScope(int kid, cudaStream_t st) : s(st) { prof_begin(kid, st); }
+  ~ProfScope() { prof_end(s); }
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Simple bump allocator over a caller-provided workspace.
+struct Carve {
+  uint8_t* base;
+  size_t cap;
+  size_t used;
+  template <typename T>
+  T* take(size_t count) {
+    size_t off = align_up(used, 256);
+    used = off + count * sizeof(T);
+    return base ? reinterpret_cast<T*>(base + off) : nullptr;
+  }
+  bool fits() const { return used <= cap; }
+};
+
+// ---------------------------------------------------------------------------
+// packed weight tiles
+//
+// A (rows, cols) quantised matrix is stored as (rows/16) strips of 16 rows;
+// each strip is cols/64 tiles of 16 rows x 64 columns (two 32-weight blocks
+// per row).  Inside a tile, the quant bytes come first, laid out so that lane
+// L = 4g + t of a warp reads one contiguous vector with the bytes of rows g and
+// g+8 it needs for an m16n8k16 A fragment; the fp16 block scales follow,
+// 8 bytes per group g: d(g,b0) d(g,b1) d(g+8,b0) d(g+8,b1).
+//   Q4_0: lane owns bytes [4t,4t+4) of each 16-byte quant array -> 16 B/lane
+//   Q8_0: lane owns bytes [8t,8t+8) of each 32-byte quant array -> 32 B/lane
+// The tile holds exactly the bytes of its 32 GGUF blocks, so a packed matrix
+// has the same size as the raw one.
+// ---------------------------------------------------------------------------
+template <int QT> struct QTraits;
+template <> struct QTraits<MOE_Q4_0> {
+  static constexpr int kBlockBytes = 18;
+  static constexpr int kQuantBytes = 16;
+  static constexpr int kLaneBytes = 16;        // quant bytes per lane per tile
+  static constexpr int kTileQuant = 512;
+  static constexpr int kTileBytes = 576;
+};
+template <> struct QTraits<MOE_Q8_0> {
+  static constexpr int kBlockBytes = 34;
+  static constexpr int kQuantBytes = 32;
+  static constexpr int kLaneBytes = 32;
+  static constexpr int kTileQuant = 1024;
+  static constexpr int kTileBytes = 1088;
+};
+
+inline int tile_bytes(int qtype) { return qtype == MOE_Q4_0 ? 576 : 1088; }
+inline int block_bytes(int qtype) { return qtype == MOE_Q4_0 ? 18 : 34; }
+inline bool qtype_ok(int qtype) { return qtype == MOE_Q4_0 || qtype == MOE_Q8_0; }
+inline size_t matrix_bytes(int qtype, int rows, int cols) {
+  return (size_t)rows * (cols / 32) * block_bytes(qtype);
+}
+
+// Element order of the activation fragments (the B operand): for a 32-wide
+// block, the 8 halves lane t of a column reads, in register order
+// (b0.lo, b0.hi, b1.lo, b1.hi) of the first k16 step then of the second.
+// They must match the A-fragment element order the dequantiser produces.
+__host__ __device__ inline int frag_elem(int qtype, int t, int i) {
+  if (qtype == MOE_Q4_0) {
+    // first k16 step: low nibbles of bytes 4t..4t+3 -> elements 4t+{0,2,1,3}
+    // second k16 step: high nibbles -> elements 16+4t+{0,2,1,3}
+    const int perm[4] = {0, 2, 1, 3};
+    return (i < 4 ? 0 : 16) + 4 * t + perm[i & 3];
+  }
+  return 8 * t + i;  // Q8_0: int8 bytes 8t..8t+7 in order
+}
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
+  uint32_t r;
+  // (a & mask) | orv  -> LUT 0xEA
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(orv));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// D = A(16x16,row) * B(16x8,col) + C, fp16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1,
+                                          const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+        "f"(c[2]), "f"(c[3]));
+}
+
+// Q4_0 quant word (nibble bytes 4t..4t+3 of one row) -> A-fragment halves
+// for the two k16 steps of the block: values (q - 8) exactly in fp16.
+//   lo01: elements {4t, 4t+2}, lo23: {4t+1, 4t+3}
+//   hi01: {16+4t, 16+4t+2},    hi23: {16+4t+1, 16+4t+3}
+__device__ __forceinline__ void dequant_q4(uint32_t w, uint32_t& lo01, uint32_t& lo23,
+                                           uint32_t& hi01, uint32_t& hi23) {
+  const uint32_t kMagic = 0x64006400u;      // fp16 1024 in both halves
+  const uint32_t kSubLo = 0xE408E408u;      // fp16 -1032
+  const uint32_t kMulHi = 0x2C002C00u;      // fp16 1/16
+  const uint32_t kSubHi = 0xD480D480u;      // fp16 -72
+  uint32_t w8 = w >> 8;
+  lo01 = hadd2_u(lop3_and_or(w, 0x000F000Fu, kMagic), kSubLo);
+  lo23 = hadd2_u(lop3_and_or(w8, 0x000F000Fu, kMagic), kSubLo);
+  hi01 = hfma2_u(lop3_and_or(w, 0x00F000F0u, kMagic), kMulHi, kSubHi);
+  hi23 = hfma2_u(lop3_and_or(w8, 0x00F000F0u, kMagic), kMulHi, kSubHi);
+}
+
+// Q8_0 quant word (int8 bytes i..i+3) -> two fp16x2 with the exact values.
+__device__ __forceinline__ void dequant_q8(uint32_t w, uint32_t& h01, uint32_t& h23) {
+  const uint32_t kSub = 0xE480E480u;        // fp16 -1152
+  uint32_t u = w ^ 0x80808080u;             // q + 128 as unsigned bytes
+  h01 = hadd2_u(prmt(u, 0x64646464u, 0x5140u), kSub);
+  h23 = hadd2_u(prmt(u, 0x64646464u, 0x7362u), kSub);
+}
+
+__device__ __forceinline__ float silu_f(float g) {
+  // moe_forward.py:43-45: x / (1 + exp(-clip(x, -88, 88)))
+  float c = fminf(fmaxf(g, -88.0f), 88.0f);
+  return g / (1.0f + expf(-c));
+}
+
+// numpy's float32 add.reduce order over n contiguous values (its pairwise
+// summation): sequential below 8 terms, eight running sums up to 128 terms,
+// and above that a split at n/2 rounded down to a multiple of 8.
+static __device__ float np_pairwise_sum(const float* a, int n) {
+  if (n < 8) {
+    float res = 0.f;
+    for (int i = 0; i < n; ++i) res = res + a[i];
+    return res;
+  }
+  if (n <= 128) {
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = a[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = r[j] + a[i + j];
+    }
+    float res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+    for (; i < n; ++i) res = res + a[i];
+    return res;
+  }
+  int n2 = n / 2;
+  n2 -= n2 % 8;
+  return np_pairwise_sum(a, n2) + np_pairwise_sum(a + n2, n - n2);
+}
+
+__device__ __forceinline__ void set_status(int* status, int bit) {
+  if (status) atomicOr(status, bit);
+}
+
+}  // namespace moe

@@ -1,0 +1,299 @@
+// Router: logits = x @ G (+ bias), top-k selection and softmax weights.
+//
+// moe_forward.py:91-109 (MoERouter.route: top-k of the logits, descending, then
+// softmax over the k selected logits) and nightmare_stream.py:3227-3238
+// (softmax over all experts, top-k of the probabilities, ascending, renormalised).
+//
+// Pass 1 (router_partial_kernel): a grid of (token tile, d-slice) CTAs; each
+// stages its slice of the router matrix in shared memory and accumulates
+// partial logits for its tokens in registers.  Pass 2 (router_select_kernel):
+// one warp per token sums the d-slice partials in a fixed order, then selects
+// and weighs the experts.  Sums use numpy's float32 order (sequential below 8
+// terms, 8-way pairwise at and above) so the denominators follow the reference.
+#include <math.h>
+
+#include "moe_common.cuh"
+
+namespace moe {
+
+constexpr int kRouterThreads = 256;
+constexpr int kRouterDC = 64;        // rows of G per staged chunk
+constexpr int kRouterTPT = 4;        // tokens per thread
+constexpr int kMaxE = 512;
+constexpr int kMaxK = 32;
+
+struct RouterPlan {
+  int ct;        // column threads (E / 4)
+  int tg;        // token groups per CTA
+  int tt;        // tokens per CTA
+  int tiles;     // token tiles
+  int nds;       // d-slices
+  int chunks;    // d-chunks per slice
+};
+
+static RouterPlan router_plan(int T, int d, int E) {
+  RouterPlan p;
+  p.ct = E / 4;
+  p.tg = kRouterThreads / p.ct;
+  if (p.tg > 8) p.tg = 8;
+  p.tt = p.tg * kRouterTPT;
+  p.tiles = (T + p.tt - 1) / p.tt;
+  int total_chunks = (d + kRouterDC - 1) / kRouterDC;
+  int want = (2 * sm_count() + p.tiles - 1) / p.tiles;
+  p.nds = want < 1 ? 1 : (want > total_chunks ? total_chunks : want);
+  p.chunks = (total_chunks + p.nds - 1) / p.nds;
+  p.nds = (total_chunks + p.chunks - 1) / p.chunks;
+  return p;
+}
+
+__global__ void __launch_bounds__(kRouterThreads)
+router_partial_kernel(const float* __restrict__ x, const float* __restrict__ G, int T, int d,
+                      int E, int layout, int tt, int chunks, float* __restrict__ part) {
+  extern __shared__ float smem[];
+  float* gs = smem;                                  // [kRouterDC][E]
+  float* xs = smem + kRouterDC * E;                  // [tt][kRouterDC + 1]
+  const int ct = E / 4;
+  const int tid = threadIdx.x;
+  const int col = tid % ct;                          // experts 4*col .. 4*col+3
+  const int tgrp = tid / ct;
+  const int tg = blockDim.x / ct;
+  const int t0 = blockIdx.x * tt;
+  const int slice = blockIdx.y;
+  float acc[kRouterTPT][4];
+#pragma unroll
+  for (int a = 0; a < kRouterTPT; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+
+  for (int c = 0; c < chunks; ++c) {
+    const int i0 = (slice * chunks + c) * kRouterDC;
+    if (i0 >= d) break;
+    const int rows = min(kRouterDC, d - i0);
+    __syncthreads();
+    // stage G[i0 : i0+rows, :] as [row][E]
+    if (layout == MOE_ROUTER_D_E) {
+      const float4* src = reinterpret_cast<const float4*>(G + (size_t)i0 * E);
+      float4* dst = reinterpret_cast<float4*>(gs);
+      for (int v = tid; v < rows * E / 4; v += blockDim.x) dst[v] = __ldg(src + v);
+    } else {
+      for (int v = tid; v < rows * E; v += blockDim.x) {
+        int e = v / rows, i = v % rows;
+        gs[i * E + e] = __ldg(G + (size_t)e * d + i0 + i);
+      }
+    }
+    // stage x[t0 : t0+tt, i0 : i0+rows]
+    for (int v = tid; v < tt * kRouterDC; v += blockDim.x) {
+      int tl = v / kRouterDC, i = v % kRouterDC;
+      int t = t0 + tl;
+      xs[tl * (kRouterDC + 1) + i] = (t < T && i < rows) ? __ldg(x + (size_t)t * d + i0 + i) : 0.f;
+    }
+    __syncthreads();
+    for (int i = 0; i < rows; ++i) {
+      float4 g4 = *reinterpret_cast<const float4*>(gs + i * E + 4 * col);
+#pragma unroll
+      for (int a = 0; a < kRouterTPT; ++a) {
+        float xv = xs[(tgrp + a * tg) * (kRouterDC + 1) + i];
+        acc[a][0] = fmaf(xv, g4.x, acc[a][0]);
+        acc[a][1] = fmaf(xv, g4.y, acc[a][1]);
+        acc[a][2] = fmaf(xv, g4.z, acc[a][2]);
+        acc[a][3] = fmaf(xv, g4.w, acc[a][3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < kRouterTPT; ++a) {
+    int t = t0 + tgrp + a * tg;
+    if (t < T) {
+      float4 v = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+      *reinterpret_cast<float4*>(part + ((size_t)slice * T + t) * E + 4 * col) = v;
+    }
+  }
+}
+
+// a beats b: larger value, NaN above numbers, equal values -> higher index.
+__device__ __forceinline__ bool beats(float a, int ia, float b, int ib) {
+  bool na = isnan(a), nb = isnan(b);
+  if (na != nb) return na;
+  if (na) return ia > ib;
+  return a > b || (a == b && ia > ib);
+}
+
+// One warp per token.  Lanes hold logits e = lane + 32 j.
+__global__ void __launch_bounds__(128)
+router_select_kernel(const float* __restrict__ part, int nds, const float* __restrict__ bias,
+                     int T, int E, int k, int mode, int32_t* __restrict__ ids,
+                     float* __restrict__ weights) {
+  __shared__ float sbuf[4][kMaxE];
+  __shared__ float ssel[4][kMaxK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + warp;
+  if (t >= T) return;
+  const int J = (E + 31) / 32;
+  float v[kMaxE / 32];
+#pragma unroll
+  for (int j = 0; j < kMaxE / 32; ++j) {
+    int e = lane + 32 * j;
+    float acc = 0.f;
+    if (j < J && e < E) {
+      for (int s = 0; s < nds; ++s) acc += part[((size_t)s * T + t) * E + e];
+      if (bias) acc += bias[e];
+    }
+    v[j] = acc;
+  }
+  float* buf = sbuf[warp];
+  if (mode == MOE_ROUTE_SOFTMAX_TOPK_RENORM) {
+    // probs = exp(l - max) / sum(exp(l - max)) over all experts
+    float m = -INFINITY;
+    bool any_nan = false;
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+      int e = lane + 32 * j;
+      if (j < J && e < E) {
+        any_nan |= isnan(v[j]);
+        m = fmaxf(m, v[j]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    any_nan = __any_sync(0xffffffffu, any_nan);
+    if (any_nan) m = NAN;
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+      int e = lane + 32 * j;
+      if (j < J && e < E) {
+        v[j] = expf(v[j] - m);
+        buf[e] = v[j];
+      }
+    }
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0) s = np_pairwise_sum(buf, E);
+    s = __shfl_sync(0xffffffffu, s, 0);
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) v[j] = v[j] / s;
+  }
+  // k rounds of warp arg-max
+  unsigned taken = 0u;  // bit j: lane's element j already selected
+  int sel_id = -1;
+  float sel_val = 0.f;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = -1;
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+      int e = lane + 32 * j;
+      if (j < J && e < E && !((taken >> j) & 1u)) {
+        if (bi < 0 || beats(v[j], e, bv, bi)) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi >= 0 && (bi < 0 || beats(ov, oi, bv, bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == 0) ssel[warp][r] = bv;
+    if (lane == r) {
+      sel_id = bi;
+      sel_val = bv;
+    }
+  }
+  __syncwarp();
+  // weights, in the reference's output order
+  float* sv = ssel[warp];
+  if (mode == MOE_ROUTE_TOPK_SOFTMAX) {
+    // descending order; softmax over the k selected logits
+    float mx = sv[0];
+    for (int r = 1; r < k; ++r) mx = fmaxf(mx, sv[r]);  // np.max
+    __syncwarp();
+    if (lane < k) buf[lane] = expf(sel_val - mx);
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0) s = np_pairwise_sum(buf, k);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (lane < k) {
+      ids[(size_t)t * k + lane] = sel_id;
+      weights[(size_t)t * k + lane] = buf[lane] / s;
+    }
+  } else {
+    // ascending order (argsort(probs)[-k:]); renormalise by their sum
+    int pos = k - 1 - lane;  // lane r holds the r-th largest -> output position k-1-r
+    __syncwarp();
+    if (lane < k) buf[pos] = sel_val;
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0) s = np_pairwise_sum(buf, k);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (lane < k) {
+      ids[(size_t)t * k + pos] = sel_id;
+      weights[(size_t)t * k + pos] = sel_val / s;
+    }
+  }
+}
+
+static size_t router_ws(int T, int d, int E) {
+  RouterPlan p = router_plan(T, d, E);
+  return align_up(256, 256) + align_up((size_t)p.nds * T * E * sizeof(float), 256);
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_router_workspace_bytes(int T, int d, int E, size_t* bytes) {
+  MOE_REQUIRE(bytes, MOE_ERR_INVALID, "null output pointer");
+  MOE_REQUIRE(T >= 0 && d > 0 && E > 0, MOE_ERR_INVALID, "bad shape");
+  *bytes = moe::router_ws(T, d, E);
+  return MOE_OK;
+}
+
+int moe_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
+               int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
+               size_t workspace_bytes, moe_stream_t stream) {
+  using namespace moe;
+  MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
+  if (T == 0) return MOE_OK;
+  MOE_REQUIRE(x && gate_w && ids && weights && workspace, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(d > 0 && E > 0 && k > 0, MOE_ERR_INVALID, "d, E and k must be positive");
+  MOE_REQUIRE(k <= E, MOE_ERR_INVALID, "top_k %d exceeds the expert count %d", k, E);
+  MOE_REQUIRE(k <= kMaxK, MOE_ERR_UNSUPPORTED, "top_k %d above %d", k, kMaxK);
+  MOE_REQUIRE(E % 4 == 0 && E <= kMaxE, MOE_ERR_UNSUPPORTED,
+              "expert count %d must be a multiple of 4 and <= %d", E, kMaxE);
+  MOE_REQUIRE(layout == MOE_ROUTER_D_E || layout == MOE_ROUTER_E_D, MOE_ERR_INVALID,
+              "bad router layout %d", layout);
+  MOE_REQUIRE(mode == MOE_ROUTE_TOPK_SOFTMAX || mode == MOE_ROUTE_SOFTMAX_TOPK_RENORM,
+              MOE_ERR_INVALID, "bad routing mode %d", mode);
+  MOE_REQUIRE(workspace_bytes >= router_ws(T, d, E), MOE_ERR_WORKSPACE,
+              "router workspace %zu < %zu", workspace_bytes, router_ws(T, d, E));
+  MOE_REQUIRE(((uintptr_t)gate_w & 15) == 0, MOE_ERR_INVALID, "router weight not 16B aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  RouterPlan p = router_plan(T, d, E);
+  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  size_t smem = ((size_t)kRouterDC * E + (size_t)p.tt * (kRouterDC + 1)) * sizeof(float);
+  if (smem > 48 * 1024) {
+    MOE_CUDA(cudaFuncSetAttribute(router_partial_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  dim3 grid(p.tiles, p.nds);
+  {
+    ::moe::ProfScope _prof(MOE_K_ROUTER_PARTIAL, s);
+    router_partial_kernel<<<grid, p.ct * p.tg, smem, s>>>(x, gate_w, T, d, E, layout, p.tt,
+                                                             p.chunks, part);
+  }
+  MOE_CHECK(check_launch("router_partial"));
+  {
+    ::moe::ProfScope _prof(MOE_K_ROUTER_SELECT, s);
+    router_select_kernel<<<(T + 3) / 4, 128, 0, s>>>(part, p.nds, bias, T, E, k, mode, ids,
+                                                     weights);
+  }
+  return check_launch("router_select");
+}
+
+}  // extern "C"

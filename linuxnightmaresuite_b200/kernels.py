@@ -1,0 +1,214 @@
+"""Torch-tensor wrappers over the C ABI.
+
+Every function takes CUDA tensors, allocates outputs and workspaces with torch
+and enqueues the library's kernels on the current CUDA stream.  Inputs that
+are not contiguous CUDA tensors of the right dtype are rejected.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+QTYPE_Q4_0 = _lib.MOE_Q4_0
+QTYPE_Q8_0 = _lib.MOE_Q8_0
+BLOCK_BYTES = {QTYPE_Q4_0: 18, QTYPE_Q8_0: 34}
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _need(t: torch.Tensor, dtype, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _size_out(fn: str, *args) -> int:
+    out = ctypes.c_size_t(0)
+    call(fn, *args, ctypes.byref(out))
+    return int(out.value)
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def block_geometry(qtype: int) -> Tuple[int, int]:
+    e, b = ctypes.c_int(0), ctypes.c_int(0)
+    call("moe_block_geometry", qtype, ctypes.byref(e), ctypes.byref(b))
+    return e.value, b.value
+
+
+# --------------------------------------------------------------------------- weights
+
+def dequantize(raw: torch.Tensor, qtype: int, n_elements: int) -> torch.Tensor:
+    _need(raw, torch.uint8, "raw")
+    out = torch.empty(n_elements, dtype=torch.float32, device=raw.device)
+    call("moe_dequantize", _ptr(raw), _ptr(out), qtype, n_elements, _stream())
+    return out
+
+
+def pack_weights(raw: torch.Tensor, qtype: int, n_mats: int, rows: int, cols: int) -> torch.Tensor:
+    _need(raw, torch.uint8, "raw")
+    nbytes = _size_out("moe_packed_bytes", qtype, n_mats, rows, cols)
+    if raw.numel() != nbytes:
+        raise ValueError(f"raw blocks hold {raw.numel()} bytes, expected {nbytes}")
+    out = torch.empty(nbytes, dtype=torch.uint8, device=raw.device)
+    call("moe_pack_weights", _ptr(raw), _ptr(out), qtype, n_mats, rows, cols, _stream())
+    return out
+
+
+def unpack_weights(packed: torch.Tensor, qtype: int, n_mats: int, rows: int, cols: int) -> torch.Tensor:
+    _need(packed, torch.uint8, "packed")
+    out = torch.empty_like(packed)
+    call("moe_unpack_weights", _ptr(packed), _ptr(out), qtype, n_mats, rows, cols, _stream())
+    return out
+
+
+# --------------------------------------------------------------------------- stages
+
+def router(x: torch.Tensor, gate_w: torch.Tensor, k: int, mode: int = 0,
+           bias: Optional[torch.Tensor] = None, layout: int = _lib.MOE_ROUTER_D_E):
+    """(ids int32 (T,k), weights f32 (T,k)) for x (T, d)."""
+    _need(x, torch.float32, "x")
+    _need(gate_w, torch.float32, "gate_w")
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+    T, d = x.shape
+    E = gate_w.shape[1] if layout == _lib.MOE_ROUTER_D_E else gate_w.shape[0]
+    ids = torch.empty((T, k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    ws = workspace(_size_out("moe_router_workspace_bytes", T, d, E), x.device)
+    call("moe_router", _ptr(x), _ptr(gate_w), _ptr(bias), T, d, E, k, layout, mode,
+         _ptr(ids), _ptr(w), _ptr(ws), ws.numel(), _stream())
+    return ids, w
+
+
+def dispatch(ids: torch.Tensor, n_experts: int, ws: Optional[torch.Tensor] = None):
+    """(expert_offsets (E+1), perm_rows (T*k), inv_perm (T*k)), all int32."""
+    _need(ids, torch.int32, "ids")
+    T, k = ids.shape
+    dev = ids.device
+    off = torch.empty(n_experts + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(T * k, dtype=torch.int32, device=dev)
+    inv = torch.empty(T * k, dtype=torch.int32, device=dev)
+    if ws is None:
+        ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+    call("moe_dispatch", _ptr(ids), T, k, n_experts, _ptr(off), _ptr(perm), _ptr(inv),
+         _ptr(ws), ws.numel(), _stream())
+    return off, perm, inv
+
+
+def read_status(ws: torch.Tensor) -> int:
+    st = ctypes.c_int(0)
+    rc = _lib.load().moe_read_status(_ptr(ws), ctypes.byref(st), _stream())
+    if rc not in (_lib.MOE_OK, _lib.MOE_ERR_DEVICE):
+        _lib.check(rc)
+    return st.value
+
+
+def experts(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, qtype: int,
+            offsets: torch.Tensor, x: torch.Tensor, d: int, F: int,
+            x_rows: Optional[torch.Tensor] = None, x_rows_div: int = 1,
+            y: Optional[torch.Tensor] = None, y_rows: Optional[torch.Tensor] = None,
+            rows: Optional[int] = None, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped SwiGLU experts on packed weights; returns y (rows, d) f32."""
+    for t, n in ((w_gate, "w_gate"), (w_up, "w_up"), (w_down, "w_down")):
+        _need(t, torch.uint8, n)
+    _need(offsets, torch.int32, "offsets")
+    _need(x, torch.float32, "x")
+    E = offsets.numel() - 1
+    if rows is None:
+        rows = int(offsets[-1].item())
+    if y is None:
+        y = torch.empty((rows, d), dtype=torch.float32, device=x.device)
+    if ws is None:
+        ws = workspace(_size_out("moe_experts_workspace_bytes", rows, E, d, F), x.device)
+        ws[:256].zero_()
+    call("moe_experts", _ptr(w_gate), _ptr(w_up), _ptr(w_down), qtype, _ptr(offsets), E, rows,
+         _ptr(x), _ptr(x_rows), x_rows_div, d, F, _ptr(y), _ptr(y_rows), _ptr(ws), ws.numel(),
+         _stream())
+    return y
+
+
+def combine(y: torch.Tensor, inv_perm: torch.Tensor, weights: torch.Tensor,
+            shared: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    T, k = weights.shape
+    d = y.shape[1]
+    if out is None:
+        out = torch.empty((T, d), dtype=torch.float32, device=y.device)
+    call("moe_combine", _ptr(y), _ptr(inv_perm), _ptr(weights), _ptr(shared), _ptr(residual),
+         T, k, d, _ptr(out), _stream())
+    return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need(x, torch.float32, "x")
+    _need(weight, torch.float32, "weight")
+    T, d = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    call("moe_rms_norm", _ptr(x), _ptr(weight), ctypes.c_float(eps), T, d, _ptr(out), _stream())
+    return out
+
+
+# --------------------------------------------------------------------------- layer
+
+class LayerWeights:
+    """Device-resident weights of one MoE layer in the library's layout."""
+
+    def __init__(self, gate_w: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                 w_down: torch.Tensor, qtype: int, E: int, k: int, d: int, F: int,
+                 mode: int = 0, bias: Optional[torch.Tensor] = None,
+                 router_layout: int = _lib.MOE_ROUTER_D_E,
+                 shared: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+                 shared_qtype: int = QTYPE_Q8_0, Fs: int = 0):
+        self.gate_w, self.bias = gate_w, bias
+        self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
+        self.shared = shared
+        self.qtype, self.E, self.k, self.d, self.F, self.mode = qtype, E, k, d, F, mode
+        self.shared_qtype, self.Fs = shared_qtype, Fs
+        s = shared or (None, None, None)
+        self.c = _lib.MoELayerWeights(
+            gate_w.data_ptr(), 0 if bias is None else bias.data_ptr(),
+            w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(),
+            0 if s[0] is None else s[0].data_ptr(), 0 if s[1] is None else s[1].data_ptr(),
+            0 if s[2] is None else s[2].data_ptr(),
+            router_layout, qtype, shared_qtype, E, k, d, F, Fs, mode)
+
+    def workspace_bytes(self, T: int) -> int:
+        out = ctypes.c_size_t(0)
+        call("moe_layer_workspace_bytes", ctypes.byref(self.c), T, ctypes.byref(out))
+        return int(out.value)
+
+
+def layer_forward(lw: LayerWeights, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                  residual: Optional[torch.Tensor] = None, ws: Optional[torch.Tensor] = None,
+                  ids: Optional[torch.Tensor] = None,
+                  weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need(x, torch.float32, "x")
+    T = x.shape[0]
+    if out is None:
+        out = torch.empty_like(x)
+    if ws is None:
+        ws = workspace(lw.workspace_bytes(T), x.device)
+        ws[:256].zero_()
+    call("moe_layer_forward", ctypes.byref(lw.c), _ptr(x), T, _ptr(out), _ptr(residual),
+         _ptr(ids), _ptr(weights), _ptr(ws), ws.numel(), _stream())
+    return out

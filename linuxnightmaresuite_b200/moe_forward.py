@@ -1,0 +1,229 @@
+"""Drop-in B200 counterpart of the reference's ``moe_forward.py`` MoE classes.
+
+Same names, constructor arguments and call results as the reference:
+
+* ``MoERouter(gate_weight, n_experts, top_k=2)`` with ``route(x) ->
+  (List[int], np.ndarray)`` for one token (moe_forward.py:78-109);
+* ``ExpertFFN`` with ``forward(x)`` (moe_forward.py:116-133);
+* ``MoELayer(router, experts, shared_expert=None)`` with ``forward(x)``
+  (moe_forward.py:140-174);
+* ``rms_norm(x, weight, eps=1e-6)`` (moe_forward.py:34-40).
+
+Everything runs in the CUDA library (``libmoe_b200.so``); there is no CPU path.
+Inputs may be numpy float32 arrays (results come back as numpy, like the
+reference) or CUDA tensors (results stay on the device).  A 2-D input of T
+tokens is processed as one batch whose row t equals the single-token result.
+
+Experts are built from GGUF Q4_0 / Q8_0 block bytes (``ExpertFFN.from_blocks``
+/ ``MoELayer.from_blocks``) -- exactly what ``gguf_parser.load_tensor_raw``
+(gguf_parser.py:532-558) or a per-expert slice of an ``ffn_*_exps`` tensor
+(nightmare_stream.py:3361-3441) yields.  ``ExpertFFN(w_gate, w_up, w_down)``
+also accepts such block arrays directly when given ``qtype``.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple, Union
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import kernels as K
+
+Array = Union[np.ndarray, torch.Tensor]
+
+QTYPE_Q4_0 = K.QTYPE_Q4_0
+QTYPE_Q8_0 = K.QTYPE_Q8_0
+
+
+def _device(device=None) -> torch.device:
+    if device is not None:
+        return torch.device(device)
+    if not torch.cuda.is_available():
+        raise RuntimeError("the B200 MoE layer needs a CUDA device")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _to_dev_f32(a: Array, device) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        return a.to(device=device, dtype=torch.float32).contiguous()
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(device)
+
+
+def _to_dev_u8(a: Array, device) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        return a.to(device=device).contiguous().view(torch.uint8).reshape(-1)
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.uint8).reshape(-1)).to(device)
+
+
+def rms_norm(x: Array, weight: Array, eps: float = 1e-6):
+    """moe_forward.rms_norm (moe_forward.py:34-40); rows normalised independently."""
+    dev = _device(x.device if isinstance(x, torch.Tensor) and x.is_cuda else None)
+    xt = _to_dev_f32(x, dev)
+    one = xt.dim() == 1
+    out = K.rms_norm(xt.reshape(1, -1) if one else xt, _to_dev_f32(weight, dev), eps)
+    out = out.reshape(-1) if one else out
+    return out if isinstance(x, torch.Tensor) else out.cpu().numpy()
+
+
+class MoERouter:
+    """Top-k expert routing (moe_forward.py:78-109).
+
+    ``mode=0`` is the reference's MoERouter (top-k logits, softmax over them,
+    descending); ``mode=1`` is the production rule of nightmare_stream.py:3227-3238
+    (softmax over all experts, top-k, renormalised, ascending).  ``bias`` is an
+    optional per-expert logit offset."""
+
+    def __init__(self, gate_weight: Array, n_experts: int, top_k: int = 2, mode: int = 0,
+                 bias: Optional[Array] = None, device=None):
+        if top_k > n_experts:
+            raise ValueError(f"top_k {top_k} exceeds n_experts {n_experts}")
+        self.gate_weight = gate_weight
+        self.n_experts = n_experts
+        self.top_k = top_k
+        self.mode = mode
+        self.device = _device(device)
+        self.g = _to_dev_f32(gate_weight, self.device)
+        if self.g.shape[1] != n_experts:
+            raise ValueError(f"gate_weight is {tuple(self.g.shape)}, expected (dim, {n_experts})")
+        self.bias = None if bias is None else _to_dev_f32(bias, self.device)
+
+    def route_batch(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(ids int32 (T,k), weights f32 (T,k)) on the device."""
+        return K.router(x, self.g, self.top_k, self.mode, self.bias)
+
+    def route(self, x: Array):
+        xt = _to_dev_f32(x, self.device)
+        if xt.dim() == 1:
+            ids, w = self.route_batch(xt.reshape(1, -1))
+            return ids[0].cpu().tolist(), w[0].cpu().numpy()
+        ids, w = self.route_batch(xt)
+        if isinstance(x, torch.Tensor):
+            return ids, w
+        return ids.cpu().numpy(), w.cpu().numpy()
+
+
+class ExpertFFN:
+    """One SwiGLU expert (moe_forward.py:116-133) on quantised GGUF blocks.
+
+    ``w_gate`` / ``w_up``: blocks of a (hidden_dim, dim) matrix; ``w_down``:
+    blocks of (dim, hidden_dim); ``qtype`` is the GGML type (2 = Q4_0,
+    8 = Q8_0).  The blocks are packed once into the device layout."""
+
+    def __init__(self, w_gate: Array, w_up: Array, w_down: Array, qtype: Optional[int] = None,
+                 dim: Optional[int] = None, hidden_dim: Optional[int] = None, device=None):
+        if qtype is None:
+            raise TypeError(
+                "ExpertFFN on the B200 path takes GGUF Q4_0 / Q8_0 block bytes; pass qtype "
+                "(2 or 8) and dim / hidden_dim, or use ExpertFFN.from_blocks")
+        if qtype not in (QTYPE_Q4_0, QTYPE_Q8_0):
+            raise ValueError(f"unsupported GGML type {qtype}")
+        self.device = _device(device)
+        self.qtype, self.dim, self.hidden_dim = qtype, int(dim), int(hidden_dim)
+        d, F = self.dim, self.hidden_dim
+        self.w_gate = K.pack_weights(_to_dev_u8(w_gate, self.device), qtype, 1, F, d)
+        self.w_up = K.pack_weights(_to_dev_u8(w_up, self.device), qtype, 1, F, d)
+        self.w_down = K.pack_weights(_to_dev_u8(w_down, self.device), qtype, 1, d, F)
+
+    @classmethod
+    def from_blocks(cls, gate_bytes: Array, up_bytes: Array, down_bytes: Array, qtype: int,
+                    dim: int, hidden_dim: int, device=None) -> "ExpertFFN":
+        return cls(gate_bytes, up_bytes, down_bytes, qtype, dim, hidden_dim, device)
+
+    def forward(self, x: Array):
+        xt = _to_dev_f32(x, self.device)
+        one = xt.dim() == 1
+        xt = xt.reshape(1, -1) if one else xt
+        T = xt.shape[0]
+        off = torch.tensor([0, T], dtype=torch.int32, device=self.device)
+        y = K.experts(self.w_gate, self.w_up, self.w_down, self.qtype, off, xt, self.dim,
+                      self.hidden_dim, rows=T)
+        y = y.reshape(-1) if one else y
+        return y if isinstance(x, torch.Tensor) else y.cpu().numpy()
+
+
+class MoELayer:
+    """Router + routed experts + optional shared expert (moe_forward.py:140-174)."""
+
+    def __init__(self, router: MoERouter, experts: Sequence[ExpertFFN],
+                 shared_expert: Optional[ExpertFFN] = None):
+        self.router = router
+        self.experts = list(experts)
+        self.shared_expert = shared_expert
+        if len(self.experts) != router.n_experts:
+            raise ValueError(f"{len(self.experts)} experts for a router over {router.n_experts}")
+        e0 = self.experts[0]
+        for ex in self.experts:
+            if (ex.qtype, ex.dim, ex.hidden_dim) != (e0.qtype, e0.dim, e0.hidden_dim):
+                raise ValueError("all routed experts must share quant type and shape")
+        dev = router.device
+        self._build(router, torch.cat([ex.w_gate for ex in self.experts]).to(dev),
+                    torch.cat([ex.w_up for ex in self.experts]).to(dev),
+                    torch.cat([ex.w_down for ex in self.experts]).to(dev),
+                    e0.qtype, e0.dim, e0.hidden_dim, shared_expert)
+
+    def _build(self, router, wg, wu, wd, qtype, d, F, shared):
+        self.dim, self.hidden_dim, self.qtype = d, F, qtype
+        sh = None
+        sq, Fs = QTYPE_Q8_0, 0
+        if shared is not None:
+            if shared.dim != d:
+                raise ValueError("shared expert dim differs from the routed experts")
+            sh = (shared.w_gate, shared.w_up, shared.w_down)
+            sq, Fs = shared.qtype, shared.hidden_dim
+        self.weights = K.LayerWeights(router.g, wg, wu, wd, qtype, router.n_experts,
+                                      router.top_k, d, F, router.mode, router.bias,
+                                      _lib.MOE_ROUTER_D_E, sh, sq, Fs)
+        self._ws = None
+
+    @classmethod
+    def from_blocks(cls, gate_weight: Array, w_gate: Array, w_up: Array, w_down: Array,
+                    qtype: int, top_k: int, shared: Optional[Tuple[Array, Array, Array]] = None,
+                    shared_qtype: int = QTYPE_Q8_0, shared_hidden: int = 0, mode: int = 0,
+                    bias: Optional[Array] = None, device=None) -> "MoELayer":
+        """Layer from stacked expert blocks: ``w_gate`` / ``w_up`` (E, F, F_row_bytes),
+        ``w_down`` (E, d, ...), i.e. the bytes of GGUF ``ffn_*_exps`` tensors."""
+        dev = _device(device)
+        G = gate_weight
+        d, E = int(G.shape[0]), int(G.shape[1])
+        F = int(w_gate.shape[1])
+        router = MoERouter(G, E, top_k, mode, bias, dev)
+        self = cls.__new__(cls)
+        self.router, self.experts = router, None
+        sh_ex = None
+        if shared is not None:
+            sh_ex = ExpertFFN(shared[0], shared[1], shared[2], shared_qtype, d, shared_hidden, dev)
+        self.shared_expert = sh_ex
+        wg = K.pack_weights(_to_dev_u8(w_gate, dev), qtype, E, F, d)
+        wu = K.pack_weights(_to_dev_u8(w_up, dev), qtype, E, F, d)
+        wd = K.pack_weights(_to_dev_u8(w_down, dev), qtype, E, d, F)
+        self._build(router, wg, wu, wd, qtype, d, F, sh_ex)
+        return self
+
+    def _workspace(self, T: int) -> torch.Tensor:
+        need = self.weights.workspace_bytes(T)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.router.device)
+        return self._ws
+
+    def forward_batch(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                      out: Optional[torch.Tensor] = None, return_routing: bool = False):
+        T = x.shape[0]
+        ids = weights = None
+        if return_routing:
+            ids = torch.empty((T, self.router.top_k), dtype=torch.int32, device=x.device)
+            weights = torch.empty((T, self.router.top_k), dtype=torch.float32, device=x.device)
+        out = K.layer_forward(self.weights, x, out=out, residual=residual,
+                              ws=self._workspace(T), ids=ids, weights=weights)
+        return (out, ids, weights) if return_routing else out
+
+    def device_status(self) -> int:
+        """Reads and clears the device status bits (synchronises)."""
+        return 0 if self._ws is None else K.read_status(self._ws)
+
+    def forward(self, x: Array):
+        xt = _to_dev_f32(x, self.router.device)
+        one = xt.dim() == 1
+        out = self.forward_batch(xt.reshape(1, -1) if one else xt)
+        out = out.reshape(-1) if one else out
+        return out if isinstance(x, torch.Tensor) else out.cpu().numpy()

@@ -1,0 +1,50 @@
+"""Stacked decode step: L MoE layers, each with an always-on shared expert,
+with the residual and RMSNorm of MoETransformerModel._layer_forward
+(moe_forward.py:348-359): ``x = x + moe(rms_norm(x, w))``."""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import kernels as K
+from .moe_forward import MoELayer
+
+
+class StackedMoE:
+    def __init__(self, layers: Sequence[MoELayer], norms: Sequence[torch.Tensor], eps: float = 1e-6):
+        self.layers = list(layers)
+        self.norms = list(norms)
+        self.eps = eps
+        self._buf: Optional[torch.Tensor] = None
+
+    @classmethod
+    def from_layers(cls, datas, device=None, eps: float = 1e-6) -> "StackedMoE":
+        """From synthetic layer data (``synth.MoELayerData`` per layer)."""
+        layers, norms = [], []
+        for data in datas:
+            cfg = data.cfg
+            shared = None
+            if cfg.shared_ffn:
+                shared = (data.s_gate[0], data.s_up[0], data.s_down[0])
+            layer = MoELayer.from_blocks(data.gate_w, data.w_gate, data.w_up, data.w_down,
+                                         cfg.qtype, cfg.top_k, shared=shared,
+                                         shared_qtype=cfg.shared_qtype,
+                                         shared_hidden=cfg.shared_ffn, bias=data.bias,
+                                         device=device)
+            layers.append(layer)
+            norms.append(torch.from_numpy(data.norm_w).to(layer.router.device))
+        return cls(layers, norms, eps)
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x (T, d) f32 on the device -> (T, d)."""
+        cur = x
+        if self._buf is None or self._buf.shape != x.shape:
+            self._buf = torch.empty_like(x)
+        xn = self._buf
+        for i, (layer, nw) in enumerate(zip(self.layers, self.norms)):
+            K.rms_norm(cur, nw, self.eps, out=xn)
+            dst = out if (out is not None and i == len(self.layers) - 1) else torch.empty_like(x)
+            layer.forward_batch(xn, residual=cur, out=dst)
+            cur = dst
+        return cur

@@ -1,0 +1,281 @@
+"""CPU oracle for the MoE layer forward -- TEST INFRASTRUCTURE ONLY.
+
+This module is the checker the CUDA path is compared against.  Only the test
+suite, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may
+import it; the product path (``linuxnightmaresuite_b200``) never does.
+
+It restates, in numpy, the reference algorithm of
+NightmareDesigns/Linuxnightmaresuite for this path:
+
+* block decoders ``dequant_fast.py:44-66`` (Q8_0) and ``:69-100`` (Q4_0);
+* ``rms_norm`` / ``silu`` / ``softmax`` ``moe_forward.py:34-52``;
+* router ``MoERouter.route`` ``moe_forward.py:91-109`` (top-k, then softmax
+  over the k logits, descending order) and the production variant
+  ``nightmare_stream.py:3227-3238`` (softmax over all experts, top-k,
+  renormalise; ascending order);
+* ``ExpertFFN.forward`` ``moe_forward.py:129-133``;
+* ``MoELayer.forward`` ``moe_forward.py:154-174`` (weighted sum in router
+  order, unweighted shared expert).
+
+Per-token functions use the same numpy calls in the same order as the
+reference, so on the same host they reproduce it bit for bit; this is pinned
+by ``tests/test_oracle_golden.py`` against fixtures made by running the
+reference itself (``tests/golden/make_golden.py``).
+
+Tie rule.  The reference sorts with ``np.argsort`` (default quicksort, which
+numpy may run as an unstable SIMD sort).  The oracle implements the stable
+rule -- descending value, ties broken by the higher expert index first, i.e.
+``argsort(kind='stable')[-k:][::-1]`` -- and reports tokens where numpy's
+default sort would pick differently so tests can treat them separately.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import numpy as np
+
+QTYPE_Q4_0 = 2
+QTYPE_Q8_0 = 8
+# dequant_fast.py:723-754, rows for Q4_0 and Q8_0
+BLOCK_SIZES = {QTYPE_Q4_0: (32, 18), QTYPE_Q8_0: (32, 34)}
+
+
+# --------------------------------------------------------------------------
+# block decoders
+# --------------------------------------------------------------------------
+
+def dequantize_q8_0(data, n_elements: int) -> np.ndarray:
+    """dequant_fast.py:44-66: f32 = fp16 scale * int8 quant, 34-byte blocks."""
+    n_blocks = n_elements // 32
+    raw = np.frombuffer(bytes(data) if not isinstance(data, np.ndarray) else data.tobytes(),
+                        dtype=np.uint8).reshape(n_blocks, 34)
+    scales = raw[:, :2].copy().view(np.float16).astype(np.float32).reshape(n_blocks, 1)
+    quants = raw[:, 2:].copy().view(np.int8).astype(np.float32)
+    return (scales * quants).reshape(-1)
+
+
+def dequantize_q4_0(data, n_elements: int) -> np.ndarray:
+    """dequant_fast.py:69-100: low nibbles -> weights 0-15, high nibbles ->
+    16-31, value (nibble - 8) * fp16 scale, 18-byte blocks."""
+    n_blocks = n_elements // 32
+    raw = np.frombuffer(bytes(data) if not isinstance(data, np.ndarray) else data.tobytes(),
+                        dtype=np.uint8).reshape(n_blocks, 18)
+    scales = raw[:, :2].copy().view(np.float16).astype(np.float32).reshape(n_blocks, 1)
+    packed = raw[:, 2:]
+    low = (packed & 0x0F).astype(np.float32) - 8.0
+    high = ((packed >> 4) & 0x0F).astype(np.float32) - 8.0
+    quants = np.empty((n_blocks, 32), dtype=np.float32)
+    quants[:, 0:16] = low
+    quants[:, 16:32] = high
+    return (scales * quants).reshape(-1)
+
+
+DEQUANT = {QTYPE_Q4_0: dequantize_q4_0, QTYPE_Q8_0: dequantize_q8_0}
+
+
+def dequantize_matrix(raw: np.ndarray, qtype: int, rows: int, cols: int) -> np.ndarray:
+    """Raw blocks of one (rows, cols) matrix -> f32 (rows, cols), the reshape
+    ``gguf_parser.load_tensor`` applies (gguf_parser.py:478-487)."""
+    return DEQUANT[qtype](np.ascontiguousarray(raw), rows * cols).reshape(rows, cols)
+
+
+# --------------------------------------------------------------------------
+# math primitives, moe_forward.py:34-52
+# --------------------------------------------------------------------------
+
+def rms_norm(x, weight, eps=1e-6):
+    ms = np.mean(x * x) + eps
+    return (x / np.sqrt(ms)) * weight
+
+
+def silu(x):
+    return x / (1.0 + np.exp(-np.clip(x, -88, 88)))
+
+
+def softmax(x):
+    m = np.max(x)
+    e = np.exp(x - m)
+    return e / np.sum(e)
+
+
+# --------------------------------------------------------------------------
+# router
+# --------------------------------------------------------------------------
+
+def stable_topk_desc(values: np.ndarray, k: int) -> np.ndarray:
+    """Indices of the k largest values, descending; ties -> higher index first.
+    NaN sorts above every number, as numpy's argsort places it last."""
+    return np.argsort(values, kind="stable")[-k:][::-1]
+
+
+def route_topk_softmax(x: np.ndarray, gate_w: np.ndarray, k: int,
+                       bias: Optional[np.ndarray] = None) -> Tuple[np.ndarray, np.ndarray, bool]:
+    """MoERouter.route, moe_forward.py:99-109 (mode 0).
+
+    Returns (ids descending, weights, tie_flag).  ``tie_flag`` is True when
+    numpy's default argsort would select or order differently from the stable
+    rule (only possible with exactly equal logits)."""
+    logits = x @ gate_w
+    if bias is not None:
+        logits = logits + bias
+    ids = stable_topk_desc(logits, k)
+    default_ids = np.argsort(logits)[-k:][::-1]
+    weights = softmax(logits[ids])
+    return ids.astype(np.int64), weights.astype(np.float32), bool(np.any(default_ids != ids))
+
+
+def route_softmax_topk_renorm(x: np.ndarray, gate_w: np.ndarray, k: int,
+                              bias: Optional[np.ndarray] = None):
+    """Production routing, nightmare_stream.py:3227-3238 (mode 1): softmax over
+    all experts, top-k by probability (ascending order, as argsort yields it),
+    renormalise the k probabilities."""
+    logits = x @ gate_w
+    if bias is not None:
+        logits = logits + bias
+    gl_max = np.max(logits)
+    exp_gl = np.exp(logits - gl_max)
+    probs = exp_gl / np.sum(exp_gl)
+    ids = np.argsort(probs, kind="stable")[-k:]
+    default_ids = np.argsort(probs)[-k:]
+    w = probs[ids]
+    w = w / np.sum(w)
+    return ids.astype(np.int64), w.astype(np.float32), bool(np.any(default_ids != ids))
+
+
+def route(x, gate_w, k, mode=0, bias=None):
+    if mode == 0:
+        return route_topk_softmax(x, gate_w, k, bias)
+    if mode == 1:
+        return route_softmax_topk_renorm(x, gate_w, k, bias)
+    raise ValueError(f"unknown routing mode {mode}")
+
+
+def router_logits(x: np.ndarray, gate_w: np.ndarray, bias: Optional[np.ndarray] = None) -> np.ndarray:
+    lg = x @ gate_w
+    return lg if bias is None else lg + bias
+
+
+# --------------------------------------------------------------------------
+# experts and layer
+# --------------------------------------------------------------------------
+
+class DenseExpert:
+    """ExpertFFN, moe_forward.py:116-133, on dequantised f32 weights."""
+
+    def __init__(self, w_gate, w_up, w_down):
+        self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
+
+    def forward(self, x):
+        gate = x @ self.w_gate.T
+        up = x @ self.w_up.T
+        return (silu(gate) * up) @ self.w_down.T
+
+
+def expert_from_blocks(raw_gate, raw_up, raw_down, qtype, d, F) -> DenseExpert:
+    return DenseExpert(dequantize_matrix(raw_gate, qtype, F, d),
+                       dequantize_matrix(raw_up, qtype, F, d),
+                       dequantize_matrix(raw_down, qtype, d, F))
+
+
+class LazyExperts:
+    """Dequantises an expert the first time a token routes to it."""
+
+    def __init__(self, w_gate, w_up, w_down, qtype, d, F):
+        self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
+        self.qtype, self.d, self.F = qtype, d, F
+        self.cache = {}
+
+    def __getitem__(self, e) -> DenseExpert:
+        e = int(e)
+        if e not in self.cache:
+            self.cache[e] = expert_from_blocks(self.w_gate[e], self.w_up[e], self.w_down[e],
+                                               self.qtype, self.d, self.F)
+        return self.cache[e]
+
+    def __len__(self):
+        return self.w_gate.shape[0]
+
+
+def moe_layer_token(x, gate_w, experts, k, mode=0, shared=None, bias=None):
+    """MoELayer.forward for one token, moe_forward.py:154-174.
+
+    Returns (output, ids, weights, tie_flag)."""
+    ids, weights, tie = route(x, gate_w, k, mode, bias)
+    output = np.zeros_like(x)
+    for eid, w in zip(ids, weights):
+        expert_out = experts[eid].forward(x)
+        output += w * expert_out
+    if shared is not None:
+        output += shared.forward(x)
+    return output, ids, weights, tie
+
+
+def moe_layer(xs, gate_w, experts, k, mode=0, shared=None, bias=None, tokens=None):
+    """Token loop over moe_layer_token (how MoETransformerModel batches,
+    moe_forward.py:261-281).  ``tokens`` selects a subset of rows."""
+    rows = range(xs.shape[0]) if tokens is None else tokens
+    outs, all_ids, all_w, ties = [], [], [], []
+    for t in rows:
+        o, ids, w, tie = moe_layer_token(xs[t], gate_w, experts, k, mode, shared, bias)
+        outs.append(o)
+        all_ids.append(ids)
+        all_w.append(w)
+        ties.append(tie)
+    return (np.stack(outs), np.stack(all_ids).astype(np.int32), np.stack(all_w),
+            np.array(ties, dtype=bool))
+
+
+def moe_layer_with_ids(xs, experts, ids, weights, shared=None):
+    """Layer output for given routing decisions (used where a near-tie lets
+    the device legitimately pick a different k-th expert)."""
+    out = np.zeros_like(xs)
+    for t in range(xs.shape[0]):
+        acc = np.zeros_like(xs[t])
+        for eid, w in zip(ids[t], weights[t]):
+            acc += np.float32(w) * experts[int(eid)].forward(xs[t])
+        if shared is not None:
+            acc += shared.forward(xs[t])
+        out[t] = acc
+    return out
+
+
+def dispatch(ids: np.ndarray, n_experts: int):
+    """Stable counting sort of (token, slot) pairs by expert.
+
+    Returns (expert_offsets[E+1], perm_rows[P], inv_perm[P]): row r of the
+    expert-sorted order holds pair perm_rows[r] = t*k + slot, and pair p sits
+    at row inv_perm[p].  Within an expert, pairs keep ascending (t, slot)."""
+    flat = ids.reshape(-1).astype(np.int64)
+    order = np.argsort(flat, kind="stable")
+    counts = np.bincount(flat, minlength=n_experts)
+    offsets = np.zeros(n_experts + 1, dtype=np.int32)
+    offsets[1:] = np.cumsum(counts)
+    inv = np.empty_like(order)
+    inv[order] = np.arange(order.size)
+    return offsets, order.astype(np.int32), inv.astype(np.int32)
+
+
+def stacked_forward(x, layers, k, mode=0):
+    """Stacked decode: per layer ``x = x + moe(rms_norm(x, w))`` with the
+    residual and RMSNorm of MoETransformerModel._layer_forward
+    (moe_forward.py:348-359).  ``layers`` is a list of
+    (gate_w, experts, shared, norm_w, bias)."""
+    out = x.copy()
+    for gate_w, experts, shared, norm_w, bias in layers:
+        nxt = np.empty_like(out)
+        for t in range(out.shape[0]):
+            xn = rms_norm(out[t], norm_w).astype(np.float32)
+            o, _, _, _ = moe_layer_token(xn, gate_w, experts, k, mode, shared, bias)
+            nxt[t] = out[t] + o
+        out = nxt
+    return out
+
+
+def compare(actual: np.ndarray, expected: np.ndarray) -> Tuple[float, float]:
+    """(max-abs, rel-L2) of actual against expected."""
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    diff = a - e
+    denom = np.linalg.norm(e)
+    return float(np.max(np.abs(diff))) if diff.size else 0.0, \
+        float(np.linalg.norm(diff) / denom) if denom > 0 else float(np.linalg.norm(diff))

@@ -1,0 +1,24 @@
+"""Shared pytest configuration.
+
+Tests marked ``gpu`` need a CUDA device (B200) and the in-tree CUDA library;
+everything else runs on the CPU.
+"""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU and the built libmoe_b200.so")
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return GOLDEN

@@ -1,0 +1,373 @@
+"""Generate the golden fixtures by running the reference implementation.
+
+Run from the repository root, in a container where the reference checkout is
+available (default ``/root/reference``, override with ``MOE_REFERENCE_DIR``):
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own modules -- ``moe_forward`` (router, expert
+FFN, layer), ``dequant_fast`` (Q8_0 / Q4_0 decoders, through the reference's
+``nightmare_np`` substrate for the known-answer blocks and through numpy for
+bulk weights, which computes the same values) and ``nightmare_stream``
+(production routing, ``GPUStreamEngine._moe_ffn``) -- feeds them the seeded
+inputs of ``linuxnightmaresuite_b200.synth`` and stores their outputs with a
+sha256 of the inputs.  The fixtures hold outputs only; tests regenerate the
+inputs from the seed and check the digest.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import platform
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("MOE_REFERENCE_DIR", "/root/reference")
+sys.path.insert(0, ROOT)
+
+from linuxnightmaresuite_b200 import synth  # noqa: E402
+
+
+def _import_reference():
+    sys.path.insert(0, REF)
+    import dequant_fast  # noqa: F401  (real nightmare_np substrate)
+    import moe_forward
+    import nightmare_stream
+    return moe_forward, dequant_fast, nightmare_stream
+
+
+def _dequant_fast_on_numpy():
+    """The reference decoder module with numpy bound as its ``np``."""
+    saved = sys.modules.get("nightmare_np")
+    sys.modules["nightmare_np"] = np
+    try:
+        spec = importlib.util.spec_from_file_location("dequant_fast_numpy",
+                                                      os.path.join(REF, "dequant_fast.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        if saved is not None:
+            sys.modules["nightmare_np"] = saved
+        else:
+            del sys.modules["nightmare_np"]
+    return mod
+
+
+def _nightmare_stream_on_numpy():
+    """nightmare_stream with numpy bound as its ``np`` (fast enough for full
+    layers; the pure-Python substrate is used for the router goldens)."""
+    saved = sys.modules.get("nightmare_np")
+    sys.modules["nightmare_np"] = np
+    try:
+        spec = importlib.util.spec_from_file_location("nightmare_stream_numpy",
+                                                      os.path.join(REF, "nightmare_stream.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        if saved is not None:
+            sys.modules["nightmare_np"] = saved
+        else:
+            del sys.modules["nightmare_np"]
+    return mod
+
+
+def _substrate(ns):
+    """(to_array, to_numpy) converters for the module's ``np``."""
+    if ns.np is np:
+        return (lambda a: a), (lambda a: np.asarray(a))
+    nnp = ns.np
+
+    def to_arr(a):
+        a = np.asarray(a, np.float32)
+        return nnp.array(a.reshape(-1).tolist(), dtype=nnp.float32).reshape(*a.shape)
+
+    def to_np(a):
+        return np.asarray(a.reshape(-1).tolist(), dtype=np.float32).reshape(tuple(a.shape))
+
+    return to_arr, to_np
+
+
+def _meta():
+    return dict(numpy_version=np.__version__, machine=platform.machine(),
+                processor=platform.processor() or "")
+
+
+def kat_blocks(dq):
+    """Known-answer blocks: special fp16 scales x extreme quants."""
+    scales = np.array([0.0, -0.0, 5.96e-08, 6.1e-05, 1.0, -1.0, 0.5, 65504.0, 0.00213],
+                      dtype=np.float16)
+    q8_vals = np.array([-128, -127, -1, 0, 1, 127], dtype=np.int8)
+    q8 = []
+    for s in scales:
+        for v in q8_vals:
+            blk = np.empty(34, np.uint8)
+            blk[:2] = np.array([s], np.float16).view(np.uint8)
+            q = np.full(32, v, np.int8)
+            q[::3] = np.int8(-v if v != -128 else 127)
+            blk[2:] = q.view(np.uint8)
+            q8.append(blk)
+    q4 = []
+    for s in scales:
+        for lo in range(16):
+            blk = np.empty(18, np.uint8)
+            blk[:2] = np.array([s], np.float16).view(np.uint8)
+            nib_lo = (np.arange(16) + lo) % 16
+            nib_hi = (15 - np.arange(16) - lo) % 16
+            blk[2:] = (nib_lo | (nib_hi << 4)).astype(np.uint8)
+            q4.append(blk)
+    q8 = np.stack(q8)
+    q4 = np.stack(q4)
+    exp8 = np.asarray(dq.dequantize_q8_0(q8.tobytes(), q8.shape[0] * 32), dtype=np.float32)
+    exp4 = np.asarray(dq.dequantize_q4_0(q4.tobytes(), q4.shape[0] * 32), dtype=np.float32)
+    np.savez(os.path.join(HERE, "kat_blocks.npz"), q8_raw=q8, q8_expected=exp8,
+             q4_raw=q4, q4_expected=exp4, **_meta())
+    print("kat_blocks", q8.shape, q4.shape)
+
+
+def router_cases(mf, ns, ns_np):
+    """Router goldens for both routing semantics, incl. exact-tie cases."""
+    rng = np.random.default_rng(123)
+    cases = {}
+    for ci, (d, E, k) in enumerate([(64, 8, 2), (256, 128, 8), (96, 16, 4)]):
+        T = 16
+        x = rng.standard_normal((T, d), dtype=np.float32)
+        G = (rng.standard_normal((d, E), dtype=np.float32) * np.float32(0.02))
+        if ci == 2:
+            # duplicated router columns -> exactly equal logits
+            G[:, 5] = G[:, 3]
+            G[:, 9] = G[:, 3]
+            G[:, 12] = G[:, 0]
+        router = mf.MoERouter(G, E, k)
+        ids0, w0 = [], []
+        for t in range(T):
+            i, w = router.route(x[t])
+            ids0.append(i)
+            w0.append(np.asarray(w, np.float32))
+        # production semantics: softmax over all experts, top-k, renormalise
+        # On the pure-Python nightmare_np substrate, argsort returns float
+        # indices and ``probs[top_idx]`` then gathers the wrong entries, so
+        # its weights are wrong while its ids are right.  Ids are pinned on
+        # both substrates; weights on the numpy-bound copy.
+        # Exactly tied logits (case 2) are ordered by numpy's default, unstable
+        # argsort in the numpy-bound copy and by nightmare_np's stable argsort
+        # in the substrate run; both are kept.
+        ids1, w1, ids1_np, substrate_weight_defects = [], [], [], 0
+        for t in range(T):
+            ids_t, w_t = _production_route(ns, G.T.copy(), x[t], E, k)
+            ids_n, w_n = _production_route(ns_np, G.T.copy(), x[t], E, k)
+            assert sorted(ids_t.tolist()) == sorted(ids_n.tolist()) or ci == 2, (ids_t, ids_n)
+            substrate_weight_defects += int(not np.allclose(np.sort(w_t), np.sort(w_n),
+                                                            rtol=1e-5, atol=1e-7))
+            # weights by expert from the numpy-bound run, in the substrate's order
+            wmap = dict(zip(ids_n.tolist(), w_n.tolist()))
+            if set(wmap) == set(ids_t.tolist()):
+                w_sub = np.array([wmap[e] for e in ids_t.tolist()], np.float32)
+            else:
+                w_sub = w_n
+                ids_t = ids_n
+            ids1.append(ids_t)
+            ids1_np.append(ids_n)
+            w1.append(w_sub)
+        cases[f"c{ci}_ids_mode1_numpy"] = np.array(ids1_np, np.int32)
+        cases[f"c{ci}_nightmare_np_weight_defects"] = np.int32(substrate_weight_defects)
+        cases[f"c{ci}_x"] = x
+        cases[f"c{ci}_G"] = G
+        cases[f"c{ci}_k"] = np.int32(k)
+        cases[f"c{ci}_ids_mode0"] = np.array(ids0, np.int32)
+        cases[f"c{ci}_w_mode0"] = np.array(w0, np.float32)
+        cases[f"c{ci}_ids_mode1"] = np.array(ids1, np.int32)
+        cases[f"c{ci}_w_mode1"] = np.array(w1, np.float32)
+    np.savez(os.path.join(HERE, "router.npz"), **cases, **_meta())
+    print("router cases", len(cases))
+
+
+class _FakeEngine:
+    """Just enough state for GPUStreamEngine._moe_ffn to run one token."""
+
+    def __init__(self, ns, dim, n_exp, k, experts):
+        self.dim = dim
+        self._n_experts = n_exp
+        self._n_experts_used = k
+        self._architecture = "qwen2moe"
+        self._ffn_activation = "swiglu"
+        to_arr, _ = _substrate(ns)
+        self._experts = {e: tuple(to_arr(m) for m in mats) for e, mats in experts.items()}
+        self.routed = []
+        self._uses_geglu_expert = lambda: ns.GPUStreamEngine._uses_geglu_expert(self)
+        self._expert_act = lambda g, u: ns.GPUStreamEngine._expert_act(self, g, u)
+
+    def _load_expert(self, layer_idx, ei):
+        self.routed.append(int(ei))
+        return self._experts[int(ei)]
+
+
+def _production_route(ns, R, x, E, k):
+    """Routing decision of GPUStreamEngine._moe_ffn (nightmare_stream.py:3227-3238).
+
+    Runs the real method with probe experts: expert e has one hidden unit that
+    reads input j (the largest |x|) and writes ``act`` to output e, so the
+    layer output at e is ``w_e * act``.  Needs d >= E."""
+    d = x.shape[0]
+    assert d >= E
+    j = int(np.argmax(np.abs(x)))
+    experts = {}
+    for e in range(E):
+        g = np.zeros((1, d), np.float32)
+        g[0, j] = 1.0
+        dn = np.zeros((d, 1), np.float32)
+        dn[e, 0] = 1.0
+        experts[e] = (g, g.copy(), dn)
+    eng = _FakeEngine(ns, d, E, k, experts)
+    to_arr, to_np = _substrate(ns)
+    out = to_np(ns.GPUStreamEngine._moe_ffn(eng, to_arr(x.reshape(1, -1)), 0,
+                                            {"moe_router": to_arr(R)})).reshape(-1)
+    ids = np.array(eng.routed, np.int32)
+    xj = to_arr(np.array([x[j]], np.float32))
+    act = to_np(eng._expert_act(xj, xj))[0]
+    return ids, (out[ids] / act).astype(np.float32)
+
+
+def _production_layer(ns, R, x, E, k, experts):
+    """Output of GPUStreamEngine._moe_ffn for one token with real experts."""
+    d = x.shape[0]
+    eng = _FakeEngine(ns, d, E, k, {e: (ex.w_gate, ex.w_up, ex.w_down)
+                                    for e, ex in enumerate(experts) if ex is not None})
+    to_arr, to_np = _substrate(ns)
+    out = to_np(ns.GPUStreamEngine._moe_ffn(eng, to_arr(x.reshape(1, -1)), 0,
+                                            {"moe_router": to_arr(R)})).reshape(-1)
+    return out, np.array(eng.routed, np.int32)
+
+
+def _ref_experts(dqn, data, E_used):
+    """Reference ExpertFFN objects for the experts in E_used (others None)."""
+    cfg = data.cfg
+    d, F, qt = cfg.d_model, cfg.ffn, cfg.qtype
+    fn = dqn.DEQUANT_FUNCTIONS[qt]
+    import moe_forward as mf
+    experts = [None] * cfg.n_experts
+    for e in sorted(set(int(v) for v in E_used)):
+        wg = np.asarray(fn(data.w_gate[e].tobytes(), F * d), np.float32).reshape(F, d)
+        wu = np.asarray(fn(data.w_up[e].tobytes(), F * d), np.float32).reshape(F, d)
+        wd = np.asarray(fn(data.w_down[e].tobytes(), d * F), np.float32).reshape(d, F)
+        experts[e] = mf.ExpertFFN(wg, wu, wd)
+    return experts
+
+
+def _ref_shared(dqn, data):
+    import moe_forward as mf
+    cfg = data.cfg
+    d, Fs, qt = cfg.d_model, cfg.shared_ffn, cfg.shared_qtype
+    fn = dqn.DEQUANT_FUNCTIONS[qt]
+    wg = np.asarray(fn(data.s_gate[0].tobytes(), Fs * d), np.float32).reshape(Fs, d)
+    wu = np.asarray(fn(data.s_up[0].tobytes(), Fs * d), np.float32).reshape(Fs, d)
+    wd = np.asarray(fn(data.s_down[0].tobytes(), d * Fs), np.float32).reshape(d, Fs)
+    return mf.ExpertFFN(wg, wu, wd)
+
+
+def layer_case(mf, ns, dqn, name, cfg, seed, tokens, mode, n_experts_built=None):
+    data = synth.make_layer(cfg, seed, tokens=tokens, n_experts_built=n_experts_built)
+    x, G = data.x, data.gate_w
+    E, k, d = cfg.n_experts, cfg.top_k, cfg.d_model
+    if data.bias is not None:
+        # the reference router has no bias term; an extra constant input
+        # feature whose router row is the bias adds it to every logit
+        G_use = np.concatenate([G, data.bias[None, :]], axis=0)
+        x_router = np.concatenate([x, np.ones((x.shape[0], 1), np.float32)], axis=1)
+    else:
+        G_use, x_router = G, x
+    router = mf.MoERouter(G_use, E, k)
+    all_ids = []
+    for t in range(x.shape[0]):
+        if mode == 0:
+            i, _ = router.route(x_router[t])
+        else:
+            i, _ = _production_route(ns, G_use.T.copy(), x_router[t], E, k)
+        all_ids.extend(int(v) for v in i)
+    experts = _ref_experts(dqn, data, all_ids)
+    shared = _ref_shared(dqn, data) if cfg.shared_ffn else None
+    outs, ids_l, w_l = [], [], []
+    for t in range(x.shape[0]):
+        if mode == 0:
+            if data.bias is None:
+                layer = mf.MoELayer(router, experts, shared)
+                out = layer.forward(x[t])
+                i, w = router.route(x[t])
+            else:
+                i, w = router.route(x_router[t])
+                out = np.zeros_like(x[t])
+                for eid, ww in zip(i, w):
+                    out += ww * experts[eid].forward(x[t])
+                if shared is not None:
+                    out += shared.forward(x[t])
+        else:
+            if data.bias is not None:
+                raise NotImplementedError("bias with production routing")
+            out, i_out = _production_layer(ns, G.T.copy(), x[t], E, k, experts)
+            if shared is not None:
+                out = out + shared.forward(x[t])
+            i, w = _production_route(ns, G.T.copy(), x[t], E, k)
+            assert np.array_equal(i, i_out)
+        outs.append(np.asarray(out, np.float32))
+        ids_l.append(np.asarray(i, np.int32))
+        w_l.append(np.asarray(w, np.float32))
+    np.savez(os.path.join(HERE, f"layer_{name}.npz"), out=np.stack(outs), ids=np.stack(ids_l),
+             weights=np.stack(w_l), seed=np.int32(seed), tokens=np.int32(x.shape[0]),
+             mode=np.int32(mode), config=cfg.name, digest=data.digest(),
+             n_experts_built=np.int32(-1 if n_experts_built is None else n_experts_built),
+             **_meta())
+    print("layer", name, np.stack(outs).shape)
+
+
+def stacked_case(mf, dqn, name, cfg, seed, n_layers, tokens):
+    """Stacked layers composed from the reference's rms_norm and MoELayer."""
+    x0 = None
+    layers = []
+    for l in range(n_layers):
+        data = synth.make_layer(cfg, seed + l, tokens=tokens)
+        if x0 is None:
+            x0 = data.x
+        layers.append(data)
+    x = x0.copy()
+    for data in layers:
+        router = mf.MoERouter(data.gate_w, cfg.n_experts, cfg.top_k)
+        xn_all = np.stack([mf.rms_norm(x[t], data.norm_w).astype(np.float32) for t in range(x.shape[0])])
+        used = []
+        for t in range(x.shape[0]):
+            used.extend(router.route(xn_all[t])[0])
+        experts = _ref_experts(dqn, data, used)
+        shared = _ref_shared(dqn, data)
+        layer = mf.MoELayer(router, experts, shared)
+        x = np.stack([x[t] + layer.forward(xn_all[t]) for t in range(x.shape[0])]).astype(np.float32)
+    np.savez(os.path.join(HERE, f"stacked_{name}.npz"), out=x, seed=np.int32(seed),
+             n_layers=np.int32(n_layers), tokens=np.int32(tokens), config=cfg.name,
+             digest=layers[0].digest(), **_meta())
+    print("stacked", name, x.shape)
+
+
+def main():
+    mf, dq_real, ns = _import_reference()
+    dqn = _dequant_fast_on_numpy()
+    kat_blocks(dq_real)
+    ns_np = _nightmare_stream_on_numpy()
+    router_cases(mf, ns, ns_np)
+    ns = ns_np
+    C = synth.CONFIGS
+    layer_case(mf, ns, dqn, "cpu_layer_mode0", C["cpu_layer"], 0, None, 0)
+    layer_case(mf, ns, dqn, "cpu_layer_mode1", C["cpu_layer"], 0, None, 1)
+    layer_case(mf, ns, dqn, "decode_t2", C["decode_t8"], 0, 2, 0)
+    small_shared = synth.MoEConfig("small_shared", 256, 16, 4, 128, 6, synth.QTYPE_Q4_0, 0.01,
+                                   shared_ffn=192, n_layers=1)
+    layer_case(mf, ns, dqn, "small_shared", small_shared, 7, None, 0)
+    small_zipf = synth.MoEConfig("small_zipf", 256, 16, 4, 128, 64, synth.QTYPE_Q8_0, 0.002,
+                                 zipf_s=1.1, zipf_max_rows=40)
+    layer_case(mf, ns, dqn, "small_zipf", small_zipf, 3, None, 0)
+    small_stack = synth.MoEConfig("small_stack", 256, 16, 4, 128, 5, synth.QTYPE_Q4_0, 0.01,
+                                  shared_ffn=192, n_layers=2)
+    stacked_case(mf, dqn, "small_stack", small_stack, 11, 2, 5)
+
+
+if __name__ == "__main__":
+    main()

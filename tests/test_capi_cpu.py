@@ -1,0 +1,66 @@
+"""CPU-side checks of the C ABI: the library loads and exports every entry
+point include/moe_b200.h declares; argument validation runs without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from linuxnightmaresuite_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "moe_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*int\s+(moe_\w+)\s*\(", src, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from linuxnightmaresuite_b200 import build
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for n in ("moe_router", "moe_dispatch", "moe_experts", "moe_combine", "moe_layer_forward",
+              "moe_pack_weights", "moe_dequantize"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+
+
+def test_version_and_geometry(lib):
+    assert lib.moe_version() == 10000
+    e, b = ctypes.c_int(), ctypes.c_int()
+    assert lib.moe_block_geometry(2, ctypes.byref(e), ctypes.byref(b)) == 0
+    assert (e.value, b.value) == (32, 18)
+    assert lib.moe_block_geometry(8, ctypes.byref(e), ctypes.byref(b)) == 0
+    assert (e.value, b.value) == (32, 34)
+    assert lib.moe_block_geometry(12, ctypes.byref(e), ctypes.byref(b)) == _lib.MOE_ERR_UNSUPPORTED
+    assert "not supported" in _lib.last_error()
+
+
+def test_argument_validation_without_gpu(lib):
+    # k > E is rejected before any device work
+    rc = lib.moe_router(ctypes.c_void_p(16), ctypes.c_void_p(16), None, 4, 64, 8, 9, 0, 0,
+                        ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 1 << 20,
+                        None)
+    assert rc == _lib.MOE_ERR_INVALID
+    assert "exceeds" in _lib.last_error()
+    # pack needs rows % 16 and cols % 64
+    rc = lib.moe_pack_weights(ctypes.c_void_p(16), ctypes.c_void_p(16), 8, 1, 10, 64, None)
+    assert rc == _lib.MOE_ERR_UNSUPPORTED
+    sz = ctypes.c_size_t()
+    assert lib.moe_packed_bytes(2, 128, 704, 2816, ctypes.byref(sz)) == 0
+    assert sz.value == 128 * 704 * 88 * 18
+    assert lib.moe_experts_workspace_bytes(512, 128, 2816, 704, ctypes.byref(sz)) == 0
+    assert sz.value > 0
