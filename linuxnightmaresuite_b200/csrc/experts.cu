@@ -20,6 +20,8 @@
 // reference's f32 tolerance needs; a single fp16 rounding does not.
 #include <math.h>
 
+#include <algorithm>
+
 #include "moe_common.cuh"
 
 namespace moe {
@@ -27,21 +29,6 @@ namespace moe {
 constexpr int kMaxCG = 4;                 // column groups (4 rows each) per pass
 constexpr float kHScale = 1.0f / 256.0f;  // hidden activations are stored / 256
 constexpr int kPlanThreads = 1024;
-
-__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
-  uint2 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-               : "=r"(r.x), "=r"(r.y)
-               : "l"(p));
-  return r;
-}
 
 __device__ __forceinline__ float half_lo(uint32_t v) {
   return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu)));
@@ -207,7 +194,7 @@ xprep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, in
 }
 
 // ---------------------------------------------------------------------------
-// one 64-wide tile of a 16-row strip against ncg column groups
+// tile fragments
 // ---------------------------------------------------------------------------
 template <int QT>
 struct TileRegs {
@@ -215,19 +202,20 @@ struct TileRegs {
   uint2 sc;
 };
 
+// fragment registers of one staged tile (shared memory, lane-contiguous)
 template <int QT>
-__device__ __forceinline__ void load_tile(TileRegs<QT>& r, const uint8_t* tile, int lane) {
+__device__ __forceinline__ void lds_tile(TileRegs<QT>& r, const uint8_t* tile, int lane) {
   using Tr = QTraits<QT>;
   const uint8_t* qp = tile + lane * Tr::kLaneBytes;
-  r.q[0] = ldg_stream_v4(qp);
-  if (QT == MOE_Q8_0) r.q[QT == MOE_Q4_0 ? 0 : 1] = ldg_stream_v4(qp + 16);
-  r.sc = ldg_stream_v2(tile + Tr::kTileQuant + (lane >> 2) * 8);
+  r.q[0] = *reinterpret_cast<const uint4*>(qp);
+  if (QT == MOE_Q8_0) r.q[QT == MOE_Q4_0 ? 0 : 1] = *reinterpret_cast<const uint4*>(qp + 16);
+  r.sc = *reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + (lane >> 2) * 8);
 }
 
-// A fragments of both k16 steps for block b (rows g and g+8)
+// A fragments of both k16 steps for block b (rows g and g+8), block scales
 template <int QT>
 __device__ __forceinline__ void tile_afrags(const TileRegs<QT>& r, int b, uint32_t (&a0)[4],
-                                            uint32_t (&a1)[4], float& dg, float& dg8) {
+                                            uint32_t (&a1)[4], float2& dg, float2& dg8) {
   if (QT == MOE_Q4_0) {
     uint32_t wg = b ? r.q[0].y : r.q[0].x;
     uint32_t w8 = b ? r.q[0].w : r.q[0].z;
@@ -249,38 +237,123 @@ __device__ __forceinline__ void tile_afrags(const TileRegs<QT>& r, int b, uint32
     dequant_q8(e1, y01, y23);
     a1[0] = x01; a1[1] = y01; a1[2] = x23; a1[3] = y23;
   }
-  dg = b ? half_hi(r.sc.x) : half_lo(r.sc.x);
-  dg8 = b ? half_hi(r.sc.y) : half_lo(r.sc.y);
+  const float s0 = b ? half_hi(r.sc.x) : half_lo(r.sc.x);
+  const float s8 = b ? half_hi(r.sc.y) : half_lo(r.sc.y);
+  dg = make_float2(s0, s0);
+  dg8 = make_float2(s8, s8);
 }
 
-__device__ __forceinline__ void block_mma(float (&acc)[4], const uint32_t (&a0)[4],
-                                          const uint32_t (&a1)[4], uint4 xf, float dg,
-                                          float dg8) {
+// One 32-weight block: two k16 MMAs into a fresh accumulator, then
+// acc += scale * block (packed f32x2 FMA).  acc[0]: row g, acc[1]: row g+8.
+__device__ __forceinline__ void block_mma(float2 (&acc)[2], const uint32_t (&a0)[4],
+                                          const uint32_t (&a1)[4], uint4 xf, float2 dg,
+                                          float2 dg8) {
   const float zero[4] = {0.f, 0.f, 0.f, 0.f};
   float tmp[4];
   mma_16816(tmp, a0[0], a0[1], a0[2], a0[3], xf.x, xf.y, zero);
   mma_16816(tmp, a1[0], a1[1], a1[2], a1[3], xf.z, xf.w, tmp);
-  acc[0] = fmaf(dg, tmp[0], acc[0]);
-  acc[1] = fmaf(dg, tmp[1], acc[1]);
-  acc[2] = fmaf(dg8, tmp[2], acc[2]);
-  acc[3] = fmaf(dg8, tmp[3], acc[3]);
+  acc[0] = __ffma2_rn(dg, make_float2(tmp[0], tmp[1]), acc[0]);
+  acc[1] = __ffma2_rn(dg8, make_float2(tmp[2], tmp[3]), acc[1]);
+}
+
+// Stages per warp of the bulk-copy rings (max / min); the split-K reduction
+// buffer (4 KB per warp) aliases a gate/up ring, so kMinGateUp * 2 tiles >= 4 KB.
+template <int QT> struct Ring;
+template <> struct Ring<MOE_Q4_0> { static constexpr int kGateUp = 8, kMinGateUp = 4, kDown = 12; };
+template <> struct Ring<MOE_Q8_0> { static constexpr int kGateUp = 6, kMinGateUp = 2, kDown = 8; };
+
+constexpr int kGuWarps = 16;            // warps per gate/up CTA
+constexpr int kDnWarps = 8;             // warps per down CTA
+constexpr int kBarArea = 2048;          // mbarriers: 1 + warps x stages, 8 B each
+constexpr int kMaxSmem = 227 * 1024;    // dynamic shared memory per CTA on sm_100
+__host__ __device__ inline int x_stage_bytes(int K, int cgp) { return cgp * (K / 32) * 512; }
+
+// ---------------------------------------------------------------------------
+// gate/up streaming for one chunk of NCG column groups.  Lane 0 keeps up to
+// nst (gate, up) tile pairs in flight with bulk copies into the warp's ring;
+// every lane reads its fragments from shared memory, releases the stage and
+// computes.  Returns false if a wait timed out.
+// ---------------------------------------------------------------------------
+template <int QT, int NCG>
+__device__ __forceinline__ bool gu_stream(float2 (&accg)[kMaxCG][2], float2 (&accu)[kMaxCG][2],
+                                          uint8_t* ring, uint64_t* bars, uint32_t& parity,
+                                          int nst, int ntile, int jb, const uint8_t* gbase,
+                                          const uint8_t* ubase, uint64_t pol,
+                                          const uint8_t* xs_lane, int cg_stride, uint64_t* xbar,
+                                          uint32_t xparity, int lane) {
+  using Tr = QTraits<QT>;
+  constexpr int TB = Tr::kTileBytes;
+  constexpr int STAGE = 2 * TB;
+  if (lane == 0) {
+    fence_proxy_async_smem();
+    for (int i = 0; i < min(nst, ntile); ++i) {
+      mbar_expect_tx(&bars[i], STAGE);
+      bulk_g2s(ring + i * STAGE, gbase + (size_t)(jb + i) * TB, TB, &bars[i], pol);
+      bulk_g2s(ring + i * STAGE + TB, ubase + (size_t)(jb + i) * TB, TB, &bars[i], pol);
+    }
+  }
+  if (!mbar_wait(xbar, xparity)) return false;
+  int st = 0;
+  for (int i = 0; i < ntile; ++i) {
+    if (!mbar_wait(&bars[st], (parity >> st) & 1u)) return false;
+    parity ^= 1u << st;
+    TileRegs<QT> tg, tu;
+    uint8_t* stage = ring + st * STAGE;
+    lds_tile<QT>(tg, stage, lane);
+    lds_tile<QT>(tu, stage + TB, lane);
+    __syncwarp();
+    if (lane == 0 && i + nst < ntile) {
+      const int j = jb + i + nst;
+      fence_proxy_async_smem();
+      mbar_expect_tx(&bars[st], STAGE);
+      bulk_g2s(stage, gbase + (size_t)j * TB, TB, &bars[st], pol);
+      bulk_g2s(stage + TB, ubase + (size_t)j * TB, TB, &bars[st], pol);
+    }
+    st = (st + 1 == nst) ? 0 : st + 1;
+    const uint8_t* xj = xs_lane + (jb + i) * 1024;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      uint32_t ga0[4], ga1[4], ua0[4], ua1[4];
+      float2 dg, dg8, du, du8;
+      tile_afrags<QT>(tg, b, ga0, ga1, dg, dg8);
+      tile_afrags<QT>(tu, b, ua0, ua1, du, du8);
+#pragma unroll
+      for (int c = 0; c < NCG; ++c) {
+        const uint4 xf = *reinterpret_cast<const uint4*>(xj + c * cg_stride + b * 512);
+        block_mma(accg[c], ga0, ga1, xf, dg, dg8);
+        block_mma(accu[c], ua0, ua1, xf, du, du8);
+      }
+    }
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
-// gate / up: CTA = 8 warps = (8 / ks) strips x ks K-slices
+// gate / up: CTA = 16 warps = (16 / ks) strips of 16 F-rows x ks K-slices of
+// one expert.  The expert's activation fragments for the chunk (cgp groups of
+// 4 rows, hi + lo) are staged once per CTA with a single bulk copy.
 // ---------------------------------------------------------------------------
 template <int QT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kGuWarps * 32, 1)
 gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t mat_bytes,
               int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
               const int* __restrict__ active, const int* __restrict__ goff,
               const float* __restrict__ row_scale, const uint8_t* __restrict__ xfrag,
-              uint8_t* __restrict__ hfrag, int ks, int* __restrict__ status) {
+              uint8_t* __restrict__ hfrag, int ks, int cgp, int nst, int* __restrict__ status) {
   using Tr = QTraits<QT>;
-  __shared__ float red[8][kMaxCG * 8][32];
+  constexpr int TB = Tr::kTileBytes;
+  constexpr int STAGE = 2 * TB;
+  constexpr int SMAX = Ring<QT>::kGateUp;
+  static_assert((kGuWarps * SMAX + 1) * 8 <= kBarArea, "barrier area");
+  extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int xbytes = x_stage_bytes(d, cgp);
+  uint8_t* xs = smem;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
+  uint64_t* bars = xbar + 1 + warp * SMAX;
+  uint8_t* ring = smem + xbytes + kBarArea + warp * nst * STAGE;
   const int g = lane >> 2, t = lane & 3;
-  const int spc = 8 / ks;
+  const int spc = kGuWarps / ks;
   const int strips = F / 16;
   const int cpe = (strips + spc - 1) / spc;
   const int a = blockIdx.x / cpe;
@@ -295,69 +368,88 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   const int n = offsets[e + 1] - row0;
   const int G0 = goff[e];
   const int nbx = d / 32, nbF = F / 32;
-  const uint8_t* gbase = wg + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * Tr::kTileBytes;
-  const uint8_t* ubase = wu + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * Tr::kTileBytes;
+  const uint8_t* gbase = wg + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * TB;
+  const uint8_t* ubase = wu + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * TB;
+  const uint64_t pol = evict_first_policy();
+  if (lane == 0) {
+    for (int i = 0; i < nst; ++i) mbar_init(&bars[i], 1);
+    if (warp == 0) mbar_init(xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t parity = 0u, xparity = 0u;
+  bool ok = true;
 
-  for (int c0 = 0; c0 < n; c0 += 4 * kMaxCG) {
-    const int ncg = min(kMaxCG, (n - c0 + 3) / 4);
-    float accg[kMaxCG][4], accu[kMaxCG][4];
+  for (int c0 = 0; c0 < n; c0 += 4 * cgp) {
+    const int ncg = min(cgp, (n - c0 + 3) / 4);
+    float2 accg[kMaxCG][2], accu[kMaxCG][2];
 #pragma unroll
     for (int c = 0; c < kMaxCG; ++c)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) accg[c][i] = accu[c][i] = 0.f;
-    if (strip_ok) {
-      const uint8_t* xg = xfrag + (size_t)(G0 + c0 / 4) * nbx * 512 + lane * 16;
-#pragma unroll 2
-      for (int j = jb; j < je; ++j) {
-        TileRegs<QT> tg, tu;
-        load_tile<QT>(tg, gbase + (size_t)j * Tr::kTileBytes, lane);
-        load_tile<QT>(tu, ubase + (size_t)j * Tr::kTileBytes, lane);
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          uint32_t ga0[4], ga1[4], ua0[4], ua1[4];
-          float dg, dg8, du, du8;
-          tile_afrags<QT>(tg, b, ga0, ga1, dg, dg8);
-          tile_afrags<QT>(tu, b, ua0, ua1, du, du8);
-#pragma unroll
-          for (int c = 0; c < kMaxCG; ++c) {
-            if (c < ncg) {
-              uint4 xf = __ldg(reinterpret_cast<const uint4*>(
-                  xg + ((size_t)c * nbx + 2 * j + b) * 512));
-              block_mma(accg[c], ga0, ga1, xf, dg, dg8);
-              block_mma(accu[c], ua0, ua1, xf, du, du8);
-            }
-          }
-        }
-      }
+      for (int i = 0; i < 2; ++i) accg[c][i] = accu[c][i] = make_float2(0.f, 0.f);
+    if (threadIdx.x == 0) {
+      const uint32_t xb = (uint32_t)(ncg * nbx * 512);
+      fence_proxy_async_smem();
+      mbar_expect_tx(xbar, xb);
+      bulk_g2s_plain(xs, xfrag + (size_t)(G0 + c0 / 4) * nbx * 512, xb, xbar);
     }
+    if (strip_ok && ok) {
+      const uint8_t* xl = xs + lane * 16;
+      const int cs = nbx * 512;
+      bool r;
+      switch (ncg) {
+        case 1: r = gu_stream<QT, 1>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
+        case 2: r = gu_stream<QT, 2>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
+        case 3: r = gu_stream<QT, 3>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
+        default: r = gu_stream<QT, 4>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
+      }
+      if (!r) {
+        set_status(status, MOE_STATUS_TIMEOUT);
+        ok = false;
+      }
+    } else if (!mbar_wait(xbar, xparity)) {
+      set_status(status, MOE_STATUS_TIMEOUT);
+      ok = false;
+    }
+    xparity ^= 1u;
     if (ks > 1) {
+      // partial sums of the K-slices meet in the (now idle) rings
+      float* red = reinterpret_cast<float*>(ring);
       __syncthreads();
 #pragma unroll
       for (int c = 0; c < kMaxCG; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          red[warp][c * 8 + i][lane] = accg[c][i];
-          red[warp][c * 8 + 4 + i][lane] = accu[c][i];
+        for (int i = 0; i < 2; ++i) {
+          red[(c * 8 + 2 * i) * 32 + lane] = accg[c][i].x;
+          red[(c * 8 + 2 * i + 1) * 32 + lane] = accg[c][i].y;
+          red[(c * 8 + 4 + 2 * i) * 32 + lane] = accu[c][i].x;
+          red[(c * 8 + 5 + 2 * i) * 32 + lane] = accu[c][i].y;
         }
       __syncthreads();
       if (kp == 0) {
-        for (int q = 1; q < ks; ++q)
+        for (int q = 1; q < ks; ++q) {
+          const float* rq = reinterpret_cast<const float*>(ring + q * nst * STAGE);
 #pragma unroll
           for (int c = 0; c < kMaxCG; ++c)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              accg[c][i] += red[warp + q][c * 8 + i][lane];
-              accu[c][i] += red[warp + q][c * 8 + 4 + i][lane];
+            for (int i = 0; i < 2; ++i) {
+              accg[c][i].x += rq[(c * 8 + 2 * i) * 32 + lane];
+              accg[c][i].y += rq[(c * 8 + 2 * i + 1) * 32 + lane];
+              accu[c][i].x += rq[(c * 8 + 4 + 2 * i) * 32 + lane];
+              accu[c][i].y += rq[(c * 8 + 5 + 2 * i) * 32 + lane];
             }
+        }
       }
     }
     if (kp == 0 && strip_ok) {
 #pragma unroll
       for (int c = 0; c < kMaxCG; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          accg[c][i] += __shfl_xor_sync(0xffffffffu, accg[c][i], 2);
-          accu[c][i] += __shfl_xor_sync(0xffffffffu, accu[c][i], 2);
+        for (int i = 0; i < 2; ++i) {
+          accg[c][i].x += __shfl_xor_sync(0xffffffffu, accg[c][i].x, 2);
+          accg[c][i].y += __shfl_xor_sync(0xffffffffu, accg[c][i].y, 2);
+          accu[c][i].x += __shfl_xor_sync(0xffffffffu, accu[c][i].x, 2);
+          accu[c][i].y += __shfl_xor_sync(0xffffffffu, accu[c][i].y, 2);
         }
       if (t < 2) {
 #pragma unroll
@@ -372,13 +464,13 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
             const float rs = row_scale[row0 + tok];
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
-              float gv = accg[c][rr * 2 + ci] * rs;
-              float uv = accu[c][rr * 2 + ci] * rs;
-              float h = silu_f(gv) * uv;
-              float hs = h * kHScale;
-              if (!(fabsf(hs) <= 65504.f)) set_status(status, MOE_STATUS_ROW_OVERFLOW);
-              __half hh = __float2half_rn(hs);
-              __half hl = __float2half_rn(hs - __half2float(hh));
+              const float gacc = ci ? accg[c][rr].y : accg[c][rr].x;
+              const float uacc = ci ? accu[c][rr].y : accu[c][rr].x;
+              const float h = silu_f(gacc * rs) * (uacc * rs);
+              const float hsc = h * kHScale;
+              if (!(fabsf(hsc) <= 65504.f)) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+              const __half hh = __float2half_rn(hsc);
+              const __half hl = __float2half_rn(hsc - __half2float(hh));
               const int f = s * 16 + g + 8 * rr;
               int tf, fi;
               frag_pos<QT>(f & 31, tf, fi);
@@ -390,67 +482,141 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
         }
       }
     }
-    if (ks > 1) __syncthreads();
+    __syncthreads();  // x stage and rings are rewritten by the next chunk
   }
 }
 
 // ---------------------------------------------------------------------------
-// down: CTA = 8 warps = 8 strips of d; K = F is short, no split
+// down streaming for one chunk of NCG column groups (one tile per stage)
+// ---------------------------------------------------------------------------
+template <int QT, int NCG>
+__device__ __forceinline__ bool dn_stream(float2 (&acc)[kMaxCG][2], uint8_t* ring,
+                                          uint64_t* bars, uint32_t& parity, int nst, int JT,
+                                          const uint8_t* base, uint64_t pol,
+                                          const uint8_t* hs_lane, int cg_stride, uint64_t* xbar,
+                                          uint32_t xparity, int lane) {
+  using Tr = QTraits<QT>;
+  constexpr int TB = Tr::kTileBytes;
+  if (lane == 0) {
+    fence_proxy_async_smem();
+    for (int j = 0; j < min(nst, JT); ++j) {
+      mbar_expect_tx(&bars[j], TB);
+      bulk_g2s(ring + j * TB, base + (size_t)j * TB, TB, &bars[j], pol);
+    }
+  }
+  if (!mbar_wait(xbar, xparity)) return false;
+  int st = 0;
+  for (int j = 0; j < JT; ++j) {
+    if (!mbar_wait(&bars[st], (parity >> st) & 1u)) return false;
+    parity ^= 1u << st;
+    TileRegs<QT> tw;
+    uint8_t* stage = ring + st * TB;
+    lds_tile<QT>(tw, stage, lane);
+    __syncwarp();
+    if (lane == 0 && j + nst < JT) {
+      fence_proxy_async_smem();
+      mbar_expect_tx(&bars[st], TB);
+      bulk_g2s(stage, base + (size_t)(j + nst) * TB, TB, &bars[st], pol);
+    }
+    st = (st + 1 == nst) ? 0 : st + 1;
+    const uint8_t* xj = hs_lane + j * 1024;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      uint32_t a0[4], a1[4];
+      float2 dw, dw8;
+      tile_afrags<QT>(tw, b, a0, a1, dw, dw8);
+#pragma unroll
+      for (int c = 0; c < NCG; ++c) {
+        const uint4 xf = *reinterpret_cast<const uint4*>(xj + c * cg_stride + b * 512);
+        block_mma(acc[c], a0, a1, xf, dw, dw8);
+      }
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// down: CTA = 8 warps = 8 strips of 16 d-rows of one expert; K = F is short.
 // ---------------------------------------------------------------------------
 template <int QT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kDnWarps * 32, 3)
 down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
             const int* __restrict__ active, const int* __restrict__ goff,
             const uint8_t* __restrict__ hfrag, float* __restrict__ y,
-            const int32_t* __restrict__ y_rows) {
+            const int32_t* __restrict__ y_rows, int cgp, int nst, int* __restrict__ status) {
   using Tr = QTraits<QT>;
+  constexpr int TB = Tr::kTileBytes;
+  constexpr int SMAX = Ring<QT>::kDown;
+  static_assert((kDnWarps * SMAX + 1) * 8 <= kBarArea, "barrier area");
+  extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int xbytes = x_stage_bytes(F, cgp);
+  uint8_t* hs = smem;
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
+  uint64_t* bars = xbar + 1 + warp * SMAX;
+  uint8_t* ring = smem + xbytes + kBarArea + warp * nst * TB;
   const int g = lane >> 2, t = lane & 3;
   const int strips = d / 16;
-  const int cpe = (strips + 7) / 8;
+  const int cpe = (strips + kDnWarps - 1) / kDnWarps;
   const int a = blockIdx.x / cpe;
   if (a >= *n_active) return;
-  const int s = (blockIdx.x % cpe) * 8 + warp;
-  if (s >= strips) return;
+  const int s = (blockIdx.x % cpe) * kDnWarps + warp;
+  const bool strip_ok = s < strips;
   const int e = active[a];
   const int JT = F / 64;
   const int row0 = offsets[e];
   const int n = offsets[e + 1] - row0;
   const int G0 = goff[e];
   const int nbF = F / 32;
-  const uint8_t* base = wd + (size_t)e * mat_bytes + (size_t)s * JT * Tr::kTileBytes;
-  for (int c0 = 0; c0 < n; c0 += 4 * kMaxCG) {
-    const int ncg = min(kMaxCG, (n - c0 + 3) / 4);
-    float acc[kMaxCG][4];
+  const uint8_t* base = wd + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * TB;
+  const uint64_t pol = evict_first_policy();
+  if (lane == 0) {
+    for (int i = 0; i < nst; ++i) mbar_init(&bars[i], 1);
+    if (warp == 0) mbar_init(xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t parity = 0u, xparity = 0u;
+  bool ok = true;
+  for (int c0 = 0; c0 < n; c0 += 4 * cgp) {
+    const int ncg = min(cgp, (n - c0 + 3) / 4);
+    float2 acc[kMaxCG][2];
 #pragma unroll
-    for (int c = 0; c < kMaxCG; ++c)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[c][i] = 0.f;
-    const uint8_t* hg = hfrag + (size_t)(G0 + c0 / 4) * nbF * 512 + lane * 16;
-#pragma unroll 2
-    for (int j = 0; j < JT; ++j) {
-      TileRegs<QT> tw;
-      load_tile<QT>(tw, base + (size_t)j * Tr::kTileBytes, lane);
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        uint32_t a0[4], a1[4];
-        float dw, dw8;
-        tile_afrags<QT>(tw, b, a0, a1, dw, dw8);
-#pragma unroll
-        for (int c = 0; c < kMaxCG; ++c) {
-          if (c < ncg) {
-            uint4 xf = __ldg(reinterpret_cast<const uint4*>(hg + ((size_t)c * nbF + 2 * j + b) * 512));
-            block_mma(acc[c], a0, a1, xf, dw, dw8);
-          }
-        }
-      }
+    for (int c = 0; c < kMaxCG; ++c) acc[c][0] = acc[c][1] = make_float2(0.f, 0.f);
+    if (threadIdx.x == 0) {
+      const uint32_t hb = (uint32_t)(ncg * nbF * 512);
+      fence_proxy_async_smem();
+      mbar_expect_tx(xbar, hb);
+      bulk_g2s_plain(hs, hfrag + (size_t)(G0 + c0 / 4) * nbF * 512, hb, xbar);
     }
+    if (strip_ok && ok) {
+      const uint8_t* hl = hs + lane * 16;
+      const int cs = nbF * 512;
+      bool r;
+      switch (ncg) {
+        case 1: r = dn_stream<QT, 1>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
+        case 2: r = dn_stream<QT, 2>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
+        case 3: r = dn_stream<QT, 3>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
+        default: r = dn_stream<QT, 4>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
+      }
+      if (!r) {
+        set_status(status, MOE_STATUS_TIMEOUT);
+        ok = false;
+      }
+    } else if (!mbar_wait(xbar, xparity)) {
+      set_status(status, MOE_STATUS_TIMEOUT);
+      ok = false;
+    }
+    xparity ^= 1u;
 #pragma unroll
     for (int c = 0; c < kMaxCG; ++c)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[c][i] += __shfl_xor_sync(0xffffffffu, acc[c][i], 2);
-    if (t < 2) {
+      for (int i = 0; i < 2; ++i) {
+        acc[c][i].x += __shfl_xor_sync(0xffffffffu, acc[c][i].x, 2);
+        acc[c][i].y += __shfl_xor_sync(0xffffffffu, acc[c][i].y, 2);
+      }
+    if (t < 2 && strip_ok) {
 #pragma unroll
       for (int c = 0; c < kMaxCG; ++c) {
         if (c >= ncg) continue;
@@ -461,11 +627,12 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
           const int r = row0 + tok;
           const int orow = y_rows ? y_rows[r] : r;
           float* yr = y + (size_t)orow * d + s * 16 + g;
-          yr[0] = acc[c][ci] * (1.0f / kHScale);
-          yr[8] = acc[c][2 + ci] * (1.0f / kHScale);
+          yr[0] = (ci ? acc[c][0].y : acc[c][0].x) * (1.0f / kHScale);
+          yr[8] = (ci ? acc[c][1].y : acc[c][1].x) * (1.0f / kHScale);
         }
       }
     }
+    __syncthreads();  // the staged hidden fragments are rewritten by the next chunk
   }
 }
 
@@ -507,6 +674,47 @@ int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
   return MOE_OK;
 }
 
+// Launch shape of the two GEMV kernels for a call.
+struct ExpertsPlan {
+  int ks, cgp_gu, nst_gu, smem_gu, grid_gu;
+  int cgp_dn, nst_dn, smem_dn, grid_dn;
+};
+
+template <int QT>
+static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
+  using Tr = QTraits<QT>;
+  const int est_active = rows < E ? rows : E;
+  const int strips_f = F / 16, strips_d = d / 16;
+  const int JT = d / 64;
+  const int target = sm_count() * kGuWarps;  // one full CTA per SM
+  p.ks = 1;
+  while (p.ks < 8 && (long long)est_active * strips_f * p.ks < target && JT / (2 * p.ks) >= 2)
+    p.ks *= 2;
+  const int spc = kGuWarps / p.ks;
+  p.grid_gu = est_active * ((strips_f + spc - 1) / spc);
+  // column groups per pass: about twice the mean rows of an expert
+  const int mean_rows = (rows + est_active - 1) / est_active;
+  const int want_cg = std::max(1, std::min(kMaxCG, (2 * mean_rows + 3) / 4));
+  // gate/up: stages = tiles a warp streams (clamped), then the largest cgp that fits
+  p.nst_gu = std::max(Ring<QT>::kMinGateUp, std::min(Ring<QT>::kGateUp, (JT + p.ks - 1) / p.ks));
+  for (;;) {
+    const int ring = kGuWarps * p.nst_gu * 2 * Tr::kTileBytes;
+    const int fit = (kMaxSmem - kBarArea - ring) / x_stage_bytes(d, 1);
+    p.cgp_gu = std::min(want_cg, fit);
+    if (p.cgp_gu >= want_cg || p.nst_gu == Ring<QT>::kMinGateUp) break;
+    --p.nst_gu;
+  }
+  if (p.cgp_gu < 1) return false;
+  p.smem_gu = x_stage_bytes(d, p.cgp_gu) + kBarArea + kGuWarps * p.nst_gu * 2 * Tr::kTileBytes;
+  p.nst_dn = std::max(2, std::min(Ring<QT>::kDown, F / 64));
+  const int ring_dn = kDnWarps * p.nst_dn * Tr::kTileBytes;
+  p.cgp_dn = std::min(want_cg, (kMaxSmem - kBarArea - ring_dn) / x_stage_bytes(F, 1));
+  if (p.cgp_dn < 1) return false;
+  p.smem_dn = x_stage_bytes(F, p.cgp_dn) + kBarArea + ring_dn;
+  p.grid_dn = est_active * ((strips_d + kDnWarps - 1) / kDnWarps);
+  return true;
+}
+
 // Launches the grouped experts with an already-carved workspace.
 template <int QT>
 static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down,
@@ -514,6 +722,19 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
                           const int32_t* x_rows, int x_div, int d, int F, float* y,
                           const int32_t* y_rows, const ExpertsWs& w, cudaStream_t s) {
   using Tr = QTraits<QT>;
+  ExpertsPlan p;
+  MOE_REQUIRE(plan_experts<QT>(rows, E, d, F, p), MOE_ERR_UNSUPPORTED,
+              "d=%d / F=%d too large for the staged activation buffers", d, F);
+  static unsigned long long attr_set = 0;  // per template instance, bit per device
+  int dev = 0;
+  MOE_CUDA(cudaGetDevice(&dev));
+  if (!((attr_set >> (dev & 63)) & 1ull)) {
+    MOE_CUDA(cudaFuncSetAttribute(gateup_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kMaxSmem));
+    MOE_CUDA(cudaFuncSetAttribute(down_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kMaxSmem));
+    attr_set |= 1ull << (dev & 63);
+  }
   const int mg = max_groups(rows, E);
   {
     ::moe::ProfScope _prof(MOE_K_PLAN, s);
@@ -528,27 +749,18 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   }
   MOE_CHECK(check_launch("xprep"));
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
-  const int est_active = rows < E ? rows : E;
-  const int strips_f = F / 16;
-  const int JT = d / 64;
-  const int target = sm_count() * 16;  // resident warps to aim for
-  int ks = 1;
-  while (ks < 8 && (long long)est_active * strips_f * ks < target && JT / (2 * ks) >= 2) ks *= 2;
-  const int spc = 8 / ks;
-  const int gu_grid = est_active * ((strips_f + spc - 1) / spc);
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
-    gateup_kernel<QT><<<gu_grid, 256, 0, s>>>(w_gate, w_up, mat_bytes, d, F, offsets, w.n_active,
-                                             w.active, w.goff, w.row_scale, w.xfrag, w.hfrag, ks,
-                                             w.status);
+    gateup_kernel<QT><<<p.grid_gu, kGuWarps * 32, p.smem_gu, s>>>(
+        w_gate, w_up, mat_bytes, d, F, offsets, w.n_active, w.active, w.goff, w.row_scale,
+        w.xfrag, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.status);
   }
   MOE_CHECK(check_launch("gateup"));
-  const int strips_d = d / 16;
-  const int dn_grid = est_active * ((strips_d + 7) / 8);
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
-    down_kernel<QT><<<dn_grid, 256, 0, s>>>(w_down, mat_bytes, d, F, offsets, w.n_active,
-                                            w.active, w.goff, w.hfrag, y, y_rows);
+    down_kernel<QT><<<p.grid_dn, kDnWarps * 32, p.smem_dn, s>>>(
+        w_down, mat_bytes, d, F, offsets, w.n_active, w.active, w.goff, w.hfrag, y, y_rows,
+        p.cgp_dn, p.nst_dn, w.status);
   }
   return check_launch("down");
 }

@@ -135,7 +135,16 @@ router_select_kernel(const float* __restrict__ part, int nds, const float* __res
     int e = lane + 32 * j;
     float acc = 0.f;
     if (j < J && e < E) {
-      for (int s = 0; s < nds; ++s) acc += part[((size_t)s * T + t) * E + e];
+      // fixed summation order; loads issued eight at a time
+      int s = 0;
+      for (; s + 8 <= nds; s += 8) {
+        float v8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v8[u] = part[((size_t)(s + u) * T + t) * E + e];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += v8[u];
+      }
+      for (; s < nds; ++s) acc += part[((size_t)s * T + t) * E + e];
       if (bias) acc += bias[e];
     }
     v[j] = acc;

@@ -119,9 +119,11 @@ CONFIGS: Dict[str, MoEConfig] = {
 
 
 def zipf_bias(rng: np.random.Generator, n_experts: int, s: float, c: float) -> np.ndarray:
-    """Per-expert logit bias ``c * rank^-s`` over a seeded permutation of experts."""
+    """Per-expert logit bias ``c * log(rank^-s)`` over a seeded permutation of
+    experts: adding the log of Zipf(s) probabilities to the logits skews the
+    routing towards low ranks and starves the tail."""
     ranks = rng.permutation(n_experts).astype(np.float64) + 1.0
-    return (c * ranks ** (-s)).astype(np.float32)
+    return (c * (-s) * np.log(ranks)).astype(np.float32)
 
 
 @dataclasses.dataclass

@@ -111,7 +111,9 @@ def test_prefill_layer_sampled_tokens():
     data = synth.make_layer(synth.CONFIGS["prefill"], 0)
     out, ids, w = run(build_layer(data), data.x)
     counts = np.bincount(ids.reshape(-1), minlength=128)
-    assert counts.max() > 1000 and (counts == 0).any() or counts.min() < 20
+    # Zipf-skewed: the busiest expert takes ~1500 of 32768 rows, the tail a
+    # fraction of the 256-row mean
+    assert counts.max() > 1000 and counts.min() < 128
     assert np.isfinite(out).all()
     rng = np.random.default_rng(0)
     busiest = int(np.argmax(counts))
