@@ -125,6 +125,20 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
                int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
                size_t workspace_bytes, moe_stream_t stream);
 
+/* moe_router without a workspace: no counterpart in the reference.  For callers
+ * that can neither allocate device memory nor let the library allocate (all
+ * device memory already belongs to the caller's own pool, or a fixed memory
+ * footprint is required).  Same inputs, outputs and results as moe_router; its
+ * scratch is a fixed 4 MiB array inside the library (held on every GPU that
+ * loads it), so it rejects with MOE_ERR_WORKSPACE any call needing more than
+ * 1,048,576 partial logits (slices x T x E; e.g. T up to 128 tokens at d=2816,
+ * E=128).  The first call on a device looks up the array's device address;
+ * make it before any stream capture.  Calls share the array: calls that overlap
+ * on the GPU race and must be serialised by the caller.  Allocates nothing. */
+int moe_router_noalloc(const float* x, const float* gate_w, const float* bias, int T, int d,
+                       int E, int k, int layout, int mode, int32_t* ids, float* weights,
+                       moe_stream_t stream);
+
 /* ---- dispatch ------------------------------------------------------------------ */
 
 int moe_dispatch_workspace_bytes(int T, int k, int E, size_t* bytes);

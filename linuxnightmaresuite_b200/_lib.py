@@ -61,6 +61,7 @@ SIGNATURES = {
     "moe_unpack_weights": [vp, vp, ci, ci, ci, ci, vp],
     "moe_router_workspace_bytes": [ci, ci, ci, ctypes.POINTER(csz)],
     "moe_router": [vp, vp, vp, ci, ci, ci, ci, ci, ci, vp, vp, vp, csz, vp],
+    "moe_router_noalloc": [vp, vp, vp, ci, ci, ci, ci, ci, ci, vp, vp, vp],
     "moe_dispatch_workspace_bytes": [ci, ci, ci, ctypes.POINTER(csz)],
     "moe_dispatch": [vp, ci, ci, ci, vp, vp, vp, vp, csz, vp],
     "moe_experts_workspace_bytes": [ci, ci, ci, ci, ctypes.POINTER(csz)],

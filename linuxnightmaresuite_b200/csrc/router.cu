@@ -12,6 +12,8 @@
 // terms, 8-way pairwise at and above) so the denominators follow the reference.
 #include <math.h>
 
+#include <mutex>
+
 #include "moe_common.cuh"
 
 namespace moe {
@@ -306,3 +308,96 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free router.
+//
+// Some callers cannot give this library a workspace: they run where no device
+// allocation may happen at all -- a host program that has already handed every
+// byte of device memory to its own pool, or a serving loop that must keep a
+// fixed memory footprint -- so neither the caller nor the library may call
+// cudaMalloc.  moe_router_noalloc serves them: it takes the same inputs and
+// outputs as moe_router, and keeps its only scratch (the per-slice partial
+// logits, slices x T x E floats) in the fixed array below, which is part of the
+// library image.  Every GPU that loads the library holds these 4 MiB until the
+// process exits.
+//
+// Host code cannot use the array's name as a device address (on the host it
+// names a host-side stand-in), so the address is looked up with
+// cudaGetSymbolAddress once per device, with that device current, on the first
+// call made on that device; make that first call before any stream capture.
+// All calls share the array and it keeps the last call's contents.  Nothing
+// needs clearing: a call writes every partial logit it later reads.  Calls
+// whose kernels overlap on the GPU (different streams, or different host
+// threads) race on the array and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace moe {
+
+constexpr size_t kNoAllocScratchFloats = (size_t)1 << 20;  // 4 MiB of partial logits
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[64] = {nullptr};
+
+static int noalloc_scratch(float** out) {
+  int dev = -1;
+  MOE_CUDA(cudaGetDevice(&dev));
+  MOE_REQUIRE(dev >= 0 && dev < 64, MOE_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    MOE_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    MOE_REQUIRE(p != nullptr, MOE_ERR_CUDA, "no device address for the fixed router scratch");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return MOE_OK;
+}
+
+}  // namespace moe
+
+extern "C" int moe_router_noalloc(const float* x, const float* gate_w, const float* bias, int T,
+                                  int d, int E, int k, int layout, int mode, int32_t* ids,
+                                  float* weights, moe_stream_t stream) {
+  using namespace moe;
+  MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
+  if (T == 0) return MOE_OK;
+  MOE_REQUIRE(x && gate_w && ids && weights, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(d > 0 && E > 0 && k > 0, MOE_ERR_INVALID, "d, E and k must be positive");
+  MOE_REQUIRE(k <= E, MOE_ERR_INVALID, "top_k %d exceeds the expert count %d", k, E);
+  MOE_REQUIRE(k <= kMaxK, MOE_ERR_UNSUPPORTED, "top_k %d above %d", k, kMaxK);
+  MOE_REQUIRE(E % 4 == 0 && E <= kMaxE, MOE_ERR_UNSUPPORTED,
+              "expert count %d must be a multiple of 4 and <= %d", E, kMaxE);
+  MOE_REQUIRE(layout == MOE_ROUTER_D_E || layout == MOE_ROUTER_E_D, MOE_ERR_INVALID,
+              "bad router layout %d", layout);
+  MOE_REQUIRE(mode == MOE_ROUTE_TOPK_SOFTMAX || mode == MOE_ROUTE_SOFTMAX_TOPK_RENORM,
+              MOE_ERR_INVALID, "bad routing mode %d", mode);
+  MOE_REQUIRE(((uintptr_t)gate_w & 15) == 0, MOE_ERR_INVALID, "router weight not 16B aligned");
+  RouterPlan p = router_plan(T, d, E);
+  const size_t need = (size_t)p.nds * T * E;
+  MOE_REQUIRE(need <= kNoAllocScratchFloats, MOE_ERR_WORKSPACE,
+              "moe_router_noalloc: T=%d E=%d needs %zu partial logits (%d slices), above the "
+              "fixed scratch of %zu floats; call moe_router with a workspace instead",
+              T, E, need, p.nds, kNoAllocScratchFloats);
+  float* part = nullptr;
+  MOE_CHECK(noalloc_scratch(&part));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  size_t smem = ((size_t)kRouterDC * E + (size_t)p.tt * (kRouterDC + 1)) * sizeof(float);
+  if (smem > 48 * 1024) {
+    MOE_CUDA(cudaFuncSetAttribute(router_partial_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  }
+  dim3 grid(p.tiles, p.nds);
+  {
+    ::moe::ProfScope _prof(MOE_K_ROUTER_PARTIAL, s);
+    router_partial_kernel<<<grid, p.ct * p.tg, smem, s>>>(x, gate_w, T, d, E, layout, p.tt,
+                                                          p.chunks, part);
+  }
+  MOE_CHECK(check_launch("router_partial"));
+  {
+    ::moe::ProfScope _prof(MOE_K_ROUTER_SELECT, s);
+    router_select_kernel<<<(T + 3) / 4, 128, 0, s>>>(part, p.nds, bias, T, E, k, mode, ids,
+                                                     weights);
+  }
+  return check_launch("router_select");
+}
