@@ -23,15 +23,23 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm
   __syncthreads();
   for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < k; ++q) {
-      int r = rows[q];
-      if (r < 0) continue;
-      float wq = wts[q];
-      float4 v = __ldg(reinterpret_cast<const float4*>(y + (size_t)r * d) + i);
-      acc.x = __fadd_rn(acc.x, __fmul_rn(wq, v.x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(wq, v.y));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(wq, v.z));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(wq, v.w));
+    for (int q0 = 0; q0 < k; q0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {   // loads first, so they overlap
+        const int r = (q0 + u < k) ? rows[q0 + u] : -1;
+        v[u] = r >= 0 ? __ldg(reinterpret_cast<const float4*>(y + (size_t)r * d) + i)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (q0 + u >= k || rows[q0 + u] < 0) continue;
+        const float wq = wts[q0 + u];
+        acc.x = __fadd_rn(acc.x, __fmul_rn(wq, v[u].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(wq, v[u].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(wq, v[u].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(wq, v[u].w));
+      }
     }
     if (shared) {
       float4 v = __ldg(reinterpret_cast<const float4*>(shared + (size_t)t * d) + i);

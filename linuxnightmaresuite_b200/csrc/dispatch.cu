@@ -20,10 +20,12 @@ constexpr int kDispWarps = kDispThreads / 32;
 __global__ void __launch_bounds__(kDispThreads)
 dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restrict__ offsets,
                 int32_t* __restrict__ perm_rows, int32_t* __restrict__ inv_perm,
-                int* __restrict__ status) {
+                int* __restrict__ status, int* __restrict__ n_active, int* __restrict__ active,
+                int* __restrict__ goff, int* __restrict__ gexp, int max_groups) {
   extern __shared__ int sm[];
   int* wcnt = sm;                          // [kDispWarps][E]
   int* etot = sm + kDispWarps * E;         // [E]
+  __shared__ int sh[33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned lt_mask = (1u << lane) - 1u;
   const int chunk = ((P + kDispWarps - 1) / kDispWarps + 31) / 32 * 32;
@@ -62,6 +64,29 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
     etot[e] = run;
   }
   __syncthreads();
+  if (n_active) {
+    // plan of the grouped expert kernels: active experts (ascending), offsets
+    // of 4-row groups, group -> expert map (E <= blockDim.x)
+    const int e = threadIdx.x;
+    const int n = e < E ? etot[e] : 0;
+    const int ng = (n + 3) / 4;
+    int tot_g, tot_a;
+    const int g0 = block_excl_scan(ng, sh, tot_g);
+    const int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
+    const bool overflow = tot_g > max_groups;
+    if (e < E) {
+      goff[e] = g0;
+      if (n > 0) active[a0] = e;
+      if (!overflow)
+        for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
+    }
+    if (e == 0) {
+      goff[E] = tot_g;
+      *n_active = overflow ? 0 : tot_a;
+      if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+    }
+    __syncthreads();
+  }
   // exclusive scan of etot over experts (single warp; E is small)
   if (warp == 0) {
     int carry = 0;
@@ -106,6 +131,27 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
   }
 }
 
+// moe_dispatch that also writes the grouped-expert plan (see plan_kernel).
+int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
+                            int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
+                            int* active, int* goff, int* gexp, int max_groups, cudaStream_t s) {
+  MOE_REQUIRE(E > 0 && E <= kDispThreads, MOE_ERR_UNSUPPORTED, "expert count %d above %d", E,
+              kDispThreads);
+  const int P = T * k;
+  MOE_REQUIRE(P > 0, MOE_ERR_INVALID, "no pairs");
+  size_t smem = sizeof(int) * ((size_t)kDispWarps * E + E);
+  if (smem > 48 * 1024) {
+    MOE_CUDA(cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+  }
+  {
+    ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
+    dispatch_kernel<<<1, kDispThreads, smem, s>>>(ids, P, E, offsets, perm_rows, inv_perm, status,
+                                                  n_active, active, goff, gexp, max_groups);
+  }
+  return check_launch("dispatch");
+}
+
 }  // namespace moe
 
 extern "C" {
@@ -143,7 +189,8 @@ int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offset
   {
     ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
     dispatch_kernel<<<1, kDispThreads, smem, s>>>(ids, (int)P, E, expert_offsets, perm_rows,
-                                                  inv_perm, static_cast<int*>(workspace));
+                                                  inv_perm, static_cast<int*>(workspace), nullptr,
+                                                  nullptr, nullptr, nullptr, 0);
   }
   return check_launch("dispatch");
 }

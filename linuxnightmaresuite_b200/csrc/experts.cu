@@ -61,34 +61,6 @@ __device__ __forceinline__ void frag_pos(int e, int& t, int& i) {
 // ---------------------------------------------------------------------------
 // plan: active experts, group offsets, group -> expert map
 // ---------------------------------------------------------------------------
-__device__ int block_excl_scan(int v, int* sh, int& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    int n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += n;
-  }
-  if (lane == 31) sh[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0;
-    int wi = w;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int n = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += n;
-    }
-    sh[lane] = wi - w;
-    if (lane == 31) sh[32] = wi;
-  }
-  __syncthreads();
-  int res = sh[warp] + incl - v;
-  total = sh[32];
-  __syncthreads();
-  return res;
-}
-
 __global__ void __launch_bounds__(kPlanThreads)
 plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups,
             int* __restrict__ n_active, int* __restrict__ active, int* __restrict__ goff,
@@ -127,9 +99,9 @@ plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups
 template <int QT>
 __global__ void __launch_bounds__(128)
 xprep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
-             const int32_t* __restrict__ offsets, const int* __restrict__ goff,
-             const int* __restrict__ gexp, int E, int d, float* __restrict__ row_scale,
-             uint8_t* __restrict__ xfrag) {
+             const float* __restrict__ x_row_max, const int32_t* __restrict__ offsets,
+             const int* __restrict__ goff, const int* __restrict__ gexp, int E, int d,
+             float* __restrict__ row_scale, uint8_t* __restrict__ xfrag) {
   const int G = blockIdx.x;
   if (G >= goff[E]) return;
   const int e = gexp[G];
@@ -150,12 +122,16 @@ xprep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, in
   const int src_row = x_rows ? x_rows[r] / x_div : r;
   const float4* src = reinterpret_cast<const float4*>(x + (size_t)src_row * d);
   float m = 0.f;
-  for (int i = lane; i < d / 4; i += 32) {
-    float4 v = __ldg(src + i);
-    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-  }
+  if (x_row_max) {
+    m = x_row_max[src_row];
+  } else {
+    for (int i = lane; i < d / 4; i += 32) {
+      float4 v = __ldg(src + i);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  }
   float scale = 1.f, inv = 1.f;
   if (m > 0.f && isfinite(m)) {
     int ex = ilogbf(m);
@@ -256,76 +232,214 @@ __device__ __forceinline__ void block_mma(float2 (&acc)[2], const uint32_t (&a0)
   acc[1] = __ffma2_rn(dg8, make_float2(tmp[2], tmp[3]), acc[1]);
 }
 
-// Stages per warp of the bulk-copy rings (max / min); the split-K reduction
-// buffer (4 KB per warp) aliases a gate/up ring, so kMinGateUp * 2 tiles >= 4 KB.
+// Bulk-copy ring geometry: U tiles (of each matrix) per stage, stages per warp.
+// The split-K reduction buffer (NCG KB per warp) aliases a gate/up ring.
 template <int QT> struct Ring;
-template <> struct Ring<MOE_Q4_0> { static constexpr int kGateUp = 8, kMinGateUp = 4, kDown = 12; };
-template <> struct Ring<MOE_Q8_0> { static constexpr int kGateUp = 6, kMinGateUp = 2, kDown = 8; };
+template <> struct Ring<MOE_Q4_0> {
+  static constexpr int kGuU = 2, kGuStages = 3, kDnU = 4, kDnStages = 3;
+};
+template <> struct Ring<MOE_Q8_0> {
+  static constexpr int kGuU = 2, kGuStages = 2, kDnU = 2, kDnStages = 3;
+};
 
 constexpr int kGuWarps = 16;            // warps per gate/up CTA
+constexpr int kGuMaxCG = 2;             // column groups per pass of either GEMV (registers)
 constexpr int kDnWarps = 8;             // warps per down CTA
-constexpr int kBarArea = 2048;          // mbarriers: 1 + warps x stages, 8 B each
+constexpr int kBarArea = 1024;          // mbarriers: 1 + warps x stages, 8 B each
 constexpr int kMaxSmem = 227 * 1024;    // dynamic shared memory per CTA on sm_100
 __host__ __device__ inline int x_stage_bytes(int K, int cgp) { return cgp * (K / 32) * 512; }
 
-// ---------------------------------------------------------------------------
-// gate/up streaming for one chunk of NCG column groups.  Lane 0 keeps up to
-// nst (gate, up) tile pairs in flight with bulk copies into the warp's ring;
-// every lane reads its fragments from shared memory, releases the stage and
-// computes.  Returns false if a wait timed out.
-// ---------------------------------------------------------------------------
+template <int QT>
+__host__ __device__ constexpr int gu_stage_bytes() {
+  return 2 * Ring<QT>::kGuU * QTraits<QT>::kTileBytes;
+}
+template <int QT>
+__host__ __device__ constexpr int dn_stage_bytes() {
+  return Ring<QT>::kDnU * QTraits<QT>::kTileBytes;
+}
+
+// Per-CTA state of a gate/up work item.
+struct GuCtx {
+  const uint8_t* gbase;   // this warp's strip of W_gate (tile 0)
+  const uint8_t* ubase;   // ... of W_up
+  uint8_t* ring;          // this warp's stages
+  uint64_t* bars;         // this warp's stage barriers
+  uint64_t* xbar;         // activation-stage barrier
+  const uint8_t* xs;      // activation fragments (shared)
+  uint8_t* hfrag;
+  const float* row_scale;
+  int* status;
+  uint64_t pol;
+  int nst, jb, ntile, nbx, nbF, ks, kp, s, row0, n, G0, lane;
+  bool strip_ok;
+};
+
+// Streams this warp's tiles through its ring for one chunk of NCG column
+// groups.  Lane 0 keeps up to nst stages of U (gate, up) tile pairs in flight
+// with bulk copies; every lane reads its fragments of a whole stage from shared
+// memory, releases the stage, then computes.  False if a wait timed out.
 template <int QT, int NCG>
-__device__ __forceinline__ bool gu_stream(float2 (&accg)[kMaxCG][2], float2 (&accu)[kMaxCG][2],
-                                          uint8_t* ring, uint64_t* bars, uint32_t& parity,
-                                          int nst, int ntile, int jb, const uint8_t* gbase,
-                                          const uint8_t* ubase, uint64_t pol,
-                                          const uint8_t* xs_lane, int cg_stride, uint64_t* xbar,
-                                          uint32_t xparity, int lane) {
+__device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)[NCG][2],
+                                          const GuCtx& c, uint32_t& parity, uint32_t xparity) {
   using Tr = QTraits<QT>;
+  constexpr int U = Ring<QT>::kGuU;
   constexpr int TB = Tr::kTileBytes;
-  constexpr int STAGE = 2 * TB;
-  if (lane == 0) {
+  constexpr int SB = U * TB;
+  constexpr int STAGE = 2 * SB;
+  const int nstage = (c.ntile + U - 1) / U;
+  auto issue = [&](int q, int slot) {
+    const int t0 = q * U;
+    const uint32_t bytes = (uint32_t)(min(U, c.ntile - t0) * TB);
+    uint8_t* st = c.ring + slot * STAGE;
+    mbar_expect_tx(&c.bars[slot], 2 * bytes);
+    bulk_g2s(st, c.gbase + (size_t)(c.jb + t0) * TB, bytes, &c.bars[slot], c.pol);
+    bulk_g2s(st + SB, c.ubase + (size_t)(c.jb + t0) * TB, bytes, &c.bars[slot], c.pol);
+  };
+  if (c.lane == 0) {
     fence_proxy_async_smem();
-    for (int i = 0; i < min(nst, ntile); ++i) {
-      mbar_expect_tx(&bars[i], STAGE);
-      bulk_g2s(ring + i * STAGE, gbase + (size_t)(jb + i) * TB, TB, &bars[i], pol);
-      bulk_g2s(ring + i * STAGE + TB, ubase + (size_t)(jb + i) * TB, TB, &bars[i], pol);
-    }
+    for (int q = 0; q < min(c.nst, nstage); ++q) issue(q, q);
   }
-  if (!mbar_wait(xbar, xparity)) return false;
-  int st = 0;
-  for (int i = 0; i < ntile; ++i) {
-    if (!mbar_wait(&bars[st], (parity >> st) & 1u)) return false;
-    parity ^= 1u << st;
-    TileRegs<QT> tg, tu;
-    uint8_t* stage = ring + st * STAGE;
-    lds_tile<QT>(tg, stage, lane);
-    lds_tile<QT>(tu, stage + TB, lane);
-    __syncwarp();
-    if (lane == 0 && i + nst < ntile) {
-      const int j = jb + i + nst;
-      fence_proxy_async_smem();
-      mbar_expect_tx(&bars[st], STAGE);
-      bulk_g2s(stage, gbase + (size_t)j * TB, TB, &bars[st], pol);
-      bulk_g2s(stage + TB, ubase + (size_t)j * TB, TB, &bars[st], pol);
+  if (!mbar_wait(c.xbar, xparity)) return false;
+  const int cs = c.nbx * 512;
+  const uint8_t* xq = c.xs + c.lane * 16 + c.jb * 1024;
+  int slot = 0;
+  for (int q = 0; q < nstage; ++q) {
+    if (!mbar_wait(&c.bars[slot], (parity >> slot) & 1u)) return false;
+    parity ^= 1u << slot;
+    const int nt = min(U, c.ntile - q * U);
+    const uint8_t* st = c.ring + slot * STAGE;
+    TileRegs<QT> tg[U], tu[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (u < nt) {
+        lds_tile<QT>(tg[u], st + u * TB, c.lane);
+        lds_tile<QT>(tu[u], st + SB + u * TB, c.lane);
+      }
     }
-    st = (st + 1 == nst) ? 0 : st + 1;
-    const uint8_t* xj = xs_lane + (jb + i) * 1024;
+    __syncwarp();
+    if (c.lane == 0 && q + c.nst < nstage) {
+      fence_proxy_async_smem();
+      issue(q + c.nst, slot);
+    }
+    slot = (slot + 1 == c.nst) ? 0 : slot + 1;
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      uint32_t ga0[4], ga1[4], ua0[4], ua1[4];
-      float2 dg, dg8, du, du8;
-      tile_afrags<QT>(tg, b, ga0, ga1, dg, dg8);
-      tile_afrags<QT>(tu, b, ua0, ua1, du, du8);
+    for (int u = 0; u < U; ++u) {
+      if (u < nt) {
 #pragma unroll
-      for (int c = 0; c < NCG; ++c) {
-        const uint4 xf = *reinterpret_cast<const uint4*>(xj + c * cg_stride + b * 512);
-        block_mma(accg[c], ga0, ga1, xf, dg, dg8);
-        block_mma(accu[c], ua0, ua1, xf, du, du8);
+        for (int b = 0; b < 2; ++b) {
+          uint32_t ga0[4], ga1[4], ua0[4], ua1[4];
+          float2 dg, dg8, du, du8;
+          tile_afrags<QT>(tg[u], b, ga0, ga1, dg, dg8);
+          tile_afrags<QT>(tu[u], b, ua0, ua1, du, du8);
+#pragma unroll
+          for (int cg = 0; cg < NCG; ++cg) {
+            const uint4 xf = *reinterpret_cast<const uint4*>(xq + cg * cs + u * 1024 + b * 512);
+            block_mma(accg[cg], ga0, ga1, xf, dg, dg8);
+            block_mma(accu[cg], ua0, ua1, xf, du, du8);
+          }
+        }
+      }
+    }
+    xq += U * 1024;
+  }
+  return true;
+}
+
+// One chunk of NCG column groups: stream, split-K reduction across the
+// warps of a strip (rank order), SiLU(gate) * up epilogue into hidden
+// fragments.  Called uniformly by every warp of the CTA.
+template <int QT, int NCG>
+__device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, uint32_t xparity,
+                                         int c0, bool ok) {
+  float2 accg[NCG][2], accu[NCG][2];
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) accg[cg][i] = accu[cg][i] = make_float2(0.f, 0.f);
+  if (c.strip_ok && ok) {
+    if (!gu_stream<QT, NCG>(accg, accu, c, parity, xparity)) {
+      set_status(c.status, MOE_STATUS_TIMEOUT);
+      ok = false;
+    }
+  } else if (!mbar_wait(c.xbar, xparity)) {
+    set_status(c.status, MOE_STATUS_TIMEOUT);
+    ok = false;
+  }
+  const int lane = c.lane;
+  if (c.ks > 1) {
+    // partial sums of the K-slices meet in the (now idle) rings
+    float* red = reinterpret_cast<float*>(c.ring);
+    constexpr int RING = Ring<QT>::kGuStages * gu_stage_bytes<QT>();
+    (void)RING;
+    __syncthreads();
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        red[(cg * 8 + 2 * i) * 32 + lane] = accg[cg][i].x;
+        red[(cg * 8 + 2 * i + 1) * 32 + lane] = accg[cg][i].y;
+        red[(cg * 8 + 4 + 2 * i) * 32 + lane] = accu[cg][i].x;
+        red[(cg * 8 + 5 + 2 * i) * 32 + lane] = accu[cg][i].y;
+      }
+    __syncthreads();
+    if (c.kp == 0) {
+      for (int q = 1; q < c.ks; ++q) {
+        const float* rq = reinterpret_cast<const float*>(c.ring + q * c.nst * gu_stage_bytes<QT>());
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            accg[cg][i].x += rq[(cg * 8 + 2 * i) * 32 + lane];
+            accg[cg][i].y += rq[(cg * 8 + 2 * i + 1) * 32 + lane];
+            accu[cg][i].x += rq[(cg * 8 + 4 + 2 * i) * 32 + lane];
+            accu[cg][i].y += rq[(cg * 8 + 5 + 2 * i) * 32 + lane];
+          }
       }
     }
   }
-  return true;
+  if (c.kp == 0 && c.strip_ok) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        accg[cg][i].x += __shfl_xor_sync(0xffffffffu, accg[cg][i].x, 2);
+        accg[cg][i].y += __shfl_xor_sync(0xffffffffu, accg[cg][i].y, 2);
+        accu[cg][i].x += __shfl_xor_sync(0xffffffffu, accu[cg][i].x, 2);
+        accu[cg][i].y += __shfl_xor_sync(0xffffffffu, accu[cg][i].y, 2);
+      }
+    if (t < 2) {
+#pragma unroll
+      for (int cg = 0; cg < NCG; ++cg) {
+        const int G = c.G0 + c0 / 4 + cg;
+#pragma unroll
+        for (int ci = 0; ci < 2; ++ci) {
+          const int rig = 2 * t + ci;              // row inside the group
+          const int tok = c0 + 4 * cg + rig;
+          if (tok >= c.n) continue;
+          const float rs = c.row_scale[c.row0 + tok];
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const float gacc = ci ? accg[cg][rr].y : accg[cg][rr].x;
+            const float uacc = ci ? accu[cg][rr].y : accu[cg][rr].x;
+            const float h = silu_f(gacc * rs) * (uacc * rs);
+            const float hsc = h * kHScale;
+            if (!(fabsf(hsc) <= 65504.f)) set_status(c.status, MOE_STATUS_ROW_OVERFLOW);
+            const __half hh = __float2half_rn(hsc);
+            const __half hl = __float2half_rn(hsc - __half2float(hh));
+            const int f = c.s * 16 + g + 8 * rr;
+            int tf, fi;
+            frag_pos<QT>(f & 31, tf, fi);
+            uint8_t* dst =
+                c.hfrag + ((size_t)G * c.nbF + (f >> 5)) * 512 + rig * 64 + tf * 16 + fi * 2;
+            *reinterpret_cast<__half*>(dst) = hh;
+            *reinterpret_cast<__half*>(dst + 256) = hl;
+          }
+        }
+      }
+    }
+  }
+  return ok;
 }
 
 // ---------------------------------------------------------------------------
@@ -342,204 +456,183 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
               uint8_t* __restrict__ hfrag, int ks, int cgp, int nst, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
-  constexpr int STAGE = 2 * TB;
-  constexpr int SMAX = Ring<QT>::kGateUp;
+  constexpr int SMAX = Ring<QT>::kGuStages;
   static_assert((kGuWarps * SMAX + 1) * 8 <= kBarArea, "barrier area");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int xbytes = x_stage_bytes(d, cgp);
-  uint8_t* xs = smem;
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
-  uint64_t* bars = xbar + 1 + warp * SMAX;
-  uint8_t* ring = smem + xbytes + kBarArea + warp * nst * STAGE;
-  const int g = lane >> 2, t = lane & 3;
+  GuCtx c;
+  c.xs = smem;
+  c.xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
+  c.bars = c.xbar + 1 + warp * SMAX;
+  c.ring = smem + xbytes + kBarArea + warp * nst * gu_stage_bytes<QT>();
   const int spc = kGuWarps / ks;
   const int strips = F / 16;
   const int cpe = (strips + spc - 1) / spc;
   const int a = blockIdx.x / cpe;
   if (a >= *n_active) return;
   const int e = active[a];
-  const int sl = warp / ks, kp = warp % ks;
-  const int s = (blockIdx.x % cpe) * spc + sl;
-  const bool strip_ok = s < strips;
+  c.ks = ks;
+  c.kp = warp % ks;
+  c.s = (blockIdx.x % cpe) * spc + warp / ks;
+  c.strip_ok = c.s < strips;
   const int JT = d / 64;
-  const int jb = kp * JT / ks, je = (kp + 1) * JT / ks;
-  const int row0 = offsets[e];
-  const int n = offsets[e + 1] - row0;
-  const int G0 = goff[e];
-  const int nbx = d / 32, nbF = F / 32;
-  const uint8_t* gbase = wg + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * TB;
-  const uint8_t* ubase = wu + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * TB;
-  const uint64_t pol = evict_first_policy();
+  c.jb = c.kp * JT / ks;
+  c.ntile = (c.kp + 1) * JT / ks - c.jb;
+  c.row0 = offsets[e];
+  c.n = offsets[e + 1] - c.row0;
+  c.G0 = goff[e];
+  c.nbx = d / 32;
+  c.nbF = F / 32;
+  c.nst = nst;
+  c.lane = lane;
+  c.hfrag = hfrag;
+  c.row_scale = row_scale;
+  c.status = status;
+  c.gbase = wg + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
+  c.ubase = wu + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
+  c.pol = evict_first_policy();
   if (lane == 0) {
-    for (int i = 0; i < nst; ++i) mbar_init(&bars[i], 1);
-    if (warp == 0) mbar_init(xbar, 1);
+    for (int i = 0; i < nst; ++i) mbar_init(&c.bars[i], 1);
+    if (warp == 0) mbar_init(c.xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
   uint32_t parity = 0u, xparity = 0u;
   bool ok = true;
-
-  for (int c0 = 0; c0 < n; c0 += 4 * cgp) {
-    const int ncg = min(cgp, (n - c0 + 3) / 4);
-    float2 accg[kMaxCG][2], accu[kMaxCG][2];
-#pragma unroll
-    for (int c = 0; c < kMaxCG; ++c)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) accg[c][i] = accu[c][i] = make_float2(0.f, 0.f);
+  for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
+    const int ncg = min(cgp, (c.n - c0 + 3) / 4);
     if (threadIdx.x == 0) {
-      const uint32_t xb = (uint32_t)(ncg * nbx * 512);
+      const uint32_t xb = (uint32_t)(ncg * c.nbx * 512);
       fence_proxy_async_smem();
-      mbar_expect_tx(xbar, xb);
-      bulk_g2s_plain(xs, xfrag + (size_t)(G0 + c0 / 4) * nbx * 512, xb, xbar);
+      mbar_expect_tx(c.xbar, xb);
+      bulk_g2s_plain(smem, xfrag + (size_t)(c.G0 + c0 / 4) * c.nbx * 512, xb, c.xbar);
     }
-    if (strip_ok && ok) {
-      const uint8_t* xl = xs + lane * 16;
-      const int cs = nbx * 512;
-      bool r;
-      switch (ncg) {
-        case 1: r = gu_stream<QT, 1>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
-        case 2: r = gu_stream<QT, 2>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
-        case 3: r = gu_stream<QT, 3>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
-        default: r = gu_stream<QT, 4>(accg, accu, ring, bars, parity, nst, je - jb, jb, gbase, ubase, pol, xl, cs, xbar, xparity, lane); break;
-      }
-      if (!r) {
-        set_status(status, MOE_STATUS_TIMEOUT);
-        ok = false;
-      }
-    } else if (!mbar_wait(xbar, xparity)) {
-      set_status(status, MOE_STATUS_TIMEOUT);
-      ok = false;
-    }
+    if (ncg == 1) ok = gu_chunk<QT, 1>(c, parity, xparity, c0, ok);
+    else ok = gu_chunk<QT, 2>(c, parity, xparity, c0, ok);
     xparity ^= 1u;
-    if (ks > 1) {
-      // partial sums of the K-slices meet in the (now idle) rings
-      float* red = reinterpret_cast<float*>(ring);
-      __syncthreads();
-#pragma unroll
-      for (int c = 0; c < kMaxCG; ++c)
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          red[(c * 8 + 2 * i) * 32 + lane] = accg[c][i].x;
-          red[(c * 8 + 2 * i + 1) * 32 + lane] = accg[c][i].y;
-          red[(c * 8 + 4 + 2 * i) * 32 + lane] = accu[c][i].x;
-          red[(c * 8 + 5 + 2 * i) * 32 + lane] = accu[c][i].y;
-        }
-      __syncthreads();
-      if (kp == 0) {
-        for (int q = 1; q < ks; ++q) {
-          const float* rq = reinterpret_cast<const float*>(ring + q * nst * STAGE);
-#pragma unroll
-          for (int c = 0; c < kMaxCG; ++c)
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              accg[c][i].x += rq[(c * 8 + 2 * i) * 32 + lane];
-              accg[c][i].y += rq[(c * 8 + 2 * i + 1) * 32 + lane];
-              accu[c][i].x += rq[(c * 8 + 4 + 2 * i) * 32 + lane];
-              accu[c][i].y += rq[(c * 8 + 5 + 2 * i) * 32 + lane];
-            }
-        }
-      }
-    }
-    if (kp == 0 && strip_ok) {
-#pragma unroll
-      for (int c = 0; c < kMaxCG; ++c)
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          accg[c][i].x += __shfl_xor_sync(0xffffffffu, accg[c][i].x, 2);
-          accg[c][i].y += __shfl_xor_sync(0xffffffffu, accg[c][i].y, 2);
-          accu[c][i].x += __shfl_xor_sync(0xffffffffu, accu[c][i].x, 2);
-          accu[c][i].y += __shfl_xor_sync(0xffffffffu, accu[c][i].y, 2);
-        }
-      if (t < 2) {
-#pragma unroll
-        for (int c = 0; c < kMaxCG; ++c) {
-          if (c >= ncg) continue;
-          const int G = G0 + c0 / 4 + c;
-#pragma unroll
-          for (int ci = 0; ci < 2; ++ci) {
-            const int rig = 2 * t + ci;              // row inside the group
-            const int tok = c0 + 4 * c + rig;
-            if (tok >= n) continue;
-            const float rs = row_scale[row0 + tok];
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-              const float gacc = ci ? accg[c][rr].y : accg[c][rr].x;
-              const float uacc = ci ? accu[c][rr].y : accu[c][rr].x;
-              const float h = silu_f(gacc * rs) * (uacc * rs);
-              const float hsc = h * kHScale;
-              if (!(fabsf(hsc) <= 65504.f)) set_status(status, MOE_STATUS_ROW_OVERFLOW);
-              const __half hh = __float2half_rn(hsc);
-              const __half hl = __float2half_rn(hsc - __half2float(hh));
-              const int f = s * 16 + g + 8 * rr;
-              int tf, fi;
-              frag_pos<QT>(f & 31, tf, fi);
-              uint8_t* dst = hfrag + ((size_t)G * nbF + (f >> 5)) * 512 + rig * 64 + tf * 16 + fi * 2;
-              *reinterpret_cast<__half*>(dst) = hh;
-              *reinterpret_cast<__half*>(dst + 256) = hl;
-            }
-          }
-        }
-      }
-    }
     __syncthreads();  // x stage and rings are rewritten by the next chunk
   }
 }
 
 // ---------------------------------------------------------------------------
-// down streaming for one chunk of NCG column groups (one tile per stage)
+// down: CTA = 8 warps = 8 strips of 16 d-rows of one expert; K = F is short.
 // ---------------------------------------------------------------------------
+struct DnCtx {
+  const uint8_t* base;
+  uint8_t* ring;
+  uint64_t* bars;
+  uint64_t* xbar;
+  const uint8_t* hs;
+  float* y;
+  const int32_t* y_rows;
+  int* status;
+  uint64_t pol;
+  int nst, JT, nbF, s, d, row0, n, lane;
+  bool strip_ok;
+};
+
 template <int QT, int NCG>
-__device__ __forceinline__ bool dn_stream(float2 (&acc)[kMaxCG][2], uint8_t* ring,
-                                          uint64_t* bars, uint32_t& parity, int nst, int JT,
-                                          const uint8_t* base, uint64_t pol,
-                                          const uint8_t* hs_lane, int cg_stride, uint64_t* xbar,
-                                          uint32_t xparity, int lane) {
+__device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
+                                          uint32_t& parity, uint32_t xparity) {
   using Tr = QTraits<QT>;
+  constexpr int U = Ring<QT>::kDnU;
   constexpr int TB = Tr::kTileBytes;
-  if (lane == 0) {
+  constexpr int STAGE = U * TB;
+  const int nstage = (c.JT + U - 1) / U;
+  auto issue = [&](int q, int slot) {
+    const int t0 = q * U;
+    const uint32_t bytes = (uint32_t)(min(U, c.JT - t0) * TB);
+    mbar_expect_tx(&c.bars[slot], bytes);
+    bulk_g2s(c.ring + slot * STAGE, c.base + (size_t)t0 * TB, bytes, &c.bars[slot], c.pol);
+  };
+  if (c.lane == 0) {
     fence_proxy_async_smem();
-    for (int j = 0; j < min(nst, JT); ++j) {
-      mbar_expect_tx(&bars[j], TB);
-      bulk_g2s(ring + j * TB, base + (size_t)j * TB, TB, &bars[j], pol);
-    }
+    for (int q = 0; q < min(c.nst, nstage); ++q) issue(q, q);
   }
-  if (!mbar_wait(xbar, xparity)) return false;
-  int st = 0;
-  for (int j = 0; j < JT; ++j) {
-    if (!mbar_wait(&bars[st], (parity >> st) & 1u)) return false;
-    parity ^= 1u << st;
-    TileRegs<QT> tw;
-    uint8_t* stage = ring + st * TB;
-    lds_tile<QT>(tw, stage, lane);
+  if (!mbar_wait(c.xbar, xparity)) return false;
+  const int cs = c.nbF * 512;
+  const uint8_t* xq = c.hs + c.lane * 16;
+  int slot = 0;
+  for (int q = 0; q < nstage; ++q) {
+    if (!mbar_wait(&c.bars[slot], (parity >> slot) & 1u)) return false;
+    parity ^= 1u << slot;
+    const int nt = min(U, c.JT - q * U);
+    const uint8_t* st = c.ring + slot * STAGE;
+    TileRegs<QT> tw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (u < nt) lds_tile<QT>(tw[u], st + u * TB, c.lane);
     __syncwarp();
-    if (lane == 0 && j + nst < JT) {
+    if (c.lane == 0 && q + c.nst < nstage) {
       fence_proxy_async_smem();
-      mbar_expect_tx(&bars[st], TB);
-      bulk_g2s(stage, base + (size_t)(j + nst) * TB, TB, &bars[st], pol);
+      issue(q + c.nst, slot);
     }
-    st = (st + 1 == nst) ? 0 : st + 1;
-    const uint8_t* xj = hs_lane + j * 1024;
+    slot = (slot + 1 == c.nst) ? 0 : slot + 1;
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      uint32_t a0[4], a1[4];
-      float2 dw, dw8;
-      tile_afrags<QT>(tw, b, a0, a1, dw, dw8);
+    for (int u = 0; u < U; ++u) {
+      if (u < nt) {
 #pragma unroll
-      for (int c = 0; c < NCG; ++c) {
-        const uint4 xf = *reinterpret_cast<const uint4*>(xj + c * cg_stride + b * 512);
-        block_mma(acc[c], a0, a1, xf, dw, dw8);
+        for (int b = 0; b < 2; ++b) {
+          uint32_t a0[4], a1[4];
+          float2 dw, dw8;
+          tile_afrags<QT>(tw[u], b, a0, a1, dw, dw8);
+#pragma unroll
+          for (int cg = 0; cg < NCG; ++cg) {
+            const uint4 xf = *reinterpret_cast<const uint4*>(xq + cg * cs + u * 1024 + b * 512);
+            block_mma(acc[cg], a0, a1, xf, dw, dw8);
+          }
+        }
       }
     }
+    xq += U * 1024;
   }
   return true;
 }
 
-// ---------------------------------------------------------------------------
-// down: CTA = 8 warps = 8 strips of 16 d-rows of one expert; K = F is short.
-// ---------------------------------------------------------------------------
+template <int QT, int NCG>
+__device__ __forceinline__ bool dn_chunk(const DnCtx& c, uint32_t& parity, uint32_t xparity,
+                                         int c0, bool ok) {
+  float2 acc[NCG][2];
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = make_float2(0.f, 0.f);
+  if (c.strip_ok && ok) {
+    if (!dn_stream<QT, NCG>(acc, c, parity, xparity)) {
+      set_status(c.status, MOE_STATUS_TIMEOUT);
+      ok = false;
+    }
+  } else if (!mbar_wait(c.xbar, xparity)) {
+    set_status(c.status, MOE_STATUS_TIMEOUT);
+    ok = false;
+  }
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      acc[cg][i].x += __shfl_xor_sync(0xffffffffu, acc[cg][i].x, 2);
+      acc[cg][i].y += __shfl_xor_sync(0xffffffffu, acc[cg][i].y, 2);
+    }
+  const int g = c.lane >> 2, t = c.lane & 3;
+  if (t < 2 && c.strip_ok) {
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg) {
+#pragma unroll
+      for (int ci = 0; ci < 2; ++ci) {
+        const int tok = c0 + 4 * cg + 2 * t + ci;
+        if (tok >= c.n) continue;
+        const int r = c.row0 + tok;
+        const int orow = c.y_rows ? c.y_rows[r] : r;
+        float* yr = c.y + (size_t)orow * c.d + c.s * 16 + g;
+        yr[0] = (ci ? acc[cg][0].y : acc[cg][0].x) * (1.0f / kHScale);
+        yr[8] = (ci ? acc[cg][1].y : acc[cg][1].x) * (1.0f / kHScale);
+      }
+    }
+  }
+  return ok;
+}
+
 template <int QT>
-__global__ void __launch_bounds__(kDnWarps * 32, 3)
+__global__ void __launch_bounds__(kDnWarps * 32, 2)
 down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
             const int* __restrict__ active, const int* __restrict__ goff,
@@ -547,91 +640,55 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ y_rows, int cgp, int nst, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
-  constexpr int SMAX = Ring<QT>::kDown;
+  constexpr int SMAX = Ring<QT>::kDnStages;
   static_assert((kDnWarps * SMAX + 1) * 8 <= kBarArea, "barrier area");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int xbytes = x_stage_bytes(F, cgp);
-  uint8_t* hs = smem;
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
-  uint64_t* bars = xbar + 1 + warp * SMAX;
-  uint8_t* ring = smem + xbytes + kBarArea + warp * nst * TB;
-  const int g = lane >> 2, t = lane & 3;
+  DnCtx c;
+  c.hs = smem;
+  c.xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
+  c.bars = c.xbar + 1 + warp * SMAX;
+  c.ring = smem + xbytes + kBarArea + warp * nst * dn_stage_bytes<QT>();
   const int strips = d / 16;
   const int cpe = (strips + kDnWarps - 1) / kDnWarps;
   const int a = blockIdx.x / cpe;
   if (a >= *n_active) return;
-  const int s = (blockIdx.x % cpe) * kDnWarps + warp;
-  const bool strip_ok = s < strips;
+  c.s = (blockIdx.x % cpe) * kDnWarps + warp;
+  c.strip_ok = c.s < strips;
   const int e = active[a];
-  const int JT = F / 64;
-  const int row0 = offsets[e];
-  const int n = offsets[e + 1] - row0;
+  c.JT = F / 64;
+  c.row0 = offsets[e];
+  c.n = offsets[e + 1] - c.row0;
   const int G0 = goff[e];
-  const int nbF = F / 32;
-  const uint8_t* base = wd + (size_t)e * mat_bytes + (size_t)(strip_ok ? s : 0) * JT * TB;
-  const uint64_t pol = evict_first_policy();
+  c.nbF = F / 32;
+  c.d = d;
+  c.nst = nst;
+  c.lane = lane;
+  c.y = y;
+  c.y_rows = y_rows;
+  c.status = status;
+  c.base = wd + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * c.JT * TB;
+  c.pol = evict_first_policy();
   if (lane == 0) {
-    for (int i = 0; i < nst; ++i) mbar_init(&bars[i], 1);
-    if (warp == 0) mbar_init(xbar, 1);
+    for (int i = 0; i < nst; ++i) mbar_init(&c.bars[i], 1);
+    if (warp == 0) mbar_init(c.xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
   uint32_t parity = 0u, xparity = 0u;
   bool ok = true;
-  for (int c0 = 0; c0 < n; c0 += 4 * cgp) {
-    const int ncg = min(cgp, (n - c0 + 3) / 4);
-    float2 acc[kMaxCG][2];
-#pragma unroll
-    for (int c = 0; c < kMaxCG; ++c) acc[c][0] = acc[c][1] = make_float2(0.f, 0.f);
+  for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
+    const int ncg = min(cgp, (c.n - c0 + 3) / 4);
     if (threadIdx.x == 0) {
-      const uint32_t hb = (uint32_t)(ncg * nbF * 512);
+      const uint32_t hb = (uint32_t)(ncg * c.nbF * 512);
       fence_proxy_async_smem();
-      mbar_expect_tx(xbar, hb);
-      bulk_g2s_plain(hs, hfrag + (size_t)(G0 + c0 / 4) * nbF * 512, hb, xbar);
+      mbar_expect_tx(c.xbar, hb);
+      bulk_g2s_plain(smem, hfrag + (size_t)(G0 + c0 / 4) * c.nbF * 512, hb, c.xbar);
     }
-    if (strip_ok && ok) {
-      const uint8_t* hl = hs + lane * 16;
-      const int cs = nbF * 512;
-      bool r;
-      switch (ncg) {
-        case 1: r = dn_stream<QT, 1>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
-        case 2: r = dn_stream<QT, 2>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
-        case 3: r = dn_stream<QT, 3>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
-        default: r = dn_stream<QT, 4>(acc, ring, bars, parity, nst, JT, base, pol, hl, cs, xbar, xparity, lane); break;
-      }
-      if (!r) {
-        set_status(status, MOE_STATUS_TIMEOUT);
-        ok = false;
-      }
-    } else if (!mbar_wait(xbar, xparity)) {
-      set_status(status, MOE_STATUS_TIMEOUT);
-      ok = false;
-    }
+    if (ncg == 1) ok = dn_chunk<QT, 1>(c, parity, xparity, c0, ok);
+    else ok = dn_chunk<QT, 2>(c, parity, xparity, c0, ok);
     xparity ^= 1u;
-#pragma unroll
-    for (int c = 0; c < kMaxCG; ++c)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        acc[c][i].x += __shfl_xor_sync(0xffffffffu, acc[c][i].x, 2);
-        acc[c][i].y += __shfl_xor_sync(0xffffffffu, acc[c][i].y, 2);
-      }
-    if (t < 2 && strip_ok) {
-#pragma unroll
-      for (int c = 0; c < kMaxCG; ++c) {
-        if (c >= ncg) continue;
-#pragma unroll
-        for (int ci = 0; ci < 2; ++ci) {
-          const int tok = c0 + 4 * c + 2 * t + ci;
-          if (tok >= n) continue;
-          const int r = row0 + tok;
-          const int orow = y_rows ? y_rows[r] : r;
-          float* yr = y + (size_t)orow * d + s * 16 + g;
-          yr[0] = (ci ? acc[c][0].y : acc[c][0].x) * (1.0f / kHScale);
-          yr[8] = (ci ? acc[c][1].y : acc[c][1].x) * (1.0f / kHScale);
-        }
-      }
-    }
     __syncthreads();  // the staged hidden fragments are rewritten by the next chunk
   }
 }
@@ -682,7 +739,6 @@ struct ExpertsPlan {
 
 template <int QT>
 static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
-  using Tr = QTraits<QT>;
   const int est_active = rows < E ? rows : E;
   const int strips_f = F / 16, strips_d = d / 16;
   const int JT = d / 64;
@@ -695,20 +751,25 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   // column groups per pass: about twice the mean rows of an expert
   const int mean_rows = (rows + est_active - 1) / est_active;
   const int want_cg = std::max(1, std::min(kMaxCG, (2 * mean_rows + 3) / 4));
-  // gate/up: stages = tiles a warp streams (clamped), then the largest cgp that fits
-  p.nst_gu = std::max(Ring<QT>::kMinGateUp, std::min(Ring<QT>::kGateUp, (JT + p.ks - 1) / p.ks));
+  // gate/up: stages for the tiles a warp streams (clamped), then the largest
+  // column-group count that fits; fewer stages before fewer groups
+  const int gu_u = Ring<QT>::kGuU;
+  p.nst_gu = std::max(1, std::min(Ring<QT>::kGuStages, ((JT + p.ks - 1) / p.ks + gu_u - 1) / gu_u));
   for (;;) {
-    const int ring = kGuWarps * p.nst_gu * 2 * Tr::kTileBytes;
+    const int ring = kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
     const int fit = (kMaxSmem - kBarArea - ring) / x_stage_bytes(d, 1);
-    p.cgp_gu = std::min(want_cg, fit);
-    if (p.cgp_gu >= want_cg || p.nst_gu == Ring<QT>::kMinGateUp) break;
+    p.cgp_gu = std::min(std::min(want_cg, kGuMaxCG), fit);
+    if (p.cgp_gu >= std::min(want_cg, kGuMaxCG) || p.nst_gu <= 2) break;
     --p.nst_gu;
   }
   if (p.cgp_gu < 1) return false;
-  p.smem_gu = x_stage_bytes(d, p.cgp_gu) + kBarArea + kGuWarps * p.nst_gu * 2 * Tr::kTileBytes;
-  p.nst_dn = std::max(2, std::min(Ring<QT>::kDown, F / 64));
-  const int ring_dn = kDnWarps * p.nst_dn * Tr::kTileBytes;
-  p.cgp_dn = std::min(want_cg, (kMaxSmem - kBarArea - ring_dn) / x_stage_bytes(F, 1));
+  // the split-K reduction (cgp KB per warp) lives in the rings
+  if (p.ks > 1 && p.nst_gu * gu_stage_bytes<QT>() < p.cgp_gu * 1024) return false;
+  p.smem_gu = x_stage_bytes(d, p.cgp_gu) + kBarArea + kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
+  const int dn_u = Ring<QT>::kDnU;
+  p.nst_dn = std::max(1, std::min(Ring<QT>::kDnStages, (F / 64 + dn_u - 1) / dn_u));
+  const int ring_dn = kDnWarps * p.nst_dn * dn_stage_bytes<QT>();
+  p.cgp_dn = std::min(std::min(want_cg, kGuMaxCG), (kMaxSmem - kBarArea - ring_dn) / x_stage_bytes(F, 1));
   if (p.cgp_dn < 1) return false;
   p.smem_dn = x_stage_bytes(F, p.cgp_dn) + kBarArea + ring_dn;
   p.grid_dn = est_active * ((strips_d + kDnWarps - 1) / kDnWarps);
@@ -719,8 +780,9 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
 template <int QT>
 static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down,
                           const int32_t* offsets, int E, int rows, const float* x,
-                          const int32_t* x_rows, int x_div, int d, int F, float* y,
-                          const int32_t* y_rows, const ExpertsWs& w, cudaStream_t s) {
+                          const int32_t* x_rows, int x_div, const float* x_row_max, bool planned,
+                          int d, int F, float* y, const int32_t* y_rows, const ExpertsWs& w,
+                          cudaStream_t s) {
   using Tr = QTraits<QT>;
   ExpertsPlan p;
   MOE_REQUIRE(plan_experts<QT>(rows, E, d, F, p), MOE_ERR_UNSUPPORTED,
@@ -736,7 +798,7 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
     attr_set |= 1ull << (dev & 63);
   }
   const int mg = max_groups(rows, E);
-  {
+  if (!planned) {
     ::moe::ProfScope _prof(MOE_K_PLAN, s);
     plan_kernel<<<1, kPlanThreads, 0, s>>>(offsets, E, rows, mg, w.n_active, w.active, w.goff,
                                            w.gexp, w.status);
@@ -744,8 +806,8 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   MOE_CHECK(check_launch("plan"));
   {
     ::moe::ProfScope _prof(MOE_K_XPREP, s);
-    xprep_kernel<QT><<<mg, 128, 0, s>>>(x, x_rows, x_div, offsets, w.goff, w.gexp, E, d,
-                                        w.row_scale, w.xfrag);
+    xprep_kernel<QT><<<mg, 128, 0, s>>>(x, x_rows, x_div, x_row_max, offsets, w.goff, w.gexp, E,
+                                        d, w.row_scale, w.xfrag);
   }
   MOE_CHECK(check_launch("xprep"));
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
@@ -765,10 +827,22 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   return check_launch("down");
 }
 
+// Plan arrays inside an experts workspace, for a dispatch that writes them.
+void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
+                         int** goff, int** gexp, int* mg) {
+  ExpertsWs w = carve_experts(ws, rows, E, d, F);
+  *n_active = w.n_active;
+  *active = w.active;
+  *goff = w.goff;
+  *gexp = w.gexp;
+  *mg = max_groups(rows, E);
+}
+
 int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
                 const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
-                size_t ws_bytes, cudaStream_t s, int* status) {
+                size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
+                bool planned) {
   MOE_REQUIRE(qtype_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
   MOE_REQUIRE(E > 0 && E <= kPlanThreads, MOE_ERR_UNSUPPORTED, "local expert count %d", E);
   MOE_REQUIRE(d > 0 && F > 0 && d % 64 == 0 && F % 64 == 0, MOE_ERR_UNSUPPORTED,
@@ -785,10 +859,10 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
   MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "experts workspace %zu < %zu", ws_bytes,
               w.bytes);
   if (qtype == MOE_Q4_0)
-    return launch_experts<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div, d,
-                                    F, y, y_rows, w, s);
-  return launch_experts<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div, d,
-                                  F, y, y_rows, w, s);
+    return launch_experts<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
+                                    x_row_max, planned, d, F, y, y_rows, w, s);
+  return launch_experts<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
+                                  x_row_max, planned, d, F, y, y_rows, w, s);
 }
 
 }  // namespace moe
@@ -808,7 +882,7 @@ int moe_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 moe_stream_t stream) {
   return moe::run_experts(w_gate, w_up, w_down, qtype, expert_offsets, E_local, rows, x, x_rows,
                           x_rows_div, d, F, y, y_rows, workspace, workspace_bytes,
-                          reinterpret_cast<cudaStream_t>(stream), nullptr);
+                          reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, false);
 }
 
 }  // extern "C"

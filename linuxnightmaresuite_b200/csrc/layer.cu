@@ -7,7 +7,16 @@ namespace moe {
 int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
                 const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
-                size_t ws_bytes, cudaStream_t s, int* status);
+                size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
+                bool planned);
+void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
+                         int** goff, int** gexp, int* mg);
+int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
+                  int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream, float* row_max);
+int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
+                            int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
+                            int* active, int* goff, int* gexp, int max_groups, cudaStream_t s);
 int experts_workspace(int rows, int E, int d, int F, size_t* bytes);
 int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
                    const float* residual, int T, int k, int d, float* out, cudaStream_t s);
@@ -33,6 +42,7 @@ struct LayerWs {
   float* y;
   int32_t* s_off;
   float* s_y;
+  float* row_max;
   size_t bytes;
 };
 
@@ -56,6 +66,7 @@ static LayerWs carve_layer(void* ws, const moe_layer_weights* w, int T) {
   L.y = c.take<float>(P * w->d);
   L.s_off = c.take<int32_t>(2);
   L.s_y = w->s_gate ? c.take<float>((size_t)T * w->d) : nullptr;
+  L.row_max = c.take<float>(T > 0 ? T : 1);
   L.bytes = align_up(c.used, 256);
   return L;
 }
@@ -92,11 +103,15 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
   int32_t* ids = ids_out ? ids_out : L.ids;
   float* wts = weights_out ? weights_out : L.wts;
   const int P = T * w->k;
-  MOE_CHECK(moe_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
-                       ids, wts, L.router_ws, L.router_bytes, stream));
-  MOE_CHECK(moe_dispatch(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status, 256, stream));
+  MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
+                          ids, wts, L.router_ws, L.router_bytes, s, L.row_max));
+  int *n_active, *active, *goff, *gexp, mg;
+  experts_plan_arrays(L.exp_ws, P, w->E, w->d, w->F, &n_active, &active, &goff, &gexp, &mg);
+  MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
+                                    n_active, active, goff, gexp, mg, s));
   MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
-                        w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status));
+                        w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
+                        L.row_max, true));
   if (w->s_gate) {
     {
       ::moe::ProfScope _prof(MOE_K_AUX, s);
@@ -105,7 +120,7 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
     MOE_CHECK(check_launch("fill_offsets"));
     MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
                           nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.exp_ws, L.exp_bytes, s,
-                          L.status));
+                          L.status, L.row_max, false));
   }
   return launch_combine(L.y, L.inv, wts, L.s_y, residual, T, w->k, w->d, out, s);
 }

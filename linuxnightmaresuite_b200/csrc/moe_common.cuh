@@ -264,11 +264,18 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   return p;
 }
 
-// Bounded wait for an mbarrier phase.  Returns false (and the caller flags
-// MOE_STATUS_TIMEOUT) if the phase has not completed after ~2^26 polls.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for an mbarrier phase.  Gives up (returns false; the caller
+// flags MOE_STATUS_TIMEOUT) after ~0.2 s of wall time or 2^24 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t it = 0; it < (1u << 26); ++it) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -277,8 +284,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(a), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((it & 255u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (it == 0u) t0 = now;
+      else if (now - t0 > 200000000ull) return false;
+    }
   }
   return false;
+}
+
+// Exclusive scan of one int per thread over the block (<= 1024 threads);
+// sh needs 33 ints.
+static __device__ int block_excl_scan(int v, int* sh, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) sh[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    sh[lane] = wi - w;
+    if (lane == 31) sh[32] = wi;
+  }
+  __syncthreads();
+  int res = sh[warp] + incl - v;
+  total = sh[32];
+  __syncthreads();
+  return res;
 }
 
 __device__ __forceinline__ void set_status(int* status, int bit) {

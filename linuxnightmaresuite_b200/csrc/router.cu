@@ -12,6 +12,8 @@
 // terms, 8-way pairwise at and above) so the denominators follow the reference.
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "moe_common.cuh"
@@ -118,6 +120,308 @@ __device__ __forceinline__ bool beats(float a, int ia, float b, int ib) {
   if (na != nb) return na;
   if (na) return ia > ib;
   return a > b || (a == b && ia > ib);
+}
+
+// Selection and weights for one token whose E logits (bias included) sit in
+// shared memory; executed by one warp.  Same rules as router_select_kernel.
+__device__ void select_token(const float* __restrict__ lg, float* __restrict__ buf,
+                             float* __restrict__ sv, int E, int k, int mode,
+                             int32_t* __restrict__ ids_t, float* __restrict__ w_t) {
+  const int lane = threadIdx.x & 31;
+  const int J = (E + 31) / 32;
+  float v[kMaxE / 32];
+#pragma unroll
+  for (int j = 0; j < kMaxE / 32; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = (j < J && e < E) ? lg[e] : 0.f;
+  }
+  if (mode == MOE_ROUTE_SOFTMAX_TOPK_RENORM) {
+    float m = -INFINITY;
+    bool any_nan = false;
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+      const int e = lane + 32 * j;
+      if (j < J && e < E) {
+        any_nan |= isnan(v[j]);
+        m = fmaxf(m, v[j]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    any_nan = __any_sync(0xffffffffu, any_nan);
+    if (any_nan) m = NAN;
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+      const int e = lane + 32 * j;
+      if (j < J && e < E) {
+        v[j] = expf(v[j] - m);
+        buf[e] = v[j];
+      }
+    }
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0) s = np_pairwise_sum(buf, E);
+    s = __shfl_sync(0xffffffffu, s, 0);
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) v[j] = v[j] / s;
+  }
+  unsigned taken = 0u;
+  int sel_id = -1;
+  float sel_val = 0.f;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = -1;
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+      const int e = lane + 32 * j;
+      if (j < J && e < E && !((taken >> j) & 1u)) {
+        if (bi < 0 || beats(v[j], e, bv, bi)) {
+          bv = v[j];
+          bi = e;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi >= 0 && (bi < 0 || beats(ov, oi, bv, bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == 0) sv[r] = bv;
+    if (lane == r) {
+      sel_id = bi;
+      sel_val = bv;
+    }
+  }
+  __syncwarp();
+  if (mode == MOE_ROUTE_TOPK_SOFTMAX) {
+    float mx = sv[0];
+    for (int r = 1; r < k; ++r) mx = fmaxf(mx, sv[r]);
+    __syncwarp();
+    if (lane < k) buf[lane] = expf(sel_val - mx);
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0) s = np_pairwise_sum(buf, k);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (lane < k) {
+      ids_t[lane] = sel_id;
+      w_t[lane] = buf[lane] / s;
+    }
+  } else {
+    const int pos = k - 1 - lane;
+    __syncwarp();
+    if (lane < k) buf[pos] = sel_val;
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0) s = np_pairwise_sum(buf, k);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (lane < k) {
+      ids_t[pos] = sel_id;
+      w_t[pos] = sel_val / s;
+    }
+  }
+  __syncwarp();
+}
+
+// Router in one launch: a cluster of kRouterCluster CTAs per token tile.  CTA
+// rank r accumulates partial logits of the tile's tokens over its d-range:
+// 32-row chunks of the router matrix and the matching slice of the tokens are
+// double-buffered into shared memory by bulk copies (TMA), and each thread
+// keeps TPT tokens x 4 experts of partial sums in registers.  The partials stay
+// in the CTA's shared memory; after a cluster barrier CTA r sums, for its share
+// of the tile's tokens, the partials of ranks 0..C-1 in rank order through
+// distributed shared memory, adds the bias and selects with one warp per token.
+// The same pass records each token's max |x| when row_max is given.
+constexpr int kRouterCluster = 8;
+constexpr int kFusedDC = 32;            // router rows per chunk
+constexpr int kFusedXP = kFusedDC + 4;  // padded x row (16-byte aligned)
+
+struct FusedShape {
+  int ct, tg, tt, per, tiles;
+};
+
+// Thread shape of router_fused_kernel: ct threads cover the E experts (4 each),
+// tg token groups of TPT tokens fill the 256 threads; tt = tg * TPT tokens per
+// cluster, a multiple of the cluster size so every rank reduces per = tt / C.
+static FusedShape fused_shape(int T, int E, int tpt) {
+  FusedShape f;
+  f.ct = E / 4;
+  f.tg = kRouterThreads / f.ct;
+  if (f.tg >= kRouterCluster) f.tg -= f.tg % kRouterCluster;
+  f.tt = f.tg * tpt;
+  f.per = f.tt / kRouterCluster;
+  f.tiles = (T + f.tt - 1) / f.tt;
+  return f;
+}
+
+static size_t fused_smem(const FusedShape& f, int E) {
+  return (2 * (size_t)kFusedDC * E + 2 * (size_t)f.tt * kFusedXP + (size_t)f.tt * E +
+          (size_t)f.per * E + (size_t)(kRouterThreads / 32) * (kMaxE + kMaxK) + (size_t)f.tt) *
+             sizeof(float) +
+         64;
+}
+
+template <int TPT>
+__global__ void __launch_bounds__(kRouterThreads)
+router_fused_kernel(const float* __restrict__ x, const float* __restrict__ G,
+                    const float* __restrict__ bias, int T, int d, int E, int k, int layout,
+                    int mode, int tg, int32_t* __restrict__ ids, float* __restrict__ weights,
+                    float* __restrict__ row_max, int* __restrict__ status) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(128) float smem[];
+  constexpr int NT = kRouterThreads;
+  constexpr int NW = NT / 32;
+  const int ct = E / 4;
+  const int tt = tg * TPT;
+  const int per = tt / kRouterCluster;
+  float* gbuf = smem;                                // [2][kFusedDC][E] (E_D: [2][E][kFusedDC])
+  float* xbuf = gbuf + 2 * kFusedDC * E;             // [2][tt][kFusedXP]
+  float* part = xbuf + 2 * tt * kFusedXP;            // [tt][E] partial logits
+  float* lg = part + tt * E;                         // [per][E] reduced logits
+  float* buf = lg + per * E;                         // [NW][kMaxE]
+  float* sv = buf + NW * kMaxE;                      // [NW][kMaxK]
+  float* xmax = sv + NW * kMaxK;                     // [tt]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xmax + tt + ((tt & 1) ? 1 : 0));  // [2]
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int col = tid % ct;
+  const int tgrp = tid / ct;                         // >= tg: idle in the compute
+  const int rank = (int)cluster.block_rank();
+  const int t0 = (blockIdx.x / kRouterCluster) * tt;
+  const int nchunks = (d + kFusedDC - 1) / kFusedDC;
+  const int cb = rank * nchunks / kRouterCluster, ce = (rank + 1) * nchunks / kRouterCluster;
+  const int nvalid = max(0, min(tt, T - t0));
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  // rows of tokens past T stay zero in both stages
+  for (int v = tid; v < 2 * tt * kFusedXP; v += NT) {
+    const int tl = (v / kFusedXP) % tt;
+    if (tl >= nvalid) xbuf[v] = 0.f;
+  }
+  for (int tl = tid; tl < tt; tl += NT) xmax[tl] = 0.f;
+  __syncthreads();
+
+  // warp 0 issues one chunk into a stage: the router rows and the tile's x slice
+  auto issue = [&](int c, int stg) {
+    if (warp != 0) return;
+    const int i0 = c * kFusedDC;
+    const int rows = min(kFusedDC, d - i0);
+    float* gs = gbuf + stg * kFusedDC * E;
+    float* xs = xbuf + stg * tt * kFusedXP;
+    const uint32_t gbytes = (uint32_t)(rows * E * 4);
+    const uint32_t xbytes = (uint32_t)(rows * 4);
+    if (lane == 0) {
+      fence_proxy_async_smem();
+      mbar_expect_tx(&bar[stg], gbytes + xbytes * nvalid);
+    }
+    __syncwarp();
+    if (layout == MOE_ROUTER_D_E) {
+      if (lane == 0) bulk_g2s_plain(gs, G + (size_t)i0 * E, gbytes, &bar[stg]);
+    } else {
+      for (int e = lane; e < E; e += 32)
+        bulk_g2s_plain(gs + e * kFusedDC, G + (size_t)e * d + i0, xbytes, &bar[stg]);
+    }
+    for (int tl = lane; tl < nvalid; tl += 32)
+      bulk_g2s_plain(xs + tl * kFusedXP, x + (size_t)(t0 + tl) * d + i0, xbytes, &bar[stg]);
+  };
+
+  float acc[TPT][4];
+#pragma unroll
+  for (int a = 0; a < TPT; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  if (cb < ce) issue(cb, 0);
+  if (cb + 1 < ce) issue(cb + 1, 1);
+  bool ok = true;
+  for (int c = cb; c < ce; ++c) {
+    const int stg = (c - cb) & 1;
+    const uint32_t parity = ((c - cb) >> 1) & 1;
+    if (ok && !mbar_wait(&bar[stg], parity)) {
+      set_status(status, MOE_STATUS_TIMEOUT);
+      ok = false;
+    }
+    const int rows = min(kFusedDC, d - c * kFusedDC);
+    const float* gs = gbuf + stg * kFusedDC * E;
+    const float* xs = xbuf + stg * tt * kFusedXP;
+    if (row_max) {  // each token row owned by one thread
+      for (int tl = tid; tl < tt; tl += NT) {
+        float m = xmax[tl];
+        for (int i = 0; i < rows; ++i) m = fmaxf(m, fabsf(xs[tl * kFusedXP + i]));
+        xmax[tl] = m;
+      }
+    }
+    if (tgrp < tg) {
+      if (layout == MOE_ROUTER_D_E) {
+        for (int i = 0; i < rows; ++i) {
+          const float4 g4 = *reinterpret_cast<const float4*>(gs + i * E + 4 * col);
+#pragma unroll
+          for (int a = 0; a < TPT; ++a) {
+            const float xv = xs[(tgrp + a * tg) * kFusedXP + i];
+            acc[a][0] = fmaf(xv, g4.x, acc[a][0]);
+            acc[a][1] = fmaf(xv, g4.y, acc[a][1]);
+            acc[a][2] = fmaf(xv, g4.z, acc[a][2]);
+            acc[a][3] = fmaf(xv, g4.w, acc[a][3]);
+          }
+        }
+      } else {
+        for (int i = 0; i < rows; ++i) {
+          float g[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) g[j] = gs[(4 * col + j) * kFusedDC + i];
+#pragma unroll
+          for (int a = 0; a < TPT; ++a) {
+            const float xv = xs[(tgrp + a * tg) * kFusedXP + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[a][j] = fmaf(xv, g[j], acc[a][j]);
+          }
+        }
+      }
+    }
+    __syncthreads();  // stage fully read before it is refilled
+    if (ok && c + 2 < ce) issue(c + 2, stg);
+  }
+  if (tgrp < tg) {
+#pragma unroll
+    for (int a = 0; a < TPT; ++a) {
+      const float4 v = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+      *reinterpret_cast<float4*>(part + (tgrp + a * tg) * E + 4 * col) = v;
+    }
+  }
+  cluster.sync();
+  // reduce this rank's tokens over the cluster, in rank order
+  for (int v = tid; v < per * E; v += NT) {
+    const int tl = rank * per + v / E, e = v % E;
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < kRouterCluster; ++q) sum += cluster.map_shared_rank(part, q)[tl * E + e];
+    if (bias) sum += __ldg(bias + e);
+    lg[(v / E) * E + e] = sum;
+  }
+  if (row_max) {
+    for (int i = tid; i < per; i += NT) {
+      const int tl = rank * per + i;
+      float m = 0.f;
+#pragma unroll
+      for (int q = 0; q < kRouterCluster; ++q) m = fmaxf(m, cluster.map_shared_rank(xmax, q)[tl]);
+      if (t0 + tl < T) row_max[t0 + tl] = m;
+    }
+  }
+  __syncthreads();
+  for (int i = warp; i < per; i += NW) {
+    const int t = t0 + rank * per + i;
+    if (t < T)
+      select_token(lg + i * E, buf + warp * kMaxE, sv + warp * kMaxK, E, k, mode,
+                   ids + (size_t)t * k, weights + (size_t)t * k);
+  }
+  cluster.sync();  // peers may still be reading this CTA's partials
 }
 
 // One warp per token.  Lanes hold logits e = lane + 32 j.
@@ -249,12 +553,22 @@ router_select_kernel(const float* __restrict__ part, int nds, const float* __res
   }
 }
 
+// moe_router keeps its partial logits in shared memory (cluster reduction);
+// the workspace only carries the status word.
 static size_t router_ws(int T, int d, int E) {
-  RouterPlan p = router_plan(T, d, E);
-  return align_up(256, 256) + align_up((size_t)p.nds * T * E * sizeof(float), 256);
+  (void)T;
+  (void)d;
+  (void)E;
+  return 256;
 }
 
 }  // namespace moe
+
+namespace moe {
+int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
+                  int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream, float* row_max);
+}
 
 extern "C" {
 
@@ -268,7 +582,19 @@ int moe_router_workspace_bytes(int T, int d, int E, size_t* bytes) {
 int moe_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
                int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
                size_t workspace_bytes, moe_stream_t stream) {
-  using namespace moe;
+  return moe::launch_router(x, gate_w, bias, T, d, E, k, layout, mode, ids, weights, workspace,
+                            workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // extern "C"
+
+namespace moe {
+
+// moe_router plus, when row_max is given, each token's max |x| (used by the
+// expert activation prep of the fused layer).
+int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
+                  int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream, float* row_max) {
   MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
   if (T == 0) return MOE_OK;
   MOE_REQUIRE(x && gate_w && ids && weights && workspace, MOE_ERR_INVALID, "null pointer");
@@ -284,30 +610,61 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
   MOE_REQUIRE(workspace_bytes >= router_ws(T, d, E), MOE_ERR_WORKSPACE,
               "router workspace %zu < %zu", workspace_bytes, router_ws(T, d, E));
   MOE_REQUIRE(((uintptr_t)gate_w & 15) == 0, MOE_ERR_INVALID, "router weight not 16B aligned");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  RouterPlan p = router_plan(T, d, E);
-  float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
-  size_t smem = ((size_t)kRouterDC * E + (size_t)p.tt * (kRouterDC + 1)) * sizeof(float);
-  if (smem > 48 * 1024) {
-    MOE_CUDA(cudaFuncSetAttribute(router_partial_kernel,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaStream_t s = stream;
+  MOE_REQUIRE(d % 4 == 0, MOE_ERR_UNSUPPORTED, "d=%d must be a multiple of 4", d);
+  MOE_REQUIRE(((uintptr_t)x & 15) == 0, MOE_ERR_INVALID, "x not 16B aligned");
+  // one token per thread for small batches (more clusters), four for large
+  // ones or when few token groups fit beside the experts
+  const int tg1 = fused_shape(T, E, 1).tg;
+  const int tpt = (tg1 < kRouterCluster || (T > 256 && tg1 <= kRouterCluster)) ? 4 : 1;
+  const FusedShape f = fused_shape(T, E, tpt);
+  const size_t smem = fused_smem(f, E);
+  MOE_REQUIRE(f.per >= 1 && f.tt % kRouterCluster == 0 && f.ct * f.tg <= kRouterThreads &&
+                  smem <= 227 * 1024,
+              MOE_ERR_UNSUPPORTED, "router shape E=%d does not fit the fused router", E);
+  static std::mutex attr_mu;
+  static int attr_smem[2][64] = {{0}};  // largest size set so far, per instance and device
+  {
+    int dev = 0;
+    MOE_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(attr_mu);
+    const int ti = tpt == 1 ? 0 : 1;
+    if (dev < 0 || dev >= 64 || attr_smem[ti][dev] < (int)smem) {
+      if (tpt == 1)
+        MOE_CUDA(cudaFuncSetAttribute(router_fused_kernel<1>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      else
+        MOE_CUDA(cudaFuncSetAttribute(router_fused_kernel<4>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      if (dev >= 0 && dev < 64) attr_smem[ti][dev] = (int)smem;
+    }
   }
-  dim3 grid(p.tiles, p.nds);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(f.tiles * kRouterCluster);
+  cfg.blockDim = dim3(kRouterThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kRouterCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int* status = workspace ? static_cast<int*>(workspace) : nullptr;
   {
     ::moe::ProfScope _prof(MOE_K_ROUTER_PARTIAL, s);
-    router_partial_kernel<<<grid, p.ct * p.tg, smem, s>>>(x, gate_w, T, d, E, layout, p.tt,
-                                                             p.chunks, part);
+    if (tpt == 1)
+      MOE_CUDA(cudaLaunchKernelEx(&cfg, router_fused_kernel<1>, x, gate_w, bias, T, d, E, k,
+                                  layout, mode, f.tg, ids, weights, row_max, status));
+    else
+      MOE_CUDA(cudaLaunchKernelEx(&cfg, router_fused_kernel<4>, x, gate_w, bias, T, d, E, k,
+                                  layout, mode, f.tg, ids, weights, row_max, status));
   }
-  MOE_CHECK(check_launch("router_partial"));
-  {
-    ::moe::ProfScope _prof(MOE_K_ROUTER_SELECT, s);
-    router_select_kernel<<<(T + 3) / 4, 128, 0, s>>>(part, p.nds, bias, T, E, k, mode, ids,
-                                                     weights);
-  }
-  return check_launch("router_select");
+  return check_launch("router_fused");
 }
 
-}  // extern "C"
+}  // namespace moe
 
 // ---------------------------------------------------------------------------
 // Allocation-free router.
