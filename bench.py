@@ -256,28 +256,43 @@ def run_b200(args):
 
     name, T = WORKLOADS[args.workload]
     cfg = synth.CONFIGS[name]
-    # every rank runs its own copy of the layer on its own tokens (seed per rank)
-    data = synth.make_layer(cfg, args.seed + rank, tokens=T)
-    layer = build_layer(data, dev)
-    x = torch.from_numpy(data.x).to(dev)
+    if world == 1:
+        data = synth.make_layer(cfg, args.seed, tokens=T)
+        layer = build_layer(data, dev)
+        x_np = data.x
+    else:
+        # expert parallelism: the same layer on every rank (experts sharded),
+        # T tokens per rank
+        from linuxnightmaresuite_b200.ep import EPMoELayer
+        data = synth.make_layer(cfg, args.seed, tokens=T * world)
+        layer = EPMoELayer(data.gate_w, data.w_gate, data.w_up, data.w_down, cfg.qtype,
+                           cfg.top_k, cfg.route_mode, data.bias, device=dev)
+        x_np = np.ascontiguousarray(data.x[rank * T:(rank + 1) * T])
+    x = torch.from_numpy(x_np).to(dev)
     out = torch.empty_like(x)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
-    def step():
-        layer.forward_batch(x, out=out)
+    def step(inp=x):
+        if world == 1:
+            return layer.forward_batch(inp, out=out)
+        return layer.forward(inp)
 
     for _ in range(max(args.warmup, 0)):
         flush.zero_()
         step()
     torch.cuda.synchronize()
-    if layer.device_status() != 0:
+    if world == 1 and layer.device_status() != 0:
         raise RuntimeError("device status error during warm-up")
 
     # routing statistics of this batch (unique experts -> algorithmic bytes)
-    _, ids, _ = layer.forward_batch(x, out=out, return_routing=True)
-    ids = ids.cpu().numpy()
-    uniq = int(np.unique(ids).size)
-    rows = int(ids.size)
+    if world == 1:
+        _, ids, _ = layer.forward_batch(x, out=out, return_routing=True)
+        ids = ids.cpu().numpy()
+        uniq = int(np.unique(ids).size)
+        rows = int(ids.size)
+    else:
+        step()
+        uniq, rows = layer.last["active"], layer.last["rows"]
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -308,15 +323,15 @@ def run_b200(args):
     launches = sum(c for _, c in prof.values())
 
     # end to end through the public API with host buffers
-    x_host = torch.from_numpy(data.x).pin_memory()
+    x_host = torch.from_numpy(x_np).pin_memory()
     out_host = torch.empty(x_host.shape, dtype=torch.float32).pin_memory()
     x_dev = torch.empty_like(x)
     e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for _ in range(2):
         x_dev.copy_(x_host, non_blocking=True)
-        layer.forward_batch(x_dev, out=out)
-        out_host.copy_(out, non_blocking=True)
+        res = step(x_dev)
+        out_host.copy_(res, non_blocking=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -324,8 +339,8 @@ def run_b200(args):
         flush.zero_()
         e_starts[i].record()
         x_dev.copy_(x_host, non_blocking=True)
-        layer.forward_batch(x_dev, out=out)
-        out_host.copy_(out, non_blocking=True)
+        res = step(x_dev)
+        out_host.copy_(res, non_blocking=True)
         e_ends[i].record()
     torch.cuda.synchronize()
     e2e_ms = float(np.mean([s.elapsed_time(e) for s, e in zip(e_starts, e_ends)]))
@@ -333,7 +348,7 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
     e2e_ms = float(e_t.item())
-    if layer.device_status() != 0:
+    if world == 1 and layer.device_status() != 0:
         raise RuntimeError("device status error during the timed steps")
 
     hbm_peak, tc_peak, peak_kind = peaks()
@@ -353,7 +368,7 @@ def run_b200(args):
     else:
         gu_launch_ms, achieved = None, None
     traffic = ncu_traffic(args.workload, "gateup")
-    layer_bytes = uniq * 3 * mat + d * cfg.n_experts * 4 + T * d * 8
+    layer_bytes = uniq * 3 * mat + d * cfg.n_experts * 4 + T * d * 8  # this rank's share
     roofline = {
         "kernel": "gateup (grouped gate/up GEMV + SiLU*up)",
         "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -389,7 +404,8 @@ def run_b200(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_desc(cfg, T), "tokens_per_rank": T,
                    "unique_experts": uniq, "routed_rows": rows,
-                   "parallelism": "replicas" if world > 1 else "single",
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "experts_per_rank": cfg.n_experts // world,
                    "l2": f"flushed by a {FLUSH_BYTES >> 20} MiB write before every step "
                          "(outside the step events)",
                    "weights_bytes_resident": 3 * cfg.n_experts * mat},

@@ -186,6 +186,28 @@ int moe_combine(const float* y, const int32_t* inv_perm, const float* weights,
                 const float* shared, const float* residual, int T, int k, int d, float* out,
                 moe_stream_t stream);
 
+/* ---- expert parallelism ----------------------------------------------------------- */
+
+/* out[r] = x[rows[r] / div] for r < n: the expert-sorted send buffer of the
+ * expert-parallel exchange (rows = moe_dispatch's perm_rows, div = k).  Replaces
+ * the per-expert host upload of the token vector to each card
+ * (nightmare_stream.py:4381-4395). */
+int moe_gather_rows(const float* x, const int32_t* rows, int div, int n, int d, float* out,
+                    moe_stream_t stream);
+
+/* Owner-side order of rows received in an expert-parallel exchange.
+ *   recv_counts (W, E_local) int32: rows source s sent for local expert e; the
+ *   receive buffer holds them source-major, expert-minor.
+ *   local_offsets (E_local+1) out; row_map (<= max_rows) out: expert-sorted local
+ *   row r is receive-buffer row row_map[r] (feed it to moe_experts as x_rows and
+ *   y_rows).  More than max_rows rows sets MOE_STATUS_ROW_OVERFLOW in the status
+ *   word at the start of workspace (256 B) and leaves row_map unwritten.
+ * Replaces the host-side per-expert bookkeeping of _moe_ffn_g4_gpu
+ * (nightmare_stream.py:4400-4449). */
+int moe_ep_local_order(const int32_t* recv_counts, int W, int E_local, int max_rows,
+                       int32_t* local_offsets, int32_t* row_map, void* workspace,
+                       moe_stream_t stream);
+
 /* RMSNorm of moe_forward.rms_norm (moe_forward.py:34-40):
  * out[t] = x[t] / sqrt(mean(x[t]^2) + eps) * weight. */
 int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, float* out,

@@ -68,6 +68,8 @@ SIGNATURES = {
     "moe_experts": [vp, vp, vp, ci, vp, ci, ci, vp, vp, ci, ci, ci, vp, vp, vp, csz, vp],
     "moe_combine": [vp, vp, vp, vp, vp, ci, ci, ci, vp, vp],
     "moe_rms_norm": [vp, vp, cf, ci, ci, vp, vp],
+    "moe_gather_rows": [vp, vp, ci, ci, ci, vp, vp],
+    "moe_ep_local_order": [vp, ci, ci, ci, vp, vp, vp, vp],
     "moe_layer_workspace_bytes": [ctypes.POINTER(MoELayerWeights), ci, ctypes.POINTER(csz)],
     "moe_layer_forward": [ctypes.POINTER(MoELayerWeights), vp, ci, vp, vp, vp, vp, vp, csz, vp],
 }

@@ -157,6 +157,28 @@ def combine(y: torch.Tensor, inv_perm: torch.Tensor, weights: torch.Tensor,
     return out
 
 
+def gather_rows(x: torch.Tensor, rows: torch.Tensor, div: int = 1,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _need(x, torch.float32, "x")
+    _need(rows, torch.int32, "rows")
+    n, d = rows.numel(), x.shape[1]
+    if out is None:
+        out = torch.empty((n, d), dtype=torch.float32, device=x.device)
+    call("moe_gather_rows", _ptr(x), _ptr(rows), div, n, d, _ptr(out), _stream())
+    return out
+
+
+def ep_local_order(recv_counts: torch.Tensor, max_rows: int, ws: torch.Tensor):
+    """(local_offsets (E_local+1), row_map (max_rows)) on the device."""
+    _need(recv_counts, torch.int32, "recv_counts")
+    W, El = recv_counts.shape
+    loff = torch.empty(El + 1, dtype=torch.int32, device=recv_counts.device)
+    row_map = torch.empty(max(max_rows, 1), dtype=torch.int32, device=recv_counts.device)
+    call("moe_ep_local_order", _ptr(recv_counts), W, El, max_rows, _ptr(loff), _ptr(row_map),
+         _ptr(ws), _stream())
+    return loff, row_map
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
              out: Optional[torch.Tensor] = None) -> torch.Tensor:
     _need(x, torch.float32, "x")

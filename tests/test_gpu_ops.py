@@ -191,3 +191,25 @@ def test_combine_and_rms_norm():
     got = K.rms_norm(cuda(x), cuda(nw)).cpu().numpy()
     exp = np.stack([orc.rms_norm(x[t], nw) for t in range(T)])
     np.testing.assert_allclose(got, exp, rtol=2e-6, atol=1e-6)
+
+
+def test_gather_rows_and_ep_local_order():
+    from linuxnightmaresuite_b200 import ep
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((40, 96), dtype=np.float32)
+    rows = rng.integers(0, 40 * 3, size=77).astype(np.int32)
+    got = K.gather_rows(cuda(x), cuda(rows), 3).cpu().numpy()
+    assert np.array_equal(got, x[rows // 3])
+    for W, El in ((2, 64), (4, 32), (8, 16), (3, 5)):
+        rc = rng.integers(0, 6, size=(W, El)).astype(np.int32)
+        rc[rng.random((W, El)) < 0.3] = 0
+        R = int(rc.sum())
+        ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
+        loff, rmap = K.ep_local_order(cuda(rc), R, ws)
+        e_loff, e_map = ep.local_order(rc)
+        assert np.array_equal(loff.cpu().numpy(), e_loff)
+        assert np.array_equal(rmap.cpu().numpy()[:R], e_map)
+        assert K.read_status(ws) == 0
+    ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    K.ep_local_order(cuda(np.full((2, 4), 3, np.int32)), 10, ws)   # 24 rows > 10
+    assert K.read_status(ws) & _lib.MOE_STATUS_ROW_OVERFLOW
