@@ -726,8 +726,26 @@ static ExpertsWs carve_experts(void* ws, int rows, int E, int d, int F) {
   return w;
 }
 
+size_t tc_workspace(int rows, int E, int d, int F);
+bool tc_supported(int rows, int E, int d, int F);
+int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                   const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
+                   int x_div, const float* x_row_max, int d, int F, float* y,
+                   const int32_t* y_rows, void* ws, size_t ws_bytes, int* status,
+                   cudaStream_t s);
+
+// Rows per active expert from which the tcgen05 GEMM path is used.
+constexpr int kTcMinMeanRows = 64;
+
+static bool use_tc(int rows, int E, int d, int F) {
+  const int active = rows < E ? rows : E;
+  return active > 0 && rows / active >= kTcMinMeanRows && tc_supported(rows, E, d, F);
+}
+
 int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
-  *bytes = carve_experts(nullptr, rows, E, d, F).bytes;
+  size_t a = carve_experts(nullptr, rows, E, d, F).bytes;
+  if (use_tc(rows, E, d, F)) a = std::max(a, tc_workspace(rows, E, d, F));
+  *bytes = a;
   return MOE_OK;
 }
 
@@ -854,6 +872,9 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
   MOE_REQUIRE(x_div > 0, MOE_ERR_INVALID, "x_rows_div must be positive");
   MOE_REQUIRE(((uintptr_t)w_gate | (uintptr_t)w_up | (uintptr_t)w_down | (uintptr_t)x) % 16 == 0,
               MOE_ERR_INVALID, "weights and activations must be 16-byte aligned");
+  if (use_tc(rows, E, d, F))
+    return run_experts_tc(w_gate, w_up, w_down, qtype, offsets, E, rows, x, x_rows, x_div,
+                          x_row_max, d, F, y, y_rows, ws, ws_bytes, status, s);
   ExpertsWs w = carve_experts(ws, rows, E, d, F);
   if (status) w.status = status;
   MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "experts workspace %zu < %zu", ws_bytes,

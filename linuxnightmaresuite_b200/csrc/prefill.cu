@@ -1,0 +1,670 @@
+// Grouped SwiGLU experts for large row groups (prefill): tcgen05 / TMEM GEMMs.
+//
+// For every expert with many routed rows the two products of ExpertFFN.forward
+// (moe_forward.py:129-133) are dense GEMMs:
+//   GEMM1  [rows x d] x [d x 2F]  -> h = silu(gate) * up      (rows x F)
+//   GEMM2  [rows x F] x [F x d]   -> y                        (rows x d)
+// Each CTA computes one 128-row x 128-column tile with tcgen05.mma
+// (kind::f16, fp32 accumulator in tensor memory):
+//   * the activation tile (fp16 hi and lo planes, see below) arrives by 2-D TMA
+//     with 128-byte swizzle;
+//   * four producer warps dequantise the packed Q4_0 / Q8_0 weight tiles into the
+//     same swizzled layout as fp16 hi + lo (w = d * q exactly, w_hi = fp16(w),
+//     w_lo = fp16(w - w_hi));
+//   * one thread issues three MMAs per 16-wide k step -- x_hi*w_hi + x_hi*w_lo
+//     + x_lo*w_hi -- so operands keep ~22 bits (the reference's f32 tolerance
+//     needs more than one fp16 rounding);
+//   * stage reuse is ordered by mbarriers (TMA transaction counts, producer
+//     arrivals, tcgen05.commit), every wait is bounded;
+//   * four epilogue warps read the accumulator with tcgen05.ld: GEMM1 applies
+//     SiLU(gate) * up and writes the hidden hi/lo planes, GEMM2 writes f32 rows.
+// Rows of a 128-row tile past the expert's range are computed and discarded.
+#include <cuda.h>
+#include <math.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "moe_common.cuh"
+
+namespace moe {
+
+constexpr int kTcM = 128;        // rows (tokens) per tile
+constexpr int kTcN = 128;        // output columns per tile
+constexpr int kTcK = 64;         // k per stage (one packed tile column, 128 B of fp16)
+constexpr int kTcStages = 3;
+constexpr int kTcThreads = 256;  // 8 warps
+constexpr int kTileHalf = kTcM * kTcK * 2;            // one 128 x 64 fp16 tile: 16 KB
+constexpr int kStageBytes = 4 * kTileHalf;            // A hi, A lo, B hi, B lo
+constexpr int kTcSmem = kTcStages * kStageBytes + 1024 + 1024;  // + barriers, + alignment
+constexpr float kTcHScale = 1.0f / 256.0f;            // hidden planes are stored / 256
+// The K range is spread over kTcAcc accumulators (consecutive stage ranges), summed
+// with round-to-nearest in the epilogue: the tensor core's fp32 accumulation
+// truncates, and a 2816-long K otherwise drifts by ~1e-5 relative.
+constexpr int kTcAcc = 4;
+constexpr int kTcCols = kTcAcc * kTcN;                // tensor-memory columns (all 512)
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// K-major, 128-byte-swizzled operand tile: rows of 128 B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint32_t a = smem_u32(tile);
+  uint64_t d = 0;
+  d |= (uint64_t)((a >> 4) & 0x3FFF);           // start address
+  d |= (uint64_t)1 << 16;                       // leading byte offset (unused when swizzled)
+  d |= (uint64_t)(1024 >> 4) << 32;             // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                       // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                       // swizzle: 128 B
+  return d;
+}
+
+// kind::f16 instruction descriptor: f16 A/B, f32 accumulate, K-major, M x N.
+__host__ __device__ constexpr uint32_t tc_idesc(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// sum of the same 32 columns of the first n accumulators (kTcN columns apart),
+// in accumulator order
+__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, float (&v)[32], int n) {
+  tmem_ld32(taddr, v);
+  for (int j = 1; j < n; ++j) {
+    float w[32];
+    tmem_ld32(taddr + (uint32_t)(j * kTcN), w);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], w[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// weight dequantisation into the swizzled B tile
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_store8(uint8_t* hi_row, uint8_t* lo_row, int chunk,
+                                             const float (&w)[8]) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 hh = __floats2half2_rn(w[2 * i], w[2 * i + 1]);
+    const float2 hf = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(w[2 * i] - hf.x, w[2 * i + 1] - hf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  *reinterpret_cast<uint4*>(hi_row + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(lo_row + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// One packed 16-row x 64-column tile (global) -> rows [r0, r0+16) of the
+// swizzled hi / lo tiles.  Lane (g, t) owns rows g and g + 8 and, per 32-wide
+// block, the elements its fragment layout assigns to t.
+template <int QT>
+__device__ __forceinline__ void dequant_tile_to_smem(const uint8_t* __restrict__ tile, int lane,
+                                                     uint8_t* bhi, uint8_t* blo, int r0) {
+  using Tr = QTraits<QT>;
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* qp = tile + lane * Tr::kLaneBytes;
+  const uint2 sc = __ldg(reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + g * 8));
+  const float s[4] = {__half2float(__ushort_as_half((unsigned short)(sc.x & 0xFFFF))),
+                      __half2float(__ushort_as_half((unsigned short)(sc.x >> 16))),
+                      __half2float(__ushort_as_half((unsigned short)(sc.y & 0xFFFF))),
+                      __half2float(__ushort_as_half((unsigned short)(sc.y >> 16)))};
+  if (QT == MOE_Q8_0) {
+    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(qp));       // row g: b0, b1
+    const uint4 qb = __ldg(reinterpret_cast<const uint4*>(qp + 16));  // row g+8: b0, b1
+    const uint32_t words[2][2][2] = {{{qa.x, qa.y}, {qa.z, qa.w}}, {{qb.x, qb.y}, {qb.z, qb.w}}};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int row = r0 + g + 8 * half;
+      uint8_t* hr = bhi + row * 128;
+      uint8_t* lr = blo + row * 128;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const float d = s[half * 2 + b];
+        float w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t word = words[half][b][i >> 2];
+          const int q = (int)(int8_t)((word >> (8 * (i & 3))) & 0xFF);
+          w[i] = d * (float)q;
+        }
+        // elements 32b + 8t .. +7 -> 16-byte chunk 4b + t, swizzled by row
+        split_store8(hr, lr, (4 * b + t) ^ (row & 7), w);
+      }
+    }
+  } else {
+    const uint4 q = __ldg(reinterpret_cast<const uint4*>(qp));  // (g,b0) (g,b1) (g8,b0) (g8,b1)
+    const uint32_t words[2][2] = {{q.x, q.y}, {q.z, q.w}};
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int row = r0 + g + 8 * half;
+      uint8_t* hr = bhi + row * 128;
+      uint8_t* lr = blo + row * 128;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const float d = s[half * 2 + b];
+        const uint32_t word = words[half][b];  // bytes 4t..4t+3 of the block's 16
+        float lo4[4], hi4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t byte = (word >> (8 * i)) & 0xFF;
+          lo4[i] = d * (float)((int)(byte & 0xF) - 8);   // element 4t + i
+          hi4[i] = d * (float)((int)(byte >> 4) - 8);    // element 16 + 4t + i
+        }
+        // elements 32b + 4t .. +3 and 32b + 16 + 4t .. +3: two half chunks
+        // -> write each 8-byte half into its 16-byte chunk
+        const int ch_lo = (4 * b + (t >> 1)) ^ (row & 7);        // element 32b + 4t
+        const int ch_hi = (4 * b + 2 + (t >> 1)) ^ (row & 7);    // element 32b + 16 + 4t
+        const int off = (t & 1) * 8;
+        uint32_t h[2], l[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const __half2 hh = __floats2half2_rn(lo4[2 * i], lo4[2 * i + 1]);
+          const float2 hf = __half22float2(hh);
+          const __half2 ll = __floats2half2_rn(lo4[2 * i] - hf.x, lo4[2 * i + 1] - hf.y);
+          h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+          l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+        }
+        *reinterpret_cast<uint2*>(hr + ch_lo * 16 + off) = make_uint2(h[0], h[1]);
+        *reinterpret_cast<uint2*>(lr + ch_lo * 16 + off) = make_uint2(l[0], l[1]);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const __half2 hh = __floats2half2_rn(hi4[2 * i], hi4[2 * i + 1]);
+          const float2 hf = __half22float2(hh);
+          const __half2 ll = __floats2half2_rn(hi4[2 * i] - hf.x, hi4[2 * i + 1] - hf.y);
+          h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+          l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+        }
+        *reinterpret_cast<uint2*>(hr + ch_hi * 16 + off) = make_uint2(h[0], h[1]);
+        *reinterpret_cast<uint2*>(lr + ch_hi * 16 + off) = make_uint2(l[0], l[1]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// activation planes: sorted row r -> hi plane row r, lo plane row P + r (fp16),
+// scaled by a power of two so the row's max |x| sits in [2^14, 2^15)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+tc_prep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
+               const float* __restrict__ x_row_max, int P, int d, float* __restrict__ row_scale,
+               __half* __restrict__ planes) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + warp;
+  if (r >= P) return;
+  const int src = x_rows ? x_rows[r] / x_div : r;
+  const float4* s4 = reinterpret_cast<const float4*>(x + (size_t)src * d);
+  float m = 0.f;
+  if (x_row_max) {
+    m = x_row_max[src];
+  } else {
+    for (int i = lane; i < d / 4; i += 32) {
+      const float4 v = __ldg(s4 + i);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  }
+  float scale = 1.f, inv = 1.f;
+  if (m > 0.f && isfinite(m)) {
+    const int ex = ilogbf(m);
+    scale = ldexpf(1.f, 14 - ex);
+    inv = ldexpf(1.f, ex - 14);
+  }
+  if (lane == 0) row_scale[r] = inv;
+  __half* hi = planes + (size_t)r * d;
+  __half* lo = planes + ((size_t)P + r) * d;
+  for (int i = lane; i < d / 4; i += 32) {
+    const float4 v = __ldg(s4 + i);
+    const float a[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
+    const __half2 h0 = __floats2half2_rn(a[0], a[1]), h1 = __floats2half2_rn(a[2], a[3]);
+    const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+    const __half2 l0 = __floats2half2_rn(a[0] - f0.x, a[1] - f0.y);
+    const __half2 l1 = __floats2half2_rn(a[2] - f1.x, a[3] - f1.y);
+    reinterpret_cast<__half2*>(hi)[2 * i] = h0;
+    reinterpret_cast<__half2*>(hi)[2 * i + 1] = h1;
+    reinterpret_cast<__half2*>(lo)[2 * i] = l0;
+    reinterpret_cast<__half2*>(lo)[2 * i + 1] = l1;
+  }
+}
+
+// m-tiles of 128 rows per active expert: tile_e[i], tile_r0[i] (sorted row),
+// *n_tiles.  One CTA, E <= 1024.
+__global__ void __launch_bounds__(1024)
+tc_tile_plan_kernel(const int32_t* __restrict__ offsets, int E, int max_tiles,
+                    int* __restrict__ tile_e, int* __restrict__ tile_r0, int* __restrict__ n_tiles) {
+  __shared__ int sh[33];
+  const int e = threadIdx.x;
+  const int n = e < E ? offsets[e + 1] - offsets[e] : 0;
+  const int nt = n > 0 ? (n + kTcM - 1) / kTcM : 0;
+  int tot;
+  const int t0 = block_excl_scan(nt, sh, tot);
+  if (e < E)
+    for (int i = 0; i < nt && t0 + i < max_tiles; ++i) {
+      tile_e[t0 + i] = e;
+      tile_r0[t0 + i] = offsets[e] + i * kTcM;
+    }
+  if (e == 0) *n_tiles = min(tot, max_tiles);
+}
+
+// ---------------------------------------------------------------------------
+// the GEMM.  MODE 0: gate/up (B rows 0-63 from W_gate, 64-127 from W_up, the
+// same 64 F-rows), epilogue SiLU(gate)*up -> hidden planes.  MODE 1: down.
+// ---------------------------------------------------------------------------
+struct TcArgs {
+  const uint8_t* w0;       // MODE 0: W_gate stack; MODE 1: W_down stack
+  const uint8_t* w1;       // MODE 0: W_up stack
+  size_t mat_bytes;
+  int K;                   // reduction length (d or F)
+  int n_tiles_n;           // output column tiles
+  int P;                   // sorted rows (plane height)
+  int F, d;
+  const int32_t* offsets;
+  const int* tile_e;
+  const int* tile_r0;
+  const int* n_mtiles;
+  const float* row_scale;  // MODE 0
+  __half* h_planes;        // MODE 0 output: [2][P][F]
+  float* y;                // MODE 1 output
+  const int32_t* y_rows;
+  int* status;
+};
+
+template <int QT, int MODE>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
+  using Tr = QTraits<QT>;
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  // 1024-byte alignment for the swizzled tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kTcStages * kStageBytes);
+  uint64_t* full_b = full_a + kTcStages;
+  uint64_t* empty = full_b + kTcStages;
+  uint64_t* acc_full = empty + kTcStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x / args.n_tiles_n;
+  const int nt = blockIdx.x % args.n_tiles_n;
+  if (mt >= *args.n_mtiles) return;
+  const int e = args.tile_e[mt];
+  const int row0 = args.tile_r0[mt];
+  const int row_end = args.offsets[e + 1];
+  const int ksteps = args.K / kTcK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_b[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *flag = 0;
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "n"(kTcCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // activation producer: hi and lo planes of the stage's 128 x 64 tile
+    for (int kk = 0; kk < ksteps; ++kk) {
+      const int s = kk % kTcStages, round = kk / kTcStages;
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+        *flag = 1;
+        break;
+      }
+      uint8_t* st = stage_base + s * kStageBytes;
+      mbar_expect_tx(&full_a[s], 2 * kTileHalf);
+      tma_load_2d(st, &amap, kk * kTcK, row0, &full_a[s]);
+      tma_load_2d(st + kTileHalf, &amap, kk * kTcK, args.P + row0, &full_a[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    const uint32_t idesc = tc_idesc(kTcM, kTcN);
+    bool ok = true;
+    for (int kk = 0; kk < ksteps && ok; ++kk) {
+      const int s = kk % kTcStages, round = kk / kTcStages;
+      if (!mbar_wait(&full_a[s], round & 1) || !mbar_wait(&full_b[s], round & 1)) {
+        *flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint8_t* st = stage_base + s * kStageBytes;
+      const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + kTileHalf);
+      const uint64_t bhi = sw128_desc(st + 2 * kTileHalf), blo = sw128_desc(st + 3 * kTileHalf);
+      // accumulator j = kk * nacc / ksteps takes a consecutive run of stages
+      const int nacc = ksteps < kTcAcc ? ksteps : kTcAcc;
+      const int j = kk * nacc / ksteps;
+      const bool first = kk == 0 || (kk - 1) * nacc / ksteps != j;
+      const uint32_t dacc = tmem + (uint32_t)(j * kTcN);
+#pragma unroll
+      for (int k16 = 0; k16 < kTcK / 16; ++k16) {
+        const uint64_t adv = (uint64_t)((k16 * 32) >> 4);   // +32 bytes per k16
+        const uint32_t acc0 = (!first || k16 > 0) ? 1u : 0u;
+        tc_mma(dacc, ahi + adv, bhi + adv, idesc, acc0);
+        tc_mma(dacc, ahi + adv, blo + adv, idesc, 1u);
+        tc_mma(dacc, alo + adv, bhi + adv, idesc, 1u);
+      }
+      tc_commit(&empty[s]);   // stage s free once these MMAs complete
+    }
+    tc_commit(acc_full);      // accumulator complete (or abandoned)
+  } else if (warp >= 4) {
+    // weight producers: 8 strips of 16 rows per stage, two per warp
+    const int pw = warp - 4;
+    for (int kk = 0; kk < ksteps; ++kk) {
+      const int s = kk % kTcStages, round = kk / kTcStages;
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+        if (lane == 0) *flag = 1;
+        break;
+      }
+      uint8_t* st = stage_base + s * kStageBytes;
+      uint8_t* bhi = st + 2 * kTileHalf;
+      uint8_t* blo = st + 3 * kTileHalf;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int strip = pw * 2 + q;                 // 0..7 -> B rows 16*strip
+        const uint8_t* mat;
+        int wstrip;
+        if (MODE == 0) {
+          mat = (strip < 4 ? args.w0 : args.w1) + (size_t)e * args.mat_bytes;
+          wstrip = nt * 4 + (strip & 3);              // 64 F-rows per tile
+        } else {
+          mat = args.w0 + (size_t)e * args.mat_bytes;
+          wstrip = nt * 8 + strip;                    // 128 d-rows per tile
+        }
+        const uint8_t* tile = mat + ((size_t)wstrip * ksteps + kk) * Tr::kTileBytes;
+        dequant_tile_to_smem<QT>(tile, lane, bhi, blo, strip * 16);
+      }
+      fence_proxy_async_smem();   // generic stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_b[s]);
+    }
+  }
+
+  // epilogue: warps 0-3 own TMEM lanes 32w .. 32w+31 (= tile rows)
+  __syncwarp();
+  if (warp < 4) {
+    const bool ok = mbar_wait(acc_full, 0) && *flag == 0;
+    tc_fence_after();
+    const int r = 32 * warp + lane;
+    const int row = row0 + r;
+    const bool valid = ok && row < row_end;
+    const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
+    const int acc_used = ksteps < kTcAcc ? ksteps : kTcAcc;
+    if (!ok && lane == 0) set_status(args.status, MOE_STATUS_TIMEOUT);
+    if (MODE == 0) {
+      const float rs = valid ? args.row_scale[row] : 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {           // gate columns [32c, 32c+32), up [64+32c, ..)
+        float g[32], u[32];
+        tmem_ld_sum(taddr + 32 * c, g, acc_used);
+        tmem_ld_sum(taddr + 64 + 32 * c, u, acc_used);
+        if (valid) {
+          __half* hi = args.h_planes + (size_t)row * args.F + nt * 64 + 32 * c;
+          __half* lo = args.h_planes + ((size_t)args.P + row) * args.F + nt * 64 + 32 * c;
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float hv[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const float h = silu_f(g[j + q] * rs) * (u[j + q] * rs);
+              hv[q] = h * kTcHScale;
+              if (!(fabsf(hv[q]) <= 65504.f)) set_status(args.status, MOE_STATUS_ROW_OVERFLOW);
+            }
+            const __half2 hh = __floats2half2_rn(hv[0], hv[1]);
+            const float2 hf = __half22float2(hh);
+            reinterpret_cast<__half2*>(hi)[j / 2] = hh;
+            reinterpret_cast<__half2*>(lo)[j / 2] = __floats2half2_rn(hv[0] - hf.x, hv[1] - hf.y);
+          }
+        }
+      }
+    } else {
+      const int orow = valid ? (args.y_rows ? args.y_rows[row] : row) : 0;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld_sum(taddr + 32 * c, v, acc_used);
+        if (valid) {
+          float4* dst = reinterpret_cast<float4*>(args.y + (size_t)orow * args.d + nt * kTcN + 32 * c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(v[4 * j] * (1.f / kTcHScale), v[4 * j + 1] * (1.f / kTcHScale),
+                                 v[4 * j + 2] * (1.f / kTcHScale), v[4 * j + 3] * (1.f / kTcHScale));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTcCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D map over [rows][cols] fp16, box 128 rows x 64 cols, 128-byte swizzle.
+static int make_plane_map(CUtensorMap* map, const __half* base, int rows, int cols) {
+  EncodeTiledFn fn = encode_fn();
+  MOE_REQUIRE(fn, MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  MOE_REQUIRE(((uintptr_t)base & 15) == 0 && (cols * 2) % 16 == 0, MOE_ERR_INVALID,
+              "plane not 16-byte aligned");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kTcK, (cuuint32_t)kTcM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  MOE_REQUIRE(r == CUDA_SUCCESS, MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MOE_OK;
+}
+
+struct TcWs {
+  int* n_mtiles;
+  int* tile_e;
+  int* tile_r0;
+  float* row_scale;
+  __half* x_planes;   // [2][P][d]
+  __half* h_planes;   // [2][P][F]
+  size_t bytes;
+};
+
+static int tc_max_tiles(int rows, int E) { return (rows + kTcM - 1) / kTcM + E; }
+
+static TcWs carve_tc(void* ws, int rows, int E, int d, int F) {
+  Carve c{static_cast<uint8_t*>(ws), 0, 0};
+  TcWs w;
+  const int mt = tc_max_tiles(rows, E);
+  c.take<int>(64);  // status word
+  w.n_mtiles = c.take<int>(64);
+  w.tile_e = c.take<int>(mt);
+  w.tile_r0 = c.take<int>(mt);
+  w.row_scale = c.take<float>(rows);
+  w.x_planes = c.take<__half>((size_t)2 * rows * d);
+  w.h_planes = c.take<__half>((size_t)2 * rows * F);
+  w.bytes = align_up(c.used, 256);
+  return w;
+}
+
+size_t tc_workspace(int rows, int E, int d, int F) { return carve_tc(nullptr, rows, E, d, F).bytes; }
+
+bool tc_supported(int rows, int E, int d, int F) {
+  return rows > 0 && E <= 1024 && d % kTcN == 0 && F % 64 == 0 && d % kTcK == 0;
+}
+
+template <int QT>
+static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down,
+                     const int32_t* offsets, int E, int rows, const float* x,
+                     const int32_t* x_rows, int x_div, const float* x_row_max, int d, int F,
+                     float* y, const int32_t* y_rows, const TcWs& w, int* status,
+                     cudaStream_t s) {
+  using Tr = QTraits<QT>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  MOE_CUDA(cudaGetDevice(&dev));
+  if (!((attr_set >> (dev & 63)) & 1ull)) {
+    MOE_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<QT, 0>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+    MOE_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<QT, 1>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
+    attr_set |= 1ull << (dev & 63);
+  }
+  const int max_tiles = tc_max_tiles(rows, E);
+  {
+    ::moe::ProfScope _prof(MOE_K_PLAN, s);
+    tc_tile_plan_kernel<<<1, 1024, 0, s>>>(offsets, E, max_tiles, w.tile_e, w.tile_r0,
+                                           w.n_mtiles);
+  }
+  MOE_CHECK(check_launch("tc_tile_plan"));
+  {
+    ::moe::ProfScope _prof(MOE_K_XPREP, s);
+    tc_prep_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, x_rows, x_div, x_row_max, rows, d,
+                                                  w.row_scale, w.x_planes);
+  }
+  MOE_CHECK(check_launch("tc_prep"));
+  CUtensorMap xmap, hmap;
+  MOE_CHECK(make_plane_map(&xmap, w.x_planes, 2 * rows, d));
+  MOE_CHECK(make_plane_map(&hmap, w.h_planes, 2 * rows, F));
+  const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
+  TcArgs a1 = {};
+  a1.w0 = w_gate;
+  a1.w1 = w_up;
+  a1.mat_bytes = mat_bytes;
+  a1.K = d;
+  a1.n_tiles_n = F / 64;
+  a1.P = rows;
+  a1.F = F;
+  a1.d = d;
+  a1.offsets = offsets;
+  a1.tile_e = w.tile_e;
+  a1.tile_r0 = w.tile_r0;
+  a1.n_mtiles = w.n_mtiles;
+  a1.row_scale = w.row_scale;
+  a1.h_planes = w.h_planes;
+  a1.status = status;
+  {
+    ::moe::ProfScope _prof(MOE_K_GATEUP, s);
+    tc_gemm_kernel<QT, 0><<<max_tiles * a1.n_tiles_n, kTcThreads, kTcSmem, s>>>(xmap, a1);
+  }
+  MOE_CHECK(check_launch("tc_gemm gate/up"));
+  TcArgs a2 = a1;
+  a2.w0 = w_down;
+  a2.w1 = nullptr;
+  a2.K = F;
+  a2.n_tiles_n = d / kTcN;
+  a2.y = y;
+  a2.y_rows = y_rows;
+  {
+    ::moe::ProfScope _prof(MOE_K_DOWN, s);
+    tc_gemm_kernel<QT, 1><<<max_tiles * a2.n_tiles_n, kTcThreads, kTcSmem, s>>>(hmap, a2);
+  }
+  return check_launch("tc_gemm down");
+}
+
+int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                   const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
+                   int x_div, const float* x_row_max, int d, int F, float* y,
+                   const int32_t* y_rows, void* ws, size_t ws_bytes, int* status,
+                   cudaStream_t s) {
+  MOE_REQUIRE(tc_supported(rows, E, d, F), MOE_ERR_UNSUPPORTED, "tensor-core path shape");
+  TcWs w = carve_tc(ws, rows, E, d, F);
+  MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "tensor-core workspace %zu < %zu",
+              ws_bytes, w.bytes);
+  if (!status) status = static_cast<int*>(ws);
+  if (qtype == MOE_Q4_0)
+    return launch_tc<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
+                               x_row_max, d, F, y, y_rows, w, status, s);
+  return launch_tc<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div, x_row_max,
+                             d, F, y, y_rows, w, status, s);
+}
+
+}  // namespace moe

@@ -127,7 +127,10 @@ def test_dispatch_flags_bad_expert_ids():
 
 @pytest.mark.parametrize("qt", [2, 8])
 @pytest.mark.parametrize("d,F,n", [(256, 128, 1), (256, 128, 3), (1024, 2816, 4), (2816, 704, 5),
-                                   (512, 192, 17), (2816, 704, 40), (128, 64, 2)])
+                                   (512, 192, 17), (2816, 704, 40), (128, 64, 2),
+                                   # >= 64 rows: the tcgen05 GEMM path
+                                   (256, 128, 64), (2816, 704, 300), (1024, 2816, 130),
+                                   (512, 192, 257)])
 def test_single_expert_matches_oracle(qt, d, F, n):
     rng = np.random.default_rng(d + F + n + qt)
     s = 0.002 if qt == 8 else 0.01
