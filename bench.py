@@ -299,8 +299,6 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    _lib.profile_collect()
-    _lib.profile_enable(True)
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             flush.zero_()
@@ -308,7 +306,20 @@ def run_b200(args):
             step()
             ends[i].record()
         torch.cuda.synchronize()
-    _lib.profile_enable(False)
+        # per-kernel device times: the same steps again with an event pair
+        # around every library launch (kept out of the timed steps above,
+        # because events between two kernels stop the second one from
+        # starting early as a programmatic dependent launch)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        _lib.profile_collect()
+        _lib.profile_enable(True)
+        for i in range(args.steps):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        _lib.profile_enable(False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -355,34 +366,54 @@ def run_b200(args):
     bb = synth.block_bytes(cfg.qtype)
     d, F = cfg.d_model, cfg.ffn
     mat = F * d // 32 * bb
-    # gate/up kernel: both matrices of every routed expert, the activation
-    # rows it reads and the hidden rows it writes
-    gu_bytes = uniq * 2 * mat + rows * d * 4 + rows * F * 4
-    dn_bytes = uniq * mat + rows * F * 4 + rows * d * 4
     gu_ms, gu_n = prof["gateup"]
     dn_ms, dn_n = prof["down"]
     kernels = {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof.items() if v[1]}
-    if gu_n:
-        gu_launch_ms = gu_ms / gu_n
-        achieved = gu_bytes / (gu_launch_ms / 1e3) / 1e9
-    else:
-        gu_launch_ms, achieved = None, None
-    traffic = ncu_traffic(args.workload, "gateup")
+    gu_launch_ms = gu_ms / gu_n if gu_n else None
+    dn_launch_ms = dn_ms / dn_n if dn_n else None
     layer_bytes = uniq * 3 * mat + d * cfg.n_experts * 4 + T * d * 8  # this rank's share
-    roofline = {
-        "kernel": "gateup (grouped gate/up GEMV + SiLU*up)",
-        "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-        "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-        "peak_kind": f"{peak_kind} hbm_gbs",
-        "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_launch_ms,
-        "layer": {"algorithmic_bytes": layer_bytes, "ms": ms,
-                  "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9,
-                  "frac": layer_bytes / (ms / 1e3) / 1e9 / hbm_peak},
-    }
-    if dn_n:
-        roofline["down"] = {"algorithmic_bytes_per_launch": dn_bytes,
-                            "launch_ms": dn_ms / dn_n,
-                            "achieved": dn_bytes / (dn_ms / dn_n / 1e3) / 1e9}
+    tensor_bound = rows / max(1, uniq) >= 64      # the tcgen05 GEMM path
+    if tensor_bound:
+        # gate/up GEMM: 2 * rows * d * 2F algorithmic flops (the three split-operand
+        # MMAs that keep f32 accuracy are implementation work, not counted)
+        gu_work = 2.0 * rows * d * 2 * F
+        dn_work = 2.0 * rows * F * d
+        achieved = gu_work / (gu_launch_ms / 1e3) / 1e12 if gu_launch_ms else None
+        roofline = {
+            "kernel": "tc_gemm gate/up (tcgen05 grouped GEMM + SiLU*up)",
+            "bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+            "frac": (achieved / tc_peak) if achieved else None,
+            "traffic": ncu_traffic(args.workload, "gateup"),
+            "peak_kind": f"{peak_kind} bf16_tflops (dense)",
+            "algorithmic_flops_per_launch": gu_work, "launch_ms": gu_launch_ms,
+            "executed_tensor_flops_per_launch": 3 * gu_work,
+            "layer": {"algorithmic_flops": gu_work + dn_work, "ms": ms,
+                      "achieved_tflops": (gu_work + dn_work) / (ms / 1e3) / 1e12},
+        }
+        if dn_n:
+            roofline["down"] = {"algorithmic_flops_per_launch": dn_work, "launch_ms": dn_launch_ms,
+                                "achieved_tflops": dn_work / (dn_launch_ms / 1e3) / 1e12}
+    else:
+        # gate/up GEMV: both matrices of every routed expert, the activation rows
+        # it reads and the hidden rows it writes
+        gu_bytes = uniq * 2 * mat + rows * d * 4 + rows * F * 4
+        dn_bytes = uniq * mat + rows * F * 4 + rows * d * 4
+        achieved = gu_bytes / (gu_launch_ms / 1e3) / 1e9 if gu_launch_ms else None
+        roofline = {
+            "kernel": "gateup (grouped gate/up GEMV + SiLU*up)",
+            "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+            "frac": (achieved / hbm_peak) if achieved else None,
+            "traffic": ncu_traffic(args.workload, "gateup"),
+            "peak_kind": f"{peak_kind} hbm_gbs",
+            "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_launch_ms,
+            "layer": {"algorithmic_bytes": layer_bytes, "ms": ms,
+                      "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9,
+                      "frac": layer_bytes / (ms / 1e3) / 1e9 / hbm_peak},
+        }
+        if dn_n:
+            roofline["down"] = {"algorithmic_bytes_per_launch": dn_bytes,
+                                "launch_ms": dn_launch_ms,
+                                "achieved": dn_bytes / (dn_launch_ms / 1e3) / 1e9}
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -411,6 +442,7 @@ def run_b200(args):
                    "weights_bytes_resident": 3 * cfg.n_experts * mat},
         "roofline": roofline,
         "kernels": kernels,
+        "kernels_timing": "event pair per launch, in a second pass of the same steps",
         "cpu_baseline": cpu_base,
         "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(x_host.numel() * 4),

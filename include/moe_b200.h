@@ -77,7 +77,7 @@ int moe_read_status(const void* workspace, int* status_out, moe_stream_t stream)
  * per kernel id, the summed device milliseconds and the number of launches,
  * then resets.  Do not enable while capturing a CUDA graph. */
 enum {
-  MOE_K_ROUTER_PARTIAL = 0, MOE_K_ROUTER_SELECT, MOE_K_DISPATCH, MOE_K_PLAN, MOE_K_XPREP,
+  MOE_K_ROUTER = 0, MOE_K_ROUTER_SELECT, MOE_K_DISPATCH, MOE_K_PLAN, MOE_K_XPREP,
   MOE_K_GATEUP, MOE_K_DOWN, MOE_K_COMBINE, MOE_K_RMS_NORM, MOE_K_PACK, MOE_K_DEQUANT,
   MOE_K_AUX, MOE_K_COUNT
 };

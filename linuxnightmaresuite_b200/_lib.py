@@ -75,7 +75,7 @@ SIGNATURES = {
 }
 
 
-KERNEL_NAMES = ["router_partial", "router_select", "dispatch", "plan", "xprep", "gateup", "down",
+KERNEL_NAMES = ["router", "router_select", "dispatch", "plan", "xprep", "gateup", "down",
                 "combine", "rms_norm", "pack", "dequant", "aux"]
 
 

@@ -5,11 +5,14 @@
 
 namespace moe {
 
-// One CTA per token.  moe_forward.py:165-172: output = 0; output += w * y_e in
-// router order; output += shared; then the caller's residual add
-// (moe_forward.py:359, x = x + ffn_out).  Multiply and add are rounded
-// separately, as numpy evaluates them.
-__global__ void __launch_bounds__(256)
+// CTA (token t, column slice blockIdx.y of kCombineThreads float4s).
+// moe_forward.py:165-172: output = 0; output += w * y_e in router order;
+// output += shared; then the caller's residual add (moe_forward.py:359,
+// x = x + ffn_out).  Multiply and add are rounded separately, as numpy
+// evaluates them.
+constexpr int kCombineThreads = 128;
+
+__global__ void __launch_bounds__(kCombineThreads)
 combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm,
                const float* __restrict__ w, const float* __restrict__ shared,
                const float* __restrict__ residual, int k, int d, float* __restrict__ out) {
@@ -21,7 +24,8 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm
     wts[threadIdx.x] = w[(size_t)t * k + threadIdx.x];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
+  for (int i = blockIdx.y * kCombineThreads + threadIdx.x; i < d / 4;
+       i += gridDim.y * kCombineThreads) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int q0 = 0; q0 < k; q0 += 8) {
       float4 v[8];
@@ -84,7 +88,9 @@ int launch_combine(const float* y, const int32_t* inv_perm, const float* w, cons
   if (T == 0) return MOE_OK;
   {
     ::moe::ProfScope _prof(MOE_K_COMBINE, s);
-    combine_kernel<<<T, 256, 0, s>>>(y, inv_perm, w, shared, residual, k, d, out);
+    const int slices = (d / 4 + kCombineThreads - 1) / kCombineThreads;
+    combine_kernel<<<dim3(T, slices), kCombineThreads, 0, s>>>(y, inv_perm, w, shared, residual,
+                                                               k, d, out);
   }
   return check_launch("combine");
 }

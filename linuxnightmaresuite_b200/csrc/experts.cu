@@ -5,16 +5,22 @@
 //
 // Kernels, per call:
 //   plan_kernel    active-expert list and 4-row group offsets from expert_offsets
-//   xprep_kernel   gathers each expert's rows, scales each row by a power of two
-//                  and splits it into fp16 hi + lo parts, laid out as m16n8k16
-//                  B fragments (4 rows x {hi, lo} = the 8 MMA columns)
-//   gateup_kernel  streams packed W_gate / W_up tiles with 128-bit loads,
-//                  dequantises them in registers to exact fp16 integers, runs
-//                  one pair of MMAs per 32-weight block into a zeroed
-//                  accumulator and adds it, times the block's fp16 scale, to the
-//                  fp32 running sum (so the weights are exact and only the
-//                  activations are split); SiLU(gate) * up in the epilogue,
-//                  written as fragments for the next GEMV
+//   gateup_kernel  gathers its expert's rows into shared memory, scales each by
+//                  a power of two and splits it into fp16 hi + lo parts laid out
+//                  as m16n8k16 B fragments (4 rows x {hi, lo} = the 8 MMA
+//                  columns) plus one offset correction per block and column
+//                  (below), while the first weight stages are already in
+//                  flight; then streams packed W_gate / W_up tiles with 128-bit
+//                  loads and
+//                  turns each quant into an fp16 subnormal with a bare mask
+//                  (Q4_0 nibble n -> n * 2^-24, Q8_0 byte q + 128 -> (q+128) *
+//                  2^-24): the tensor core multiplies those exactly, and the
+//                  missing "- 8" / "- 128" offset enters as the accumulator's
+//                  initial value, -offset * 2^-24 * (sum of the block's
+//                  activations).  One pair of MMAs per 32-weight block, then the
+//                  block, times its fp16 scale, is added to the fp32 running
+//                  sum; the 2^24 comes back with the row scale.  SiLU(gate) * up
+//                  in the epilogue, written as fragments for the next GEMV
 //   down_kernel    the same for W_down, writing f32 rows of y
 // The fp16 hi/lo split keeps ~22 bits of each activation, which is what the
 // reference's f32 tolerance needs; a single fp16 rounding does not.
@@ -28,6 +34,16 @@ namespace moe {
 
 constexpr int kMaxCG = 4;                 // column groups (4 rows each) per pass
 constexpr float kHScale = 1.0f / 256.0f;  // hidden activations are stored / 256
+constexpr float kSubUnit = 16777216.0f;   // 2^24: one fp16 subnormal step
+// Activation block record in shared memory: 512 B of fragments, then the
+// offset corrections as one f32x4 accumulator quad per lane column t
+// ({C[2t], C[2t+1], C[2t], C[2t+1]}), then 16 B of padding so that records of
+// consecutive blocks start on different banks.
+constexpr int kXRec = 592;
+
+// quant offset removed by the subnormal dequantisation
+template <int QT>
+__host__ __device__ constexpr float quant_offset() { return QT == MOE_Q4_0 ? 8.f : 128.f; }
 constexpr int kPlanThreads = 1024;
 
 __device__ __forceinline__ float half_lo(uint32_t v) {
@@ -94,82 +110,6 @@ plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups
 }
 
 // ---------------------------------------------------------------------------
-// xprep: one CTA of 4 warps per 4-row group; warp w handles row w of the group
-// ---------------------------------------------------------------------------
-template <int QT>
-__global__ void __launch_bounds__(128)
-xprep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
-             const float* __restrict__ x_row_max, const int32_t* __restrict__ offsets,
-             const int* __restrict__ goff, const int* __restrict__ gexp, int E, int d,
-             float* __restrict__ row_scale, uint8_t* __restrict__ xfrag) {
-  const int G = blockIdx.x;
-  if (G >= goff[E]) return;
-  const int e = gexp[G];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = offsets[e] + 4 * (G - goff[e]) + warp;
-  const bool valid = r < offsets[e + 1];
-  const int nb = d / 32;
-  uint8_t* gbase = xfrag + (size_t)G * nb * 512 + warp * 64;
-  if (!valid) {
-    for (int b = lane; b < nb; b += 32) {
-      uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int q = 0; q < 8; ++q)  // 2 parts x 4 lane-columns
-        *reinterpret_cast<uint4*>(gbase + (size_t)b * 512 + (q >> 2) * 256 + (q & 3) * 16) = z;
-    }
-    return;
-  }
-  const int src_row = x_rows ? x_rows[r] / x_div : r;
-  const float4* src = reinterpret_cast<const float4*>(x + (size_t)src_row * d);
-  float m = 0.f;
-  if (x_row_max) {
-    m = x_row_max[src_row];
-  } else {
-    for (int i = lane; i < d / 4; i += 32) {
-      float4 v = __ldg(src + i);
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  }
-  float scale = 1.f, inv = 1.f;
-  if (m > 0.f && isfinite(m)) {
-    int ex = ilogbf(m);
-    scale = ldexpf(1.f, 14 - ex);   // max |x| * scale in [2^14, 2^15)
-    inv = ldexpf(1.f, ex - 14);
-  }
-  if (lane == 0) row_scale[r] = inv;
-  for (int b = lane; b < nb; b += 32) {
-    float v[32];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float4 f = __ldg(src + b * 8 + q);
-      v[4 * q + 0] = f.x * scale;
-      v[4 * q + 1] = f.y * scale;
-      v[4 * q + 2] = f.z * scale;
-      v[4 * q + 3] = f.w * scale;
-    }
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      uint32_t hi[4], lo[4];
-#pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        float a = v[frag_elem_c<QT>(t, i)];
-        float c = v[frag_elem_c<QT>(t, i + 1)];
-        __half ha = __float2half_rn(a), hc = __float2half_rn(c);
-        __half la = __float2half_rn(a - __half2float(ha));
-        __half lc = __float2half_rn(c - __half2float(hc));
-        hi[i / 2] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hc) << 16);
-        lo[i / 2] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lc) << 16);
-      }
-      uint8_t* dst = gbase + (size_t)b * 512 + t * 16;
-      *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(dst + 256) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
 // tile fragments
 // ---------------------------------------------------------------------------
 template <int QT>
@@ -188,16 +128,41 @@ __device__ __forceinline__ void lds_tile(TileRegs<QT>& r, const uint8_t* tile, i
   r.sc = *reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + (lane >> 2) * 8);
 }
 
-// A fragments of both k16 steps for block b (rows g and g+8), block scales
-template <int QT>
+// Q4_0 quant word -> four fp16x2 subnormals: low nibbles n * 2^-24, high
+// nibbles 16 n * 2^-24 (paired with activations stored / 16).
+__device__ __forceinline__ void dequant_q4_sub(uint32_t w, uint32_t& lo01, uint32_t& lo23,
+                                               uint32_t& hi01, uint32_t& hi23) {
+  const uint32_t w8 = w >> 8;
+  lo01 = w & 0x000F000Fu;
+  lo23 = w8 & 0x000F000Fu;
+  hi01 = w & 0x00F000F0u;
+  hi23 = w8 & 0x00F000F0u;
+}
+
+// Q8_0 quant word -> two fp16x2 subnormals (q + 128) * 2^-24.
+__device__ __forceinline__ void dequant_q8_sub(uint32_t w, uint32_t& h01, uint32_t& h23) {
+  const uint32_t u = w ^ 0x80808080u;
+  h01 = prmt(u, 0u, 0x4140u);
+  h23 = prmt(u, 0u, 0x4342u);
+}
+
+// A fragments of both k16 steps for block b (rows g and g+8), block scales.
+// SUB: subnormal quants (offset handled by the accumulator's initial value);
+// otherwise exact signed fp16 integers.
+template <int QT, bool SUB>
 __device__ __forceinline__ void tile_afrags(const TileRegs<QT>& r, int b, uint32_t (&a0)[4],
                                             uint32_t (&a1)[4], float2& dg, float2& dg8) {
   if (QT == MOE_Q4_0) {
     uint32_t wg = b ? r.q[0].y : r.q[0].x;
     uint32_t w8 = b ? r.q[0].w : r.q[0].z;
     uint32_t l01, l23, h01, h23, m01, m23, n01, n23;
-    dequant_q4(wg, l01, l23, h01, h23);
-    dequant_q4(w8, m01, m23, n01, n23);
+    if (SUB) {
+      dequant_q4_sub(wg, l01, l23, h01, h23);
+      dequant_q4_sub(w8, m01, m23, n01, n23);
+    } else {
+      dequant_q4(wg, l01, l23, h01, h23);
+      dequant_q4(w8, m01, m23, n01, n23);
+    }
     a0[0] = l01; a0[1] = m01; a0[2] = l23; a0[3] = m23;
     a1[0] = h01; a1[1] = n01; a1[2] = h23; a1[3] = n23;
   } else {
@@ -206,11 +171,21 @@ __device__ __forceinline__ void tile_afrags(const TileRegs<QT>& r, int b, uint32
     uint32_t g0 = b ? qa.z : qa.x, g1 = b ? qa.w : qa.y;
     uint32_t e0 = b ? qb.z : qb.x, e1 = b ? qb.w : qb.y;
     uint32_t x01, x23, y01, y23;
-    dequant_q8(g0, x01, x23);
-    dequant_q8(e0, y01, y23);
+    if (SUB) {
+      dequant_q8_sub(g0, x01, x23);
+      dequant_q8_sub(e0, y01, y23);
+    } else {
+      dequant_q8(g0, x01, x23);
+      dequant_q8(e0, y01, y23);
+    }
     a0[0] = x01; a0[1] = y01; a0[2] = x23; a0[3] = y23;
-    dequant_q8(g1, x01, x23);
-    dequant_q8(e1, y01, y23);
+    if (SUB) {
+      dequant_q8_sub(g1, x01, x23);
+      dequant_q8_sub(e1, y01, y23);
+    } else {
+      dequant_q8(g1, x01, x23);
+      dequant_q8(e1, y01, y23);
+    }
     a1[0] = x01; a1[1] = y01; a1[2] = x23; a1[3] = y23;
   }
   const float s0 = b ? half_hi(r.sc.x) : half_lo(r.sc.x);
@@ -219,14 +194,16 @@ __device__ __forceinline__ void tile_afrags(const TileRegs<QT>& r, int b, uint32
   dg8 = make_float2(s8, s8);
 }
 
-// One 32-weight block: two k16 MMAs into a fresh accumulator, then
-// acc += scale * block (packed f32x2 FMA).  acc[0]: row g, acc[1]: row g+8.
+// One 32-weight block: two k16 MMAs into an accumulator that starts at c0
+// (zero, or the offset corrections of the lane's two columns for rows g and
+// g+8), then acc += scale * block (packed f32x2 FMA).  acc[0]: row g,
+// acc[1]: row g+8.
 __device__ __forceinline__ void block_mma(float2 (&acc)[2], const uint32_t (&a0)[4],
-                                          const uint32_t (&a1)[4], uint4 xf, float2 dg,
+                                          const uint32_t (&a1)[4], uint4 xf, float4 c0, float2 dg,
                                           float2 dg8) {
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+  const float init[4] = {c0.x, c0.y, c0.z, c0.w};
   float tmp[4];
-  mma_16816(tmp, a0[0], a0[1], a0[2], a0[3], xf.x, xf.y, zero);
+  mma_16816(tmp, a0[0], a0[1], a0[2], a0[3], xf.x, xf.y, init);
   mma_16816(tmp, a1[0], a1[1], a1[2], a1[3], xf.z, xf.w, tmp);
   acc[0] = __ffma2_rn(dg, make_float2(tmp[0], tmp[1]), acc[0]);
   acc[1] = __ffma2_rn(dg8, make_float2(tmp[2], tmp[3]), acc[1]);
@@ -248,6 +225,7 @@ constexpr int kDnWarps = 8;             // warps per down CTA
 constexpr int kBarArea = 1024;          // mbarriers: 1 + warps x stages, 8 B each
 constexpr int kMaxSmem = 227 * 1024;    // dynamic shared memory per CTA on sm_100
 __host__ __device__ inline int x_stage_bytes(int K, int cgp) { return cgp * (K / 32) * 512; }
+__host__ __device__ inline int gu_x_stage_bytes(int K, int cgp) { return cgp * (K / 32) * kXRec; }
 
 template <int QT>
 __host__ __device__ constexpr int gu_stage_bytes() {
@@ -264,44 +242,58 @@ struct GuCtx {
   const uint8_t* ubase;   // ... of W_up
   uint8_t* ring;          // this warp's stages
   uint64_t* bars;         // this warp's stage barriers
-  uint64_t* xbar;         // activation-stage barrier
   const uint8_t* xs;      // activation fragments (shared)
+  const float* rs;        // row scales of the chunk's rows (shared)
   uint8_t* hfrag;
-  const float* row_scale;
   int* status;
   uint64_t pol;
   int nst, jb, ntile, nbx, nbF, ks, kp, s, row0, n, G0, lane;
   bool strip_ok;
 };
 
+// Stage q of this warp's (gate, up) tiles into ring slot `slot` (lane 0).
+template <int QT>
+__device__ __forceinline__ void gu_issue(const GuCtx& c, int q, int slot) {
+  using Tr = QTraits<QT>;
+  constexpr int U = Ring<QT>::kGuU;
+  constexpr int TB = Tr::kTileBytes;
+  constexpr int SB = U * TB;
+  const int t0 = q * U;
+  const uint32_t bytes = (uint32_t)(min(U, c.ntile - t0) * TB);
+  uint8_t* st = c.ring + slot * 2 * SB;
+  mbar_expect_tx(&c.bars[slot], 2 * bytes);
+  bulk_g2s(st, c.gbase + (size_t)(c.jb + t0) * TB, bytes, &c.bars[slot], c.pol);
+  bulk_g2s(st + SB, c.ubase + (size_t)(c.jb + t0) * TB, bytes, &c.bars[slot], c.pol);
+}
+
+// First stages of a chunk, issued before the activations are built.
+template <int QT>
+__device__ __forceinline__ void gu_prefetch(const GuCtx& c) {
+  constexpr int U = Ring<QT>::kGuU;
+  const int nstage = (c.ntile + U - 1) / U;
+  if (c.lane == 0 && c.strip_ok) {
+    fence_proxy_async_smem();
+    for (int q = 0; q < min(c.nst, nstage); ++q) gu_issue<QT>(c, q, q);
+  }
+}
+
 // Streams this warp's tiles through its ring for one chunk of NCG column
 // groups.  Lane 0 keeps up to nst stages of U (gate, up) tile pairs in flight
-// with bulk copies; every lane reads its fragments of a whole stage from shared
-// memory, releases the stage, then computes.  False if a wait timed out.
+// with bulk copies (the first ones from gu_prefetch); every lane reads its
+// fragments of a whole stage from shared memory, releases the stage, then
+// computes.  False if a wait timed out.
 template <int QT, int NCG>
 __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)[NCG][2],
-                                          const GuCtx& c, uint32_t& parity, uint32_t xparity) {
+                                          const GuCtx& c, uint32_t& parity) {
   using Tr = QTraits<QT>;
   constexpr int U = Ring<QT>::kGuU;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SB = U * TB;
   constexpr int STAGE = 2 * SB;
   const int nstage = (c.ntile + U - 1) / U;
-  auto issue = [&](int q, int slot) {
-    const int t0 = q * U;
-    const uint32_t bytes = (uint32_t)(min(U, c.ntile - t0) * TB);
-    uint8_t* st = c.ring + slot * STAGE;
-    mbar_expect_tx(&c.bars[slot], 2 * bytes);
-    bulk_g2s(st, c.gbase + (size_t)(c.jb + t0) * TB, bytes, &c.bars[slot], c.pol);
-    bulk_g2s(st + SB, c.ubase + (size_t)(c.jb + t0) * TB, bytes, &c.bars[slot], c.pol);
-  };
-  if (c.lane == 0) {
-    fence_proxy_async_smem();
-    for (int q = 0; q < min(c.nst, nstage); ++q) issue(q, q);
-  }
-  if (!mbar_wait(c.xbar, xparity)) return false;
-  const int cs = c.nbx * 512;
-  const uint8_t* xq = c.xs + c.lane * 16 + c.jb * 1024;
+  const int cs = c.nbx * kXRec;
+  const uint8_t* xq = c.xs + c.lane * 16 + c.jb * 2 * kXRec;
+  const uint8_t* cq = c.xs + 512 + (c.lane & 3) * 16 + c.jb * 2 * kXRec;
   int slot = 0;
   for (int q = 0; q < nstage; ++q) {
     if (!mbar_wait(&c.bars[slot], (parity >> slot) & 1u)) return false;
@@ -319,7 +311,7 @@ __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)
     __syncwarp();
     if (c.lane == 0 && q + c.nst < nstage) {
       fence_proxy_async_smem();
-      issue(q + c.nst, slot);
+      gu_issue<QT>(c, q + c.nst, slot);
     }
     slot = (slot + 1 == c.nst) ? 0 : slot + 1;
 #pragma unroll
@@ -329,18 +321,21 @@ __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)
         for (int b = 0; b < 2; ++b) {
           uint32_t ga0[4], ga1[4], ua0[4], ua1[4];
           float2 dg, dg8, du, du8;
-          tile_afrags<QT>(tg[u], b, ga0, ga1, dg, dg8);
-          tile_afrags<QT>(tu[u], b, ua0, ua1, du, du8);
+          tile_afrags<QT, true>(tg[u], b, ga0, ga1, dg, dg8);
+          tile_afrags<QT, true>(tu[u], b, ua0, ua1, du, du8);
 #pragma unroll
           for (int cg = 0; cg < NCG; ++cg) {
-            const uint4 xf = *reinterpret_cast<const uint4*>(xq + cg * cs + u * 1024 + b * 512);
-            block_mma(accg[cg], ga0, ga1, xf, dg, dg8);
-            block_mma(accu[cg], ua0, ua1, xf, du, du8);
+            const int off = cg * cs + (2 * u + b) * kXRec;
+            const uint4 xf = *reinterpret_cast<const uint4*>(xq + off);
+            const float4 c0 = *reinterpret_cast<const float4*>(cq + off);
+            block_mma(accg[cg], ga0, ga1, xf, c0, dg, dg8);
+            block_mma(accu[cg], ua0, ua1, xf, c0, du, du8);
           }
         }
       }
     }
-    xq += U * 1024;
+    xq += U * 2 * kXRec;
+    cq += U * 2 * kXRec;
   }
   return true;
 }
@@ -349,21 +344,17 @@ __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)
 // warps of a strip (rank order), SiLU(gate) * up epilogue into hidden
 // fragments.  Called uniformly by every warp of the CTA.
 template <int QT, int NCG>
-__device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, uint32_t xparity,
-                                         int c0, bool ok) {
+__device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, int c0, bool ok) {
   float2 accg[NCG][2], accu[NCG][2];
 #pragma unroll
   for (int cg = 0; cg < NCG; ++cg)
 #pragma unroll
     for (int i = 0; i < 2; ++i) accg[cg][i] = accu[cg][i] = make_float2(0.f, 0.f);
   if (c.strip_ok && ok) {
-    if (!gu_stream<QT, NCG>(accg, accu, c, parity, xparity)) {
+    if (!gu_stream<QT, NCG>(accg, accu, c, parity)) {
       set_status(c.status, MOE_STATUS_TIMEOUT);
       ok = false;
     }
-  } else if (!mbar_wait(c.xbar, xparity)) {
-    set_status(c.status, MOE_STATUS_TIMEOUT);
-    ok = false;
   }
   const int lane = c.lane;
   if (c.ks > 1) {
@@ -417,7 +408,7 @@ __device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, uint3
           const int rig = 2 * t + ci;              // row inside the group
           const int tok = c0 + 4 * cg + rig;
           if (tok >= c.n) continue;
-          const float rs = c.row_scale[c.row0 + tok];
+          const float rs = c.rs[4 * cg + rig] * kSubUnit;
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
             const float gacc = ci ? accg[cg][rr].y : accg[cg][rr].x;
@@ -443,28 +434,144 @@ __device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, uint3
 }
 
 // ---------------------------------------------------------------------------
+// Activations of one chunk (ncg groups of 4 rows, from row c0 of the expert)
+// -> shared fragment records, plus each row's scale.  Rows past the expert's
+// end are zero.  Each row is scaled by a power of two so that its max |x|
+// lands in [2^14, 2^15), then split into fp16 hi + lo; for Q4_0 the high-nibble
+// half of every block is stored / 16 (exact: it meets nibbles that a bare mask
+// leaves 16x too large).  The correction of column n (hi or lo part of a row)
+// is -offset * 2^-24 * the block's sum of that part as the MMA sees it.
+template <int QT>
+__device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rmax,
+                                              const float* __restrict__ x,
+                                              const int32_t* __restrict__ x_rows, int x_div,
+                                              const float* __restrict__ x_row_max, int row0,
+                                              int c0, int n, int ncg, int d) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NT = kGuWarps * 32;
+  const int nb = d / 32;
+  const int nrows = 4 * ncg;
+  auto src_of = [&](int rr) -> const float* {
+    const int r = row0 + c0 + rr;
+    const int sr = x_rows ? x_rows[r] / x_div : r;
+    return x + (size_t)sr * d;
+  };
+  if (x_row_max) {
+    if (tid < nrows) {
+      const int r = row0 + c0 + tid;
+      rmax[tid] = c0 + tid < n ? x_row_max[x_rows ? x_rows[r] / x_div : r] : 0.f;
+    }
+  } else {
+    for (int rr = warp; rr < nrows; rr += kGuWarps) {
+      float m = 0.f;
+      if (c0 + rr < n) {
+        const float4* src = reinterpret_cast<const float4*>(src_of(rr));
+        for (int i = lane; i < d / 4; i += 32) {
+          const float4 v = __ldg(src + i);
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) rmax[rr] = m;
+    }
+  }
+  __syncthreads();
+  if (tid < nrows) {
+    const float m = rmax[tid];
+    float inv = 1.f;
+    if (m > 0.f && isfinite(m)) inv = ldexpf(1.f, ilogbf(m) - 14);
+    rs[tid] = inv;
+  }
+  const float k = -quant_offset<QT>() / kSubUnit;
+  for (int it = tid; it < nrows * nb; it += NT) {
+    const int rr = it / nb, b = it - rr * nb;
+    const int cg = rr >> 2, w = rr & 3;
+    uint8_t* rec = xs + (size_t)(cg * nb + b) * kXRec;
+    float* cor = reinterpret_cast<float*>(rec + 512);
+    if (c0 + rr >= n) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<uint4*>(rec + (q >> 2) * 256 + w * 64 + (q & 3) * 16) =
+            make_uint4(0, 0, 0, 0);
+      cor[4 * (w >> 1) + (w & 1)] = 0.f;
+      cor[4 * (w >> 1) + (w & 1) + 2] = 0.f;
+      cor[4 * (2 + (w >> 1)) + (w & 1)] = 0.f;
+      cor[4 * (2 + (w >> 1)) + (w & 1) + 2] = 0.f;
+      continue;
+    }
+    const float m = rmax[rr];
+    float scale = 1.f;
+    if (m > 0.f && isfinite(m)) scale = ldexpf(1.f, 14 - ilogbf(m));
+    const float4* src = reinterpret_cast<const float4*>(src_of(rr)) + b * 8;
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 f = __ldg(src + q);
+      v[4 * q + 0] = f.x * scale;
+      v[4 * q + 1] = f.y * scale;
+      v[4 * q + 2] = f.z * scale;
+      v[4 * q + 3] = f.w * scale;
+    }
+    float sum_hi = 0.f, sum_lo = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const float div = (QT == MOE_Q4_0 && i >= 4) ? 0.0625f : 1.0f;
+        const float mul = (QT == MOE_Q4_0 && i >= 4) ? 16.0f : 1.0f;
+        const float a = v[frag_elem_c<QT>(t, i)] * div;
+        const float c = v[frag_elem_c<QT>(t, i + 1)] * div;
+        const __half ha = __float2half_rn(a), hc = __float2half_rn(c);
+        const __half la = __float2half_rn(a - __half2float(ha));
+        const __half lc = __float2half_rn(c - __half2float(hc));
+        sum_hi += mul * (__half2float(ha) + __half2float(hc));
+        sum_lo += mul * (__half2float(la) + __half2float(lc));
+        hi[i / 2] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hc) << 16);
+        lo[i / 2] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lc) << 16);
+      }
+      uint8_t* dst = rec + w * 64 + t * 16;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(dst + 256) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    // column w (hi part) sits in lane column t = w / 2, column 4 + w (lo part)
+    // in t = 2 + w / 2; each appears for rows g and g + 8 of the quad
+    cor[4 * (w >> 1) + (w & 1)] = k * sum_hi;
+    cor[4 * (w >> 1) + (w & 1) + 2] = k * sum_hi;
+    cor[4 * (2 + (w >> 1)) + (w & 1)] = k * sum_lo;
+    cor[4 * (2 + (w >> 1)) + (w & 1) + 2] = k * sum_lo;
+  }
+}
+
 // gate / up: CTA = 16 warps = (16 / ks) strips of 16 F-rows x ks K-slices of
-// one expert.  The expert's activation fragments for the chunk (cgp groups of
-// 4 rows, hi + lo) are staged once per CTA with a single bulk copy.
+// one expert.  Per chunk of up to cgp groups of 4 rows, every warp first starts
+// its weight ring, then the CTA builds the chunk's activation fragments.
 // ---------------------------------------------------------------------------
 template <int QT>
 __global__ void __launch_bounds__(kGuWarps * 32, 1)
 gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t mat_bytes,
               int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
               const int* __restrict__ active, const int* __restrict__ goff,
-              const float* __restrict__ row_scale, const uint8_t* __restrict__ xfrag,
-              uint8_t* __restrict__ hfrag, int ks, int cgp, int nst, int* __restrict__ status) {
+              const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
+              const float* __restrict__ x_row_max, uint8_t* __restrict__ hfrag, int ks, int cgp,
+              int nst, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SMAX = Ring<QT>::kGuStages;
-  static_assert((kGuWarps * SMAX + 1) * 8 <= kBarArea, "barrier area");
+  static_assert(kGuWarps * SMAX * 8 + 2 * 4 * kGuMaxCG * 4 <= kBarArea, "barrier area");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int xbytes = x_stage_bytes(d, cgp);
+  // the down kernel may be scheduled on SMs this grid leaves idle; it waits
+  // for this grid's completion before reading the hidden fragments
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int xbytes = gu_x_stage_bytes(d, cgp);
   GuCtx c;
   c.xs = smem;
-  c.xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
-  c.bars = c.xbar + 1 + warp * SMAX;
+  c.bars = reinterpret_cast<uint64_t*>(smem + xbytes) + warp * SMAX;
+  float* rs_s = reinterpret_cast<float*>(smem + xbytes + kGuWarps * SMAX * 8);
+  float* rmax_s = rs_s + 4 * kGuMaxCG;
+  c.rs = rs_s;
   c.ring = smem + xbytes + kBarArea + warp * nst * gu_stage_bytes<QT>();
   const int spc = kGuWarps / ks;
   const int strips = F / 16;
@@ -487,30 +594,24 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   c.nst = nst;
   c.lane = lane;
   c.hfrag = hfrag;
-  c.row_scale = row_scale;
   c.status = status;
   c.gbase = wg + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
   c.ubase = wu + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
   c.pol = evict_first_policy();
   if (lane == 0) {
     for (int i = 0; i < nst; ++i) mbar_init(&c.bars[i], 1);
-    if (warp == 0) mbar_init(c.xbar, 1);
     fence_mbar_init();
   }
-  __syncthreads();
-  uint32_t parity = 0u, xparity = 0u;
+  __syncwarp();
+  uint32_t parity = 0u;
   bool ok = true;
   for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
     const int ncg = min(cgp, (c.n - c0 + 3) / 4);
-    if (threadIdx.x == 0) {
-      const uint32_t xb = (uint32_t)(ncg * c.nbx * 512);
-      fence_proxy_async_smem();
-      mbar_expect_tx(c.xbar, xb);
-      bulk_g2s_plain(smem, xfrag + (size_t)(c.G0 + c0 / 4) * c.nbx * 512, xb, c.xbar);
-    }
-    if (ncg == 1) ok = gu_chunk<QT, 1>(c, parity, xparity, c0, ok);
-    else ok = gu_chunk<QT, 2>(c, parity, xparity, c0, ok);
-    xparity ^= 1u;
+    if (ok) gu_prefetch<QT>(c);
+    build_x_stage<QT>(smem, rs_s, rmax_s, x, x_rows, x_div, x_row_max, c.row0, c0, c.n, ncg, d);
+    __syncthreads();
+    if (ncg == 1) ok = gu_chunk<QT, 1>(c, parity, c0, ok);
+    else ok = gu_chunk<QT, 2>(c, parity, c0, ok);
     __syncthreads();  // x stage and rings are rewritten by the next chunk
   }
 }
@@ -532,6 +633,30 @@ struct DnCtx {
   bool strip_ok;
 };
 
+// Stage q of this warp's W_down tiles into ring slot `slot` (lane 0).
+template <int QT>
+__device__ __forceinline__ void dn_issue(const DnCtx& c, int q, int slot) {
+  using Tr = QTraits<QT>;
+  constexpr int U = Ring<QT>::kDnU;
+  constexpr int TB = Tr::kTileBytes;
+  const int t0 = q * U;
+  const uint32_t bytes = (uint32_t)(min(U, c.JT - t0) * TB);
+  mbar_expect_tx(&c.bars[slot], bytes);
+  bulk_g2s(c.ring + slot * U * TB, c.base + (size_t)t0 * TB, bytes, &c.bars[slot], c.pol);
+}
+
+// First stages of a chunk; the weights do not depend on the gate/up kernel,
+// so the first chunk's are issued before waiting for it.
+template <int QT>
+__device__ __forceinline__ void dn_prefetch(const DnCtx& c) {
+  constexpr int U = Ring<QT>::kDnU;
+  const int nstage = (c.JT + U - 1) / U;
+  if (c.lane == 0 && c.strip_ok) {
+    fence_proxy_async_smem();
+    for (int q = 0; q < min(c.nst, nstage); ++q) dn_issue<QT>(c, q, q);
+  }
+}
+
 template <int QT, int NCG>
 __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
                                           uint32_t& parity, uint32_t xparity) {
@@ -540,16 +665,6 @@ __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
   constexpr int TB = Tr::kTileBytes;
   constexpr int STAGE = U * TB;
   const int nstage = (c.JT + U - 1) / U;
-  auto issue = [&](int q, int slot) {
-    const int t0 = q * U;
-    const uint32_t bytes = (uint32_t)(min(U, c.JT - t0) * TB);
-    mbar_expect_tx(&c.bars[slot], bytes);
-    bulk_g2s(c.ring + slot * STAGE, c.base + (size_t)t0 * TB, bytes, &c.bars[slot], c.pol);
-  };
-  if (c.lane == 0) {
-    fence_proxy_async_smem();
-    for (int q = 0; q < min(c.nst, nstage); ++q) issue(q, q);
-  }
   if (!mbar_wait(c.xbar, xparity)) return false;
   const int cs = c.nbF * 512;
   const uint8_t* xq = c.hs + c.lane * 16;
@@ -566,7 +681,7 @@ __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
     __syncwarp();
     if (c.lane == 0 && q + c.nst < nstage) {
       fence_proxy_async_smem();
-      issue(q + c.nst, slot);
+      dn_issue<QT>(c, q + c.nst, slot);
     }
     slot = (slot + 1 == c.nst) ? 0 : slot + 1;
 #pragma unroll
@@ -576,11 +691,11 @@ __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
         for (int b = 0; b < 2; ++b) {
           uint32_t a0[4], a1[4];
           float2 dw, dw8;
-          tile_afrags<QT>(tw[u], b, a0, a1, dw, dw8);
+          tile_afrags<QT, false>(tw[u], b, a0, a1, dw, dw8);
 #pragma unroll
           for (int cg = 0; cg < NCG; ++cg) {
             const uint4 xf = *reinterpret_cast<const uint4*>(xq + cg * cs + u * 1024 + b * 512);
-            block_mma(acc[cg], a0, a1, xf, dw, dw8);
+            block_mma(acc[cg], a0, a1, xf, make_float4(0.f, 0.f, 0.f, 0.f), dw, dw8);
           }
         }
       }
@@ -678,8 +793,13 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   __syncthreads();
   uint32_t parity = 0u, xparity = 0u;
   bool ok = true;
+  dn_prefetch<QT>(c);
+  // launched as a programmatic dependent of the gate/up kernel: the hidden
+  // fragments are read only after that grid has completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
     const int ncg = min(cgp, (c.n - c0 + 3) / 4);
+    if (c0 > 0 && ok) dn_prefetch<QT>(c);
     if (threadIdx.x == 0) {
       const uint32_t hb = (uint32_t)(ncg * c.nbF * 512);
       fence_proxy_async_smem();
@@ -702,8 +822,6 @@ struct ExpertsWs {
   int* active;
   int* goff;
   int* gexp;
-  float* row_scale;
-  uint8_t* xfrag;
   uint8_t* hfrag;
   size_t bytes;
 };
@@ -719,8 +837,6 @@ static ExpertsWs carve_experts(void* ws, int rows, int E, int d, int F) {
   w.active = c.take<int>(E);
   w.goff = c.take<int>(E + 1);
   w.gexp = c.take<int>(mg);
-  w.row_scale = c.take<float>(rows > 0 ? rows : 1);
-  w.xfrag = c.take<uint8_t>((size_t)mg * d * 16);
   w.hfrag = c.take<uint8_t>((size_t)mg * F * 16);
   w.bytes = align_up(c.used, 256);
   return w;
@@ -775,7 +891,7 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   p.nst_gu = std::max(1, std::min(Ring<QT>::kGuStages, ((JT + p.ks - 1) / p.ks + gu_u - 1) / gu_u));
   for (;;) {
     const int ring = kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
-    const int fit = (kMaxSmem - kBarArea - ring) / x_stage_bytes(d, 1);
+    const int fit = (kMaxSmem - kBarArea - ring) / gu_x_stage_bytes(d, 1);
     p.cgp_gu = std::min(std::min(want_cg, kGuMaxCG), fit);
     if (p.cgp_gu >= std::min(want_cg, kGuMaxCG) || p.nst_gu <= 2) break;
     --p.nst_gu;
@@ -783,7 +899,7 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   if (p.cgp_gu < 1) return false;
   // the split-K reduction (cgp KB per warp) lives in the rings
   if (p.ks > 1 && p.nst_gu * gu_stage_bytes<QT>() < p.cgp_gu * 1024) return false;
-  p.smem_gu = x_stage_bytes(d, p.cgp_gu) + kBarArea + kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
+  p.smem_gu = gu_x_stage_bytes(d, p.cgp_gu) + kBarArea + kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
   const int dn_u = Ring<QT>::kDnU;
   p.nst_dn = std::max(1, std::min(Ring<QT>::kDnStages, (F / 64 + dn_u - 1) / dn_u));
   const int ring_dn = kDnWarps * p.nst_dn * dn_stage_bytes<QT>();
@@ -822,25 +938,30 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
                                            w.gexp, w.status);
   }
   MOE_CHECK(check_launch("plan"));
-  {
-    ::moe::ProfScope _prof(MOE_K_XPREP, s);
-    xprep_kernel<QT><<<mg, 128, 0, s>>>(x, x_rows, x_div, x_row_max, offsets, w.goff, w.gexp, E,
-                                        d, w.row_scale, w.xfrag);
-  }
-  MOE_CHECK(check_launch("xprep"));
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
     gateup_kernel<QT><<<p.grid_gu, kGuWarps * 32, p.smem_gu, s>>>(
-        w_gate, w_up, mat_bytes, d, F, offsets, w.n_active, w.active, w.goff, w.row_scale,
-        w.xfrag, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.status);
+        w_gate, w_up, mat_bytes, d, F, offsets, w.n_active, w.active, w.goff, x, x_rows, x_div,
+        x_row_max, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.status);
   }
   MOE_CHECK(check_launch("gateup"));
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
-    down_kernel<QT><<<p.grid_dn, kDnWarps * 32, p.smem_dn, s>>>(
-        w_down, mat_bytes, d, F, offsets, w.n_active, w.active, w.goff, w.hfrag, y, y_rows,
-        p.cgp_dn, p.nst_dn, w.status);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid_dn);
+    cfg.blockDim = dim3(kDnWarps * 32);
+    cfg.dynamicSmemBytes = p.smem_dn;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MOE_CUDA(cudaLaunchKernelEx(&cfg, down_kernel<QT>, w_down, mat_bytes, d, F, offsets,
+                                (const int*)w.n_active, (const int*)w.active,
+                                (const int*)w.goff, (const uint8_t*)w.hfrag, y, y_rows,
+                                p.cgp_dn, p.nst_dn, w.status));
   }
   return check_launch("down");
 }

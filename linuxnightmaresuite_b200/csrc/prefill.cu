@@ -33,7 +33,7 @@ constexpr int kTcM = 128;        // rows (tokens) per tile
 constexpr int kTcN = 128;        // output columns per tile
 constexpr int kTcK = 64;         // k per stage (one packed tile column, 128 B of fp16)
 constexpr int kTcStages = 3;
-constexpr int kTcThreads = 256;  // 8 warps
+constexpr int kTcThreads = 384;  // 12 warps: 0 TMA, 1 MMA, 0-3 epilogue, 4-11 weight producers
 constexpr int kTileHalf = kTcM * kTcK * 2;            // one 128 x 64 fp16 tile: 16 KB
 constexpr int kStageBytes = 4 * kTileHalf;            // A hi, A lo, B hi, B lo
 constexpr int kTcSmem = kTcStages * kStageBytes + 1024 + 1024;  // + barriers, + alignment
@@ -146,66 +146,66 @@ __device__ __forceinline__ void split_store8(uint8_t* hi_row, uint8_t* lo_row, i
   *reinterpret_cast<uint4*>(lo_row + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// One packed 16-row x 64-column tile (global) -> rows [r0, r0+16) of the
-// swizzled hi / lo tiles.  Lane (g, t) owns rows g and g + 8 and, per 32-wide
-// block, the elements its fragment layout assigns to t.
+// Registers of one packed 16-row x 64-column weight tile for one lane.
 template <int QT>
-__device__ __forceinline__ void dequant_tile_to_smem(const uint8_t* __restrict__ tile, int lane,
-                                                     uint8_t* bhi, uint8_t* blo, int r0) {
+struct PackedTile {
+  uint4 q[QT == MOE_Q8_0 ? 2 : 1];
+  uint2 sc;
+};
+
+template <int QT>
+__device__ __forceinline__ void load_packed_tile(PackedTile<QT>& p, const uint8_t* tile, int lane) {
   using Tr = QTraits<QT>;
-  const int g = lane >> 2, t = lane & 3;
   const uint8_t* qp = tile + lane * Tr::kLaneBytes;
-  const uint2 sc = __ldg(reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + g * 8));
-  const float s[4] = {__half2float(__ushort_as_half((unsigned short)(sc.x & 0xFFFF))),
-                      __half2float(__ushort_as_half((unsigned short)(sc.x >> 16))),
-                      __half2float(__ushort_as_half((unsigned short)(sc.y & 0xFFFF))),
-                      __half2float(__ushort_as_half((unsigned short)(sc.y >> 16)))};
-  if (QT == MOE_Q8_0) {
-    const uint4 qa = __ldg(reinterpret_cast<const uint4*>(qp));       // row g: b0, b1
-    const uint4 qb = __ldg(reinterpret_cast<const uint4*>(qp + 16));  // row g+8: b0, b1
-    const uint32_t words[2][2][2] = {{{qa.x, qa.y}, {qa.z, qa.w}}, {{qb.x, qb.y}, {qb.z, qb.w}}};
+  p.q[0] = __ldg(reinterpret_cast<const uint4*>(qp));
+  if (QT == MOE_Q8_0) p.q[QT == MOE_Q8_0 ? 1 : 0] = __ldg(reinterpret_cast<const uint4*>(qp + 16));
+  p.sc = __ldg(reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + (lane >> 2) * 8));
+}
+
+// One packed tile (registers) -> rows [r0, r0+16) of the swizzled hi / lo B
+// tiles.  Lane (g, t) owns rows g and g + 8 and, per 32-wide block, the
+// elements its fragment layout assigns to t.  Odd rows write their blocks in
+// the opposite order so the eight lanes of a store phase hit distinct 16-byte
+// chunks (no bank conflicts).
+template <int QT>
+__device__ __forceinline__ void store_packed_tile(const PackedTile<QT>& p, int lane, uint8_t* bhi,
+                                                  uint8_t* blo, int r0) {
+  const int g = lane >> 2, t = lane & 3;
+  const float s[4] = {__half2float(__ushort_as_half((unsigned short)(p.sc.x & 0xFFFF))),
+                      __half2float(__ushort_as_half((unsigned short)(p.sc.x >> 16))),
+                      __half2float(__ushort_as_half((unsigned short)(p.sc.y & 0xFFFF))),
+                      __half2float(__ushort_as_half((unsigned short)(p.sc.y >> 16)))};
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int row = r0 + g + 8 * half;
-      uint8_t* hr = bhi + row * 128;
-      uint8_t* lr = blo + row * 128;
+  for (int half = 0; half < 2; ++half) {
+    const int row = r0 + g + 8 * half;
+    uint8_t* hr = bhi + row * 128;
+    uint8_t* lr = blo + row * 128;
 #pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        const float d = s[half * 2 + b];
+    for (int it = 0; it < 2; ++it) {
+      const int b = it ^ (g & 1);
+      const float d = s[half * 2 + b];
+      if (QT == MOE_Q8_0) {
+        const uint4& qv = p.q[QT == MOE_Q8_0 ? half : 0];   // row g: q[0], row g+8: q[1]
+        const uint32_t w0 = b ? qv.z : qv.x, w1 = b ? qv.w : qv.y;
         float w[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const uint32_t word = words[half][b][i >> 2];
-          const int q = (int)(int8_t)((word >> (8 * (i & 3))) & 0xFF);
-          w[i] = d * (float)q;
+          const uint32_t word = i < 4 ? w0 : w1;
+          w[i] = d * (float)(int)(int8_t)((word >> (8 * (i & 3))) & 0xFF);
         }
         // elements 32b + 8t .. +7 -> 16-byte chunk 4b + t, swizzled by row
         split_store8(hr, lr, (4 * b + t) ^ (row & 7), w);
-      }
-    }
-  } else {
-    const uint4 q = __ldg(reinterpret_cast<const uint4*>(qp));  // (g,b0) (g,b1) (g8,b0) (g8,b1)
-    const uint32_t words[2][2] = {{q.x, q.y}, {q.z, q.w}};
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int row = r0 + g + 8 * half;
-      uint8_t* hr = bhi + row * 128;
-      uint8_t* lr = blo + row * 128;
-#pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        const float d = s[half * 2 + b];
-        const uint32_t word = words[half][b];  // bytes 4t..4t+3 of the block's 16
+      } else {
+        const uint32_t word = half ? (b ? p.q[0].w : p.q[0].z) : (b ? p.q[0].y : p.q[0].x);
         float lo4[4], hi4[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const uint32_t byte = (word >> (8 * i)) & 0xFF;
-          lo4[i] = d * (float)((int)(byte & 0xF) - 8);   // element 4t + i
-          hi4[i] = d * (float)((int)(byte >> 4) - 8);    // element 16 + 4t + i
+          lo4[i] = d * (float)((int)(byte & 0xF) - 8);   // element 32b + 4t + i
+          hi4[i] = d * (float)((int)(byte >> 4) - 8);    // element 32b + 16 + 4t + i
         }
-        // elements 32b + 4t .. +3 and 32b + 16 + 4t .. +3: two half chunks
-        // -> write each 8-byte half into its 16-byte chunk
-        const int ch_lo = (4 * b + (t >> 1)) ^ (row & 7);        // element 32b + 4t
-        const int ch_hi = (4 * b + 2 + (t >> 1)) ^ (row & 7);    // element 32b + 16 + 4t
+        const int ch_lo = (4 * b + (t >> 1)) ^ (row & 7);
+        const int ch_hi = (4 * b + 2 + (t >> 1)) ^ (row & 7);
         const int off = (t & 1) * 8;
         uint32_t h[2], l[2];
 #pragma unroll
@@ -350,7 +350,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], 4);
+      mbar_init(&full_b[s], 8);
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -415,35 +415,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
     }
     tc_commit(acc_full);      // accumulator complete (or abandoned)
   } else if (warp >= 4) {
-    // weight producers: 8 strips of 16 rows per stage, two per warp
-    const int pw = warp - 4;
-    for (int kk = 0; kk < ksteps; ++kk) {
-      const int s = kk % kTcStages, round = kk / kTcStages;
-      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
-        if (lane == 0) *flag = 1;
-        break;
-      }
-      uint8_t* st = stage_base + s * kStageBytes;
-      uint8_t* bhi = st + 2 * kTileHalf;
-      uint8_t* blo = st + 3 * kTileHalf;
+    // weight producers: warp 4 + i dequantises strip i (16 B-rows) of every
+    // stage; the next stage's packed tile is loaded before this one is stored
+    const int strip = warp - 4;                       // 0..7 -> B rows 16*strip
+    const uint8_t* mat;
+    int wstrip;
+    if (MODE == 0) {
+      mat = (strip < 4 ? args.w0 : args.w1) + (size_t)e * args.mat_bytes;
+      wstrip = nt * 4 + (strip & 3);                  // 64 F-rows per tile
+    } else {
+      mat = args.w0 + (size_t)e * args.mat_bytes;
+      wstrip = nt * 8 + strip;                        // 128 d-rows per tile
+    }
+    const uint8_t* tiles = mat + (size_t)wstrip * ksteps * Tr::kTileBytes;
+    // three packed tiles in flight per lane: the load of stage kk + 3 is issued
+    // as soon as stage kk has been stored
+    PackedTile<QT> p[3];
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int strip = pw * 2 + q;                 // 0..7 -> B rows 16*strip
-        const uint8_t* mat;
-        int wstrip;
-        if (MODE == 0) {
-          mat = (strip < 4 ? args.w0 : args.w1) + (size_t)e * args.mat_bytes;
-          wstrip = nt * 4 + (strip & 3);              // 64 F-rows per tile
-        } else {
-          mat = args.w0 + (size_t)e * args.mat_bytes;
-          wstrip = nt * 8 + strip;                    // 128 d-rows per tile
+    for (int i = 0; i < 3; ++i)
+      if (i < ksteps) load_packed_tile<QT>(p[i], tiles + (size_t)i * Tr::kTileBytes, lane);
+    bool ok = true;
+    for (int k0 = 0; k0 < ksteps && ok; k0 += 3) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        const int kk = k0 + i;
+        if (kk < ksteps && ok) {
+          const int s = kk % kTcStages, round = kk / kTcStages;
+          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+            if (lane == 0) *flag = 1;
+            ok = false;
+          } else {
+            uint8_t* st = stage_base + s * kStageBytes;
+            store_packed_tile<QT>(p[i], lane, st + 2 * kTileHalf, st + 3 * kTileHalf, strip * 16);
+            if (kk + 3 < ksteps)
+              load_packed_tile<QT>(p[i], tiles + (size_t)(kk + 3) * Tr::kTileBytes, lane);
+            fence_proxy_async_smem();   // generic stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_b[s]);
+          }
         }
-        const uint8_t* tile = mat + ((size_t)wstrip * ksteps + kk) * Tr::kTileBytes;
-        dequant_tile_to_smem<QT>(tile, lane, bhi, blo, strip * 16);
       }
-      fence_proxy_async_smem();   // generic stores -> visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full_b[s]);
     }
   }
 

@@ -229,8 +229,10 @@ __device__ void select_token(const float* __restrict__ lg, float* __restrict__ b
 
 // Router in one launch: a cluster of kRouterCluster CTAs per token tile.  CTA
 // rank r accumulates partial logits of the tile's tokens over its d-range:
-// 32-row chunks of the router matrix and the matching slice of the tokens are
-// double-buffered into shared memory by bulk copies (TMA), and each thread
+// 32-row chunks of the router matrix and the matching slice of the tokens
+// stream through a ring of up to kFusedMaxStages shared-memory stages filled
+// by bulk copies (TMA) -- for decode-sized d every chunk of the CTA's range is
+// in flight at once -- and each thread
 // keeps TPT tokens x 4 experts of partial sums in registers.  The partials stay
 // in the CTA's shared memory; after a cluster barrier CTA r sums, for its share
 // of the tile's tokens, the partials of ranks 0..C-1 in rank order through
@@ -239,6 +241,7 @@ __device__ void select_token(const float* __restrict__ lg, float* __restrict__ b
 constexpr int kRouterCluster = 8;
 constexpr int kFusedDC = 32;            // router rows per chunk
 constexpr int kFusedXP = kFusedDC + 4;  // padded x row (16-byte aligned)
+constexpr int kFusedMaxStages = 16;
 
 struct FusedShape {
   int ct, tg, tt, per, tiles;
@@ -258,19 +261,31 @@ static FusedShape fused_shape(int T, int E, int tpt) {
   return f;
 }
 
-static size_t fused_smem(const FusedShape& f, int E) {
-  return (2 * (size_t)kFusedDC * E + 2 * (size_t)f.tt * kFusedXP + (size_t)f.tt * E +
+static size_t fused_smem(const FusedShape& f, int E, int nst) {
+  return ((size_t)nst * kFusedDC * E + (size_t)nst * f.tt * kFusedXP + (size_t)f.tt * E +
           (size_t)f.per * E + (size_t)(kRouterThreads / 32) * (kMaxE + kMaxK) + (size_t)f.tt) *
              sizeof(float) +
-         64;
+         8 * (size_t)nst + 64;
+}
+
+// Ring depth.  A grid that fits in one wave keeps every chunk of a rank's
+// d-range in flight (as many as shared memory holds); a larger grid keeps two
+// stages so that several CTAs share an SM.
+static int fused_stages(const FusedShape& f, int d, int E) {
+  const int nchunks = (d + kFusedDC - 1) / kFusedDC;
+  if (f.tiles * kRouterCluster > sm_count()) return 2;
+  int nst = std::min(kFusedMaxStages, (nchunks + kRouterCluster - 1) / kRouterCluster);
+  while (nst > 2 && fused_smem(f, E, nst) > 227 * 1024) --nst;
+  return std::max(nst, 1);
 }
 
 template <int TPT>
 __global__ void __launch_bounds__(kRouterThreads)
 router_fused_kernel(const float* __restrict__ x, const float* __restrict__ G,
                     const float* __restrict__ bias, int T, int d, int E, int k, int layout,
-                    int mode, int tg, int32_t* __restrict__ ids, float* __restrict__ weights,
-                    float* __restrict__ row_max, int* __restrict__ status) {
+                    int mode, int tg, int nst, int32_t* __restrict__ ids,
+                    float* __restrict__ weights, float* __restrict__ row_max,
+                    int* __restrict__ status) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(128) float smem[];
@@ -279,14 +294,14 @@ router_fused_kernel(const float* __restrict__ x, const float* __restrict__ G,
   const int ct = E / 4;
   const int tt = tg * TPT;
   const int per = tt / kRouterCluster;
-  float* gbuf = smem;                                // [2][kFusedDC][E] (E_D: [2][E][kFusedDC])
-  float* xbuf = gbuf + 2 * kFusedDC * E;             // [2][tt][kFusedXP]
-  float* part = xbuf + 2 * tt * kFusedXP;            // [tt][E] partial logits
+  float* gbuf = smem;                                // [nst][kFusedDC][E] (E_D: [nst][E][kFusedDC])
+  float* xbuf = gbuf + nst * kFusedDC * E;           // [nst][tt][kFusedXP]
+  float* part = xbuf + nst * tt * kFusedXP;          // [tt][E] partial logits
   float* lg = part + tt * E;                         // [per][E] reduced logits
   float* buf = lg + per * E;                         // [NW][kMaxE]
   float* sv = buf + NW * kMaxE;                      // [NW][kMaxK]
   float* xmax = sv + NW * kMaxK;                     // [tt]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(xmax + tt + ((tt & 1) ? 1 : 0));  // [2]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xmax + tt + ((tt & 1) ? 1 : 0));  // [nst]
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
   const int col = tid % ct;
@@ -297,12 +312,11 @@ router_fused_kernel(const float* __restrict__ x, const float* __restrict__ G,
   const int cb = rank * nchunks / kRouterCluster, ce = (rank + 1) * nchunks / kRouterCluster;
   const int nvalid = max(0, min(tt, T - t0));
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int i = 0; i < nst; ++i) mbar_init(&bar[i], 1);
     fence_mbar_init();
   }
-  // rows of tokens past T stay zero in both stages
-  for (int v = tid; v < 2 * tt * kFusedXP; v += NT) {
+  // rows of tokens past T stay zero in every stage
+  for (int v = tid; v < nst * tt * kFusedXP; v += NT) {
     const int tl = (v / kFusedXP) % tt;
     if (tl >= nvalid) xbuf[v] = 0.f;
   }
@@ -338,12 +352,11 @@ router_fused_kernel(const float* __restrict__ x, const float* __restrict__ G,
   for (int a = 0; a < TPT; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  if (cb < ce) issue(cb, 0);
-  if (cb + 1 < ce) issue(cb + 1, 1);
+  for (int i = 0; i < nst && cb + i < ce; ++i) issue(cb + i, i);
   bool ok = true;
   for (int c = cb; c < ce; ++c) {
-    const int stg = (c - cb) & 1;
-    const uint32_t parity = ((c - cb) >> 1) & 1;
+    const int stg = (c - cb) % nst;
+    const uint32_t parity = ((c - cb) / nst) & 1;
     if (ok && !mbar_wait(&bar[stg], parity)) {
       set_status(status, MOE_STATUS_TIMEOUT);
       ok = false;
@@ -385,8 +398,10 @@ router_fused_kernel(const float* __restrict__ x, const float* __restrict__ G,
         }
       }
     }
-    __syncthreads();  // stage fully read before it is refilled
-    if (ok && c + 2 < ce) issue(c + 2, stg);
+    if (c + nst < ce) {
+      __syncthreads();  // stage fully read before it is refilled
+      if (ok) issue(c + nst, stg);
+    }
   }
   if (tgrp < tg) {
 #pragma unroll
@@ -618,7 +633,8 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
   const int tg1 = fused_shape(T, E, 1).tg;
   const int tpt = (tg1 < kRouterCluster || (T > 256 && tg1 <= kRouterCluster)) ? 4 : 1;
   const FusedShape f = fused_shape(T, E, tpt);
-  const size_t smem = fused_smem(f, E);
+  const int nst = fused_stages(f, d, E);
+  const size_t smem = fused_smem(f, E, nst);
   MOE_REQUIRE(f.per >= 1 && f.tt % kRouterCluster == 0 && f.ct * f.tg <= kRouterThreads &&
                   smem <= 227 * 1024,
               MOE_ERR_UNSUPPORTED, "router shape E=%d does not fit the fused router", E);
@@ -653,13 +669,13 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
   cfg.numAttrs = 1;
   int* status = workspace ? static_cast<int*>(workspace) : nullptr;
   {
-    ::moe::ProfScope _prof(MOE_K_ROUTER_PARTIAL, s);
+    ::moe::ProfScope _prof(MOE_K_ROUTER, s);
     if (tpt == 1)
       MOE_CUDA(cudaLaunchKernelEx(&cfg, router_fused_kernel<1>, x, gate_w, bias, T, d, E, k,
-                                  layout, mode, f.tg, ids, weights, row_max, status));
+                                  layout, mode, f.tg, nst, ids, weights, row_max, status));
     else
       MOE_CUDA(cudaLaunchKernelEx(&cfg, router_fused_kernel<4>, x, gate_w, bias, T, d, E, k,
-                                  layout, mode, f.tg, ids, weights, row_max, status));
+                                  layout, mode, f.tg, nst, ids, weights, row_max, status));
   }
   return check_launch("router_fused");
 }
@@ -746,7 +762,7 @@ extern "C" int moe_router_noalloc(const float* x, const float* gate_w, const flo
   }
   dim3 grid(p.tiles, p.nds);
   {
-    ::moe::ProfScope _prof(MOE_K_ROUTER_PARTIAL, s);
+    ::moe::ProfScope _prof(MOE_K_ROUTER, s);
     router_partial_kernel<<<grid, p.ct * p.tg, smem, s>>>(x, gate_w, T, d, E, layout, p.tt,
                                                           p.chunks, part);
   }
