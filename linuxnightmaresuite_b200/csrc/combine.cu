@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(kCombineThreads)
 combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm,
                const float* __restrict__ w, const float* __restrict__ shared,
                const float* __restrict__ residual, int k, int d, float* __restrict__ out) {
+  pdl_wait();   // the expert outputs
   const int t = blockIdx.x;
   __shared__ int rows[32];
   __shared__ float wts[32];
@@ -89,8 +90,8 @@ int launch_combine(const float* y, const int32_t* inv_perm, const float* w, cons
   {
     ::moe::ProfScope _prof(MOE_K_COMBINE, s);
     const int slices = (d / 4 + kCombineThreads - 1) / kCombineThreads;
-    combine_kernel<<<dim3(T, slices), kCombineThreads, 0, s>>>(y, inv_perm, w, shared, residual,
-                                                               k, d, out);
+    MOE_CUDA(launch_pdl(combine_kernel, dim3(T, slices), dim3(kCombineThreads), 0, s, y, inv_perm,
+                        w, shared, residual, k, d, out));
   }
   return check_launch("combine");
 }

@@ -22,6 +22,8 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
                 int32_t* __restrict__ perm_rows, int32_t* __restrict__ inv_perm,
                 int* __restrict__ status, int* __restrict__ n_active, int* __restrict__ active,
                 int* __restrict__ goff, int* __restrict__ gexp, int max_groups) {
+  pdl_wait();   // the router's ids
+  pdl_trigger();
   extern __shared__ int sm[];
   int* wcnt = sm;                          // [kDispWarps][E]
   int* etot = sm + kDispWarps * E;         // [E]
@@ -146,8 +148,8 @@ int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* of
   }
   {
     ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
-    dispatch_kernel<<<1, kDispThreads, smem, s>>>(ids, P, E, offsets, perm_rows, inv_perm, status,
-                                                  n_active, active, goff, gexp, max_groups);
+    MOE_CUDA(launch_pdl(dispatch_kernel, dim3(1), dim3(kDispThreads), smem, s, ids, P, E, offsets,
+                        perm_rows, inv_perm, status, n_active, active, goff, gexp, max_groups));
   }
   return check_launch("dispatch");
 }
@@ -188,9 +190,9 @@ int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offset
   }
   {
     ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
-    dispatch_kernel<<<1, kDispThreads, smem, s>>>(ids, (int)P, E, expert_offsets, perm_rows,
-                                                  inv_perm, static_cast<int*>(workspace), nullptr,
-                                                  nullptr, nullptr, nullptr, 0);
+    MOE_CUDA(launch_pdl(dispatch_kernel, dim3(1), dim3(kDispThreads), smem, s, ids, (int)P, E,
+                        expert_offsets, perm_rows, inv_perm, static_cast<int*>(workspace),
+                        (int*)nullptr, (int*)nullptr, (int*)nullptr, (int*)nullptr, 0));
   }
   return check_launch("dispatch");
 }

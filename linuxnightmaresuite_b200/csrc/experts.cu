@@ -562,9 +562,12 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   static_assert(kGuWarps * SMAX * 8 + 2 * 4 * kGuMaxCG * 4 <= kBarArea, "barrier area");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the down kernel may be scheduled on SMs this grid leaves idle; it waits
-  // for this grid's completion before reading the hidden fragments
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Wait for the plan of the previous kernels, then let the down kernel be
+  // scheduled on SMs this grid leaves idle (it reads the plan at once, but the
+  // hidden fragments only after this grid has completed).  Triggering only
+  // after the wait keeps the plan complete for it.
+  pdl_wait();
+  pdl_trigger();
   const int xbytes = gu_x_stage_bytes(d, cgp);
   GuCtx c;
   c.xs = smem;
@@ -796,7 +799,8 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   dn_prefetch<QT>(c);
   // launched as a programmatic dependent of the gate/up kernel: the hidden
   // fragments are read only after that grid has completed
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  pdl_wait();
+  pdl_trigger();
   for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
     const int ncg = min(cgp, (c.n - c0 + 3) / 4);
     if (c0 > 0 && ok) dn_prefetch<QT>(c);
@@ -941,27 +945,18 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
-    gateup_kernel<QT><<<p.grid_gu, kGuWarps * 32, p.smem_gu, s>>>(
-        w_gate, w_up, mat_bytes, d, F, offsets, w.n_active, w.active, w.goff, x, x_rows, x_div,
-        x_row_max, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.status);
+    MOE_CUDA(launch_pdl(gateup_kernel<QT>, dim3(p.grid_gu), dim3(kGuWarps * 32), p.smem_gu, s,
+                        w_gate, w_up, mat_bytes, d, F, offsets, (const int*)w.n_active,
+                        (const int*)w.active, (const int*)w.goff, x, x_rows, x_div, x_row_max,
+                        w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.status));
   }
   MOE_CHECK(check_launch("gateup"));
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.grid_dn);
-    cfg.blockDim = dim3(kDnWarps * 32);
-    cfg.dynamicSmemBytes = p.smem_dn;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    MOE_CUDA(cudaLaunchKernelEx(&cfg, down_kernel<QT>, w_down, mat_bytes, d, F, offsets,
-                                (const int*)w.n_active, (const int*)w.active,
-                                (const int*)w.goff, (const uint8_t*)w.hfrag, y, y_rows,
-                                p.cgp_dn, p.nst_dn, w.status));
+    MOE_CUDA(launch_pdl(down_kernel<QT>, dim3(p.grid_dn), dim3(kDnWarps * 32), p.smem_dn, s,
+                        w_down, mat_bytes, d, F, offsets, (const int*)w.n_active,
+                        (const int*)w.active, (const int*)w.goff, (const uint8_t*)w.hfrag, y,
+                        y_rows, p.cgp_dn, p.nst_dn, w.status));
   }
   return check_launch("down");
 }

@@ -3,6 +3,7 @@
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <utility>
 #include <stdint.h>
 
 #include "moe_b200.h"
@@ -40,6 +41,26 @@ int sm_count();
 // Per-kernel event profiling (see moe_profile_enable).
 void prof_begin(int kernel_id, cudaStream_t s);
 void prof_end(cudaStream_t s);
+
+// Launch that may begin while the previous kernel on the stream is still
+// running (programmatic dependent launch).  The kernel must execute
+// pdl_wait() before it reads anything the previous kernel writes; the
+// previous kernel lets it start early with pdl_trigger().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Brackets one kernel launch with the profiler's events.
 struct ProfScope {
@@ -321,6 +342,13 @@ static __device__ int block_excl_scan(int v, int* sh, int& total) {
   total = sh[32];
   __syncthreads();
   return res;
+}
+
+// Programmatic dependent launch: wait for the previous kernel's completion
+// (no-op when launched normally) / allow the next kernel to start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ void set_status(int* status, int bit) {

@@ -339,6 +339,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
   int* flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Programmatic dependent launches: gate/up waits for the tile plan before
+  // anything else; down reads the plan at once (complete, because gate/up
+  // triggers only after its own wait) and waits for gate/up's hidden planes
+  // only in its activation producer, so its weight producers start early.
+  if (MODE == 0) pdl_wait();
+  pdl_trigger();
   const int mt = blockIdx.x / args.n_tiles_n;
   const int nt = blockIdx.x % args.n_tiles_n;
   if (mt >= *args.n_mtiles) return;
@@ -372,6 +378,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
 
   if (warp == 0 && lane == 0) {
     // activation producer: hi and lo planes of the stage's 128 x 64 tile
+    if (MODE == 1) pdl_wait();
     for (int kk = 0; kk < ksteps; ++kk) {
       const int s = kk % kTcStages, round = kk / kTcStages;
       if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
@@ -644,7 +651,8 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   a1.status = status;
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
-    tc_gemm_kernel<QT, 0><<<max_tiles * a1.n_tiles_n, kTcThreads, kTcSmem, s>>>(xmap, a1);
+    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 0>, dim3(max_tiles * a1.n_tiles_n), dim3(kTcThreads),
+                        kTcSmem, s, xmap, a1));
   }
   MOE_CHECK(check_launch("tc_gemm gate/up"));
   TcArgs a2 = a1;
@@ -656,7 +664,8 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   a2.y_rows = y_rows;
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
-    tc_gemm_kernel<QT, 1><<<max_tiles * a2.n_tiles_n, kTcThreads, kTcSmem, s>>>(hmap, a2);
+    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 1>, dim3(max_tiles * a2.n_tiles_n), dim3(kTcThreads),
+                        kTcSmem, s, hmap, a2));
   }
   return check_launch("tc_gemm down");
 }
