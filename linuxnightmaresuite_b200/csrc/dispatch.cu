@@ -21,7 +21,8 @@ __global__ void __launch_bounds__(kDispThreads)
 dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restrict__ offsets,
                 int32_t* __restrict__ perm_rows, int32_t* __restrict__ inv_perm,
                 int* __restrict__ status, int* __restrict__ n_active, int* __restrict__ active,
-                int* __restrict__ goff, int* __restrict__ gexp, int max_groups) {
+                int* __restrict__ goff, int* __restrict__ gexp, int* __restrict__ done,
+                int max_groups) {
   pdl_wait();   // the router's ids
   pdl_trigger();
   extern __shared__ int sm[];
@@ -78,6 +79,7 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
     const bool overflow = tot_g > max_groups;
     if (e < E) {
       goff[e] = g0;
+      done[e] = 0;
       if (n > 0) active[a0] = e;
       if (!overflow)
         for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
@@ -136,7 +138,8 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
 // moe_dispatch that also writes the grouped-expert plan (see plan_kernel).
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
-                            int* active, int* goff, int* gexp, int max_groups, cudaStream_t s) {
+                            int* active, int* goff, int* gexp, int* done, int max_groups,
+                            cudaStream_t s) {
   MOE_REQUIRE(E > 0 && E <= kDispThreads, MOE_ERR_UNSUPPORTED, "expert count %d above %d", E,
               kDispThreads);
   const int P = T * k;
@@ -149,7 +152,8 @@ int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* of
   {
     ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
     MOE_CUDA(launch_pdl(dispatch_kernel, dim3(1), dim3(kDispThreads), smem, s, ids, P, E, offsets,
-                        perm_rows, inv_perm, status, n_active, active, goff, gexp, max_groups));
+                        perm_rows, inv_perm, status, n_active, active, goff, gexp, done,
+                        max_groups));
   }
   return check_launch("dispatch");
 }
@@ -192,7 +196,8 @@ int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offset
     ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
     MOE_CUDA(launch_pdl(dispatch_kernel, dim3(1), dim3(kDispThreads), smem, s, ids, (int)P, E,
                         expert_offsets, perm_rows, inv_perm, static_cast<int*>(workspace),
-                        (int*)nullptr, (int*)nullptr, (int*)nullptr, (int*)nullptr, 0));
+                        (int*)nullptr, (int*)nullptr, (int*)nullptr, (int*)nullptr,
+                        (int*)nullptr, 0));
   }
   return check_launch("dispatch");
 }

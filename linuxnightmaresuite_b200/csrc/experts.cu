@@ -80,7 +80,7 @@ __device__ __forceinline__ void frag_pos(int e, int& t, int& i) {
 __global__ void __launch_bounds__(kPlanThreads)
 plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups,
             int* __restrict__ n_active, int* __restrict__ active, int* __restrict__ goff,
-            int* __restrict__ gexp, int* __restrict__ status) {
+            int* __restrict__ gexp, int* __restrict__ done, int* __restrict__ status) {
   __shared__ int sh[33];
   const int e = threadIdx.x;
   int n = 0;
@@ -99,6 +99,7 @@ plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups
   if (overflow && e == 0) set_status(status, MOE_STATUS_ROW_OVERFLOW);
   if (e < E) {
     goff[e] = g0;
+    done[e] = 0;
     if (n > 0) active[a0] = e;
     if (!overflow)
       for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
@@ -234,6 +235,24 @@ __host__ __device__ constexpr int gu_stage_bytes() {
 template <int QT>
 __host__ __device__ constexpr int dn_stage_bytes() {
   return Ring<QT>::kDnU * QTraits<QT>::kTileBytes;
+}
+
+// Bounded wait (thread-level) until *p >= target, with acquire semantics at
+// GPU scope: gives up after ~0.2 s of wall time or 2^22 polls.
+__device__ __forceinline__ bool wait_count(const int* p, int target) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0; it < (1u << 22); ++it) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    if ((it & 63u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (it == 0u) t0 = now;
+      else if (now - t0 > 200000000ull) return false;
+    }
+    __nanosleep(128);
+  }
+  return false;
 }
 
 // Per-CTA state of a gate/up work item.
@@ -555,7 +574,7 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
               const int* __restrict__ active, const int* __restrict__ goff,
               const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
               const float* __restrict__ x_row_max, uint8_t* __restrict__ hfrag, int ks, int cgp,
-              int nst, int* __restrict__ status) {
+              int nst, int* __restrict__ done, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SMAX = Ring<QT>::kGuStages;
@@ -617,6 +636,12 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
     else ok = gu_chunk<QT, 2>(c, parity, c0, ok);
     __syncthreads();  // x stage and rings are rewritten by the next chunk
   }
+  // this CTA's hidden fragments are complete: count it for the expert (the
+  // down kernel's CTAs of expert e start once all of e's CTAs have counted)
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + e) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -626,7 +651,6 @@ struct DnCtx {
   const uint8_t* base;
   uint8_t* ring;
   uint64_t* bars;
-  uint64_t* xbar;
   const uint8_t* hs;
   float* y;
   const int32_t* y_rows;
@@ -662,13 +686,12 @@ __device__ __forceinline__ void dn_prefetch(const DnCtx& c) {
 
 template <int QT, int NCG>
 __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
-                                          uint32_t& parity, uint32_t xparity) {
+                                          uint32_t& parity) {
   using Tr = QTraits<QT>;
   constexpr int U = Ring<QT>::kDnU;
   constexpr int TB = Tr::kTileBytes;
   constexpr int STAGE = U * TB;
   const int nstage = (c.JT + U - 1) / U;
-  if (!mbar_wait(c.xbar, xparity)) return false;
   const int cs = c.nbF * 512;
   const uint8_t* xq = c.hs + c.lane * 16;
   int slot = 0;
@@ -709,19 +732,15 @@ __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
 }
 
 template <int QT, int NCG>
-__device__ __forceinline__ bool dn_chunk(const DnCtx& c, uint32_t& parity, uint32_t xparity,
-                                         int c0, bool ok) {
+__device__ __forceinline__ bool dn_chunk(const DnCtx& c, uint32_t& parity, int c0, bool ok) {
   float2 acc[NCG][2];
 #pragma unroll
   for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = make_float2(0.f, 0.f);
   if (c.strip_ok && ok) {
-    if (!dn_stream<QT, NCG>(acc, c, parity, xparity)) {
+    if (!dn_stream<QT, NCG>(acc, c, parity)) {
       set_status(c.status, MOE_STATUS_TIMEOUT);
       ok = false;
     }
-  } else if (!mbar_wait(c.xbar, xparity)) {
-    set_status(c.status, MOE_STATUS_TIMEOUT);
-    ok = false;
   }
 #pragma unroll
   for (int cg = 0; cg < NCG; ++cg)
@@ -755,18 +774,19 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
             const int* __restrict__ active, const int* __restrict__ goff,
             const uint8_t* __restrict__ hfrag, float* __restrict__ y,
-            const int32_t* __restrict__ y_rows, int cgp, int nst, int* __restrict__ status) {
+            const int32_t* __restrict__ y_rows, int cgp, int nst, const int* __restrict__ done,
+            int gu_cpe, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SMAX = Ring<QT>::kDnStages;
-  static_assert((kDnWarps * SMAX + 1) * 8 <= kBarArea, "barrier area");
+  static_assert(kDnWarps * SMAX * 8 + 16 <= kBarArea, "barrier area");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int xbytes = x_stage_bytes(F, cgp);
   DnCtx c;
   c.hs = smem;
-  c.xbar = reinterpret_cast<uint64_t*>(smem + xbytes);
-  c.bars = c.xbar + 1 + warp * SMAX;
+  c.bars = reinterpret_cast<uint64_t*>(smem + xbytes) + warp * SMAX;
+  int* ok_s = reinterpret_cast<int*>(smem + xbytes + kDnWarps * SMAX * 8);
   c.ring = smem + xbytes + kBarArea + warp * nst * dn_stage_bytes<QT>();
   const int strips = d / 16;
   const int cpe = (strips + kDnWarps - 1) / kDnWarps;
@@ -790,29 +810,32 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   c.pol = evict_first_policy();
   if (lane == 0) {
     for (int i = 0; i < nst; ++i) mbar_init(&c.bars[i], 1);
-    if (warp == 0) mbar_init(c.xbar, 1);
     fence_mbar_init();
   }
-  __syncthreads();
-  uint32_t parity = 0u, xparity = 0u;
-  bool ok = true;
+  __syncwarp();
+  uint32_t parity = 0u;
   dn_prefetch<QT>(c);
-  // launched as a programmatic dependent of the gate/up kernel: the hidden
-  // fragments are read only after that grid has completed
-  pdl_wait();
+  // Launched as a programmatic dependent of the gate/up kernel, which may still
+  // be running: wait (bounded) until every gate/up CTA of expert e has counted
+  // its hidden fragments as written.  The plan read above is complete (gate/up
+  // lets this grid start only after its own wait for the plan).
+  if (threadIdx.x == 0) *ok_s = wait_count(done + e, gu_cpe) ? 1 : 0;
+  __syncthreads();
+  bool ok = *ok_s != 0;
+  if (!ok && threadIdx.x == 0) set_status(status, MOE_STATUS_TIMEOUT);
+  ok = true;   // stream regardless, so every issued copy is consumed
   pdl_trigger();
   for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
     const int ncg = min(cgp, (c.n - c0 + 3) / 4);
     if (c0 > 0 && ok) dn_prefetch<QT>(c);
-    if (threadIdx.x == 0) {
-      const uint32_t hb = (uint32_t)(ncg * c.nbF * 512);
-      fence_proxy_async_smem();
-      mbar_expect_tx(c.xbar, hb);
-      bulk_g2s_plain(smem, hfrag + (size_t)(G0 + c0 / 4) * c.nbF * 512, hb, c.xbar);
-    }
-    if (ncg == 1) ok = dn_chunk<QT, 1>(c, parity, xparity, c0, ok);
-    else ok = dn_chunk<QT, 2>(c, parity, xparity, c0, ok);
-    xparity ^= 1u;
+    // hidden fragments of the chunk's groups: plain loads (they were written by
+    // other CTAs' plain stores, ordered by the counter's release / acquire)
+    const uint4* src = reinterpret_cast<const uint4*>(hfrag + (size_t)(G0 + c0 / 4) * c.nbF * 512);
+    uint4* dst = reinterpret_cast<uint4*>(smem);
+    for (int i = threadIdx.x; i < ncg * c.nbF * 32; i += kDnWarps * 32) dst[i] = src[i];
+    __syncthreads();
+    if (ncg == 1) ok = dn_chunk<QT, 1>(c, parity, c0, ok);
+    else ok = dn_chunk<QT, 2>(c, parity, c0, ok);
     __syncthreads();  // the staged hidden fragments are rewritten by the next chunk
   }
 }
@@ -826,6 +849,7 @@ struct ExpertsWs {
   int* active;
   int* goff;
   int* gexp;
+  int* done;    // per expert: gate/up CTAs finished
   uint8_t* hfrag;
   size_t bytes;
 };
@@ -841,6 +865,7 @@ static ExpertsWs carve_experts(void* ws, int rows, int E, int d, int F) {
   w.active = c.take<int>(E);
   w.goff = c.take<int>(E + 1);
   w.gexp = c.take<int>(mg);
+  w.done = c.take<int>(E);
   w.hfrag = c.take<uint8_t>((size_t)mg * F * 16);
   w.bytes = align_up(c.used, 256);
   return w;
@@ -871,7 +896,7 @@ int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
 
 // Launch shape of the two GEMV kernels for a call.
 struct ExpertsPlan {
-  int ks, cgp_gu, nst_gu, smem_gu, grid_gu;
+  int ks, cgp_gu, nst_gu, smem_gu, grid_gu, cpe_gu;
   int cgp_dn, nst_dn, smem_dn, grid_dn;
 };
 
@@ -885,7 +910,8 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   while (p.ks < 8 && (long long)est_active * strips_f * p.ks < target && JT / (2 * p.ks) >= 2)
     p.ks *= 2;
   const int spc = kGuWarps / p.ks;
-  p.grid_gu = est_active * ((strips_f + spc - 1) / spc);
+  p.cpe_gu = (strips_f + spc - 1) / spc;
+  p.grid_gu = est_active * p.cpe_gu;
   // column groups per pass: about twice the mean rows of an expert
   const int mean_rows = (rows + est_active - 1) / est_active;
   const int want_cg = std::max(1, std::min(kMaxCG, (2 * mean_rows + 3) / 4));
@@ -939,7 +965,7 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   if (!planned) {
     ::moe::ProfScope _prof(MOE_K_PLAN, s);
     plan_kernel<<<1, kPlanThreads, 0, s>>>(offsets, E, rows, mg, w.n_active, w.active, w.goff,
-                                           w.gexp, w.status);
+                                           w.gexp, w.done, w.status);
   }
   MOE_CHECK(check_launch("plan"));
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
@@ -948,7 +974,7 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
     MOE_CUDA(launch_pdl(gateup_kernel<QT>, dim3(p.grid_gu), dim3(kGuWarps * 32), p.smem_gu, s,
                         w_gate, w_up, mat_bytes, d, F, offsets, (const int*)w.n_active,
                         (const int*)w.active, (const int*)w.goff, x, x_rows, x_div, x_row_max,
-                        w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.status));
+                        w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.done, w.status));
   }
   MOE_CHECK(check_launch("gateup"));
   {
@@ -956,19 +982,20 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
     MOE_CUDA(launch_pdl(down_kernel<QT>, dim3(p.grid_dn), dim3(kDnWarps * 32), p.smem_dn, s,
                         w_down, mat_bytes, d, F, offsets, (const int*)w.n_active,
                         (const int*)w.active, (const int*)w.goff, (const uint8_t*)w.hfrag, y,
-                        y_rows, p.cgp_dn, p.nst_dn, w.status));
+                        y_rows, p.cgp_dn, p.nst_dn, (const int*)w.done, p.cpe_gu, w.status));
   }
   return check_launch("down");
 }
 
 // Plan arrays inside an experts workspace, for a dispatch that writes them.
 void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
-                         int** goff, int** gexp, int* mg) {
+                         int** goff, int** gexp, int** done, int* mg) {
   ExpertsWs w = carve_experts(ws, rows, E, d, F);
   *n_active = w.n_active;
   *active = w.active;
   *goff = w.goff;
   *gexp = w.gexp;
+  *done = w.done;
   *mg = max_groups(rows, E);
 }
 

@@ -292,18 +292,34 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Bounded wait for an mbarrier phase.  Gives up (returns false; the caller
-// flags MOE_STATUS_TIMEOUT) after ~0.2 s of wall time or 2^24 polls.
+// flags MOE_STATUS_TIMEOUT) after ~0.2 s of wall time or 2^24 polls.  Each
+// poll may suspend the thread in hardware for up to that many ns while the
+// phase is incomplete, so a waiting warp takes few issue slots
+// (MOE_MBAR_SUSPEND_NS, 0 for the hardware's default).
+#ifndef MOE_MBAR_SUSPEND_NS
+#define MOE_MBAR_SUSPEND_NS 20000
+#endif
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
   uint64_t t0 = 0;
   for (uint32_t it = 0; it < (1u << 24); ++it) {
     uint32_t done;
+#if MOE_MBAR_SUSPEND_NS > 0
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity), "n"(MOE_MBAR_SUSPEND_NS)
+        : "memory");
+#else
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
         " selp.u32 %0, 1, 0, p;\n}"
         : "=r"(done)
         : "r"(a), "r"(parity)
         : "memory");
+#endif
     if (done) return true;
     if ((it & 255u) == 0u) {
       const uint64_t now = globaltimer_ns();
