@@ -291,8 +291,7 @@ def run_b200(args):
         uniq = int(np.unique(ids).size)
         rows = int(ids.size)
     else:
-        step()
-        uniq, rows = layer.last["active"], layer.last["rows"]
+        uniq, rows = layer.routing_stats(x)
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -425,6 +424,7 @@ def run_b200(args):
                               f"pre-dequantised ({dq:.1f} s, untimed)"}
 
     if world > 1:
+        layer.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:

@@ -246,6 +246,36 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
                       const float* residual, int32_t* ids_out, float* weights_out,
                       void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* ---- expert parallelism over NVLink peer memory ----------------------------------
+ * One process per GPU of a node.  Each rank allocates an exchange window
+ * (moe_ipc_alloc, moe_ep_window_bytes), shares its IPC handle with the other
+ * ranks (moe_ipc_handle; 64 bytes, exchanged by the caller, e.g. over
+ * torch.distributed) and maps theirs (moe_ipc_open).  moe_ep_forward then runs
+ * one expert-parallel layer step with no host synchronisation and no collective
+ * library: the routed rows are stored straight into the owners' windows, the
+ * owners run their experts on them and store the outputs straight back, and
+ * release/acquire flags carrying `epoch` (1, 2, 3, ... the same on every rank
+ * and step) order each exchange.  Replaces the multi-card MoE of
+ * _moe_ffn_g4_gpu (nightmare_stream.py:4381-4449), which uploads the token to
+ * every card and sums the per-expert outputs on the host. */
+int moe_ipc_alloc(size_t bytes, void** ptr);          /* zeroed device memory */
+int moe_ipc_free(void* ptr);
+int moe_ipc_handle(void* ptr, void* handle_out);       /* 64-byte IPC handle */
+int moe_ipc_open(const void* handle, void** ptr);      /* a peer's window */
+int moe_ipc_close(void* ptr);
+int moe_ep_window_bytes(int W, int E, int T, int k, int d, size_t* bytes);
+/* w: router over all E experts; expert weights of this rank's E / W experts
+ * (experts rank * E/W .. (rank+1) * E/W - 1).  No shared expert. */
+int moe_ep_workspace_bytes(const moe_layer_weights* w, int W, int T, size_t* bytes);
+/* peers: device array of the W window pointers (own window at index rank,
+ * peers' as mapped by moe_ipc_open); window: this rank's window; x, out (T, d)
+ * f32; residual as in moe_layer_forward.  Every rank must call it with the same
+ * T and epoch.  Waits on other ranks give up after about a second and set
+ * MOE_STATUS_TIMEOUT in the status word at the start of workspace. */
+int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* peers, void* window,
+                   const float* x, int T, float* out, const float* residual, int epoch,
+                   void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,6 +70,14 @@ SIGNATURES = {
     "moe_rms_norm": [vp, vp, cf, ci, ci, vp, vp],
     "moe_gather_rows": [vp, vp, ci, ci, ci, vp, vp],
     "moe_ep_local_order": [vp, ci, ci, ci, vp, vp, vp, vp],
+    "moe_ipc_alloc": [csz, ctypes.POINTER(ctypes.c_void_p)],
+    "moe_ipc_free": [vp],
+    "moe_ipc_handle": [vp, vp],
+    "moe_ipc_open": [vp, ctypes.POINTER(ctypes.c_void_p)],
+    "moe_ipc_close": [vp],
+    "moe_ep_window_bytes": [ci, ci, ci, ci, ci, ctypes.POINTER(csz)],
+    "moe_ep_workspace_bytes": [vp, ci, ci, ctypes.POINTER(csz)],
+    "moe_ep_forward": [vp, ci, ci, vp, vp, vp, ci, vp, vp, ci, vp, csz, vp],
     "moe_layer_workspace_bytes": [ctypes.POINTER(MoELayerWeights), ci, ctypes.POINTER(csz)],
     "moe_layer_forward": [ctypes.POINTER(MoELayerWeights), vp, ci, vp, vp, vp, vp, vp, csz, vp],
 }

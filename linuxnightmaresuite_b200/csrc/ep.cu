@@ -1,5 +1,7 @@
 // Expert-parallel helpers: row gather for the send buffer and the owner-side
 // expert order of received rows.
+#include <string.h>
+
 #include "moe_common.cuh"
 
 namespace moe {
@@ -85,6 +87,426 @@ int moe_ep_local_order(const int32_t* recv_counts, int W, int E_local, int max_r
                                                  static_cast<int*>(workspace));
   }
   return moe::check_launch("ep_local_order");
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Expert parallelism over NVLink peer memory.
+//
+// Every rank owns one exchange window (cudaMalloc, shared with the other ranks
+// of the node through CUDA IPC).  Window layout (bytes):
+//   0      recv_flag[32]  int  rank s writes the step's epoch after its rows
+//   128    counters[2]    int  this rank's last-CTA counters (send, return)
+//   256    ret_flag[32]   int  owner o writes the epoch after returning results
+//   512    meta[W][El+1]  int  from source s: rows per local expert, then the
+//                              sorted position of its first row for this rank
+//   recv_x [W][cap][d]    f32  rows from source s at s * cap (cap = T * k); the
+//                              expert outputs overwrite them in place
+//   ret_y  [cap][d]       f32  this rank's expert outputs, in its sorted order
+// One step, with no host synchronisation and no collective library:
+//   router -> dispatch -> ep_send (rows and counts straight into the owners'
+//   windows, then a release flag per owner) -> ep_recv_plan (acquire all
+//   sources' flags, expert order of the received rows, expert plan) ->
+//   grouped experts on the window's rows -> ep_return (outputs straight into
+//   the sources' windows, then a release flag per source) -> ep_wait (acquire
+//   all owners' flags) -> combine.
+// Waits on other ranks are bounded (1 s); a timeout sets MOE_STATUS_TIMEOUT.
+// A source's next send cannot overtake an owner still reading its rows: the
+// source's next step starts after its combine, which waited for every
+// owner's return, which each owner issued after its experts had read them.
+// ===========================================================================
+namespace moe {
+
+constexpr int kEpMaxW = 32;
+
+struct EpWin {
+  size_t recv_flag, counters, ret_flag, meta, recv_x, ret_y, bytes;
+};
+
+static EpWin ep_win(int W, int El, int T, int k, int d) {
+  EpWin w;
+  const size_t cap = (size_t)T * k;
+  w.recv_flag = 0;
+  w.counters = 128;
+  w.ret_flag = 256;
+  w.meta = 512;
+  w.recv_x = 512 + align_up((size_t)W * (El + 1) * sizeof(int), 256);
+  w.ret_y = w.recv_x + align_up((size_t)W * cap * d * sizeof(float), 256);
+  w.bytes = w.ret_y + align_up(cap * d * sizeof(float), 256);
+  return w;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait for a flag written by another GPU: *p >= target (acquire, system
+// scope); gives up after ~1 s.
+__device__ __forceinline__ bool wait_flag_sys(const int* p, int target) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0; it < (1u << 26); ++it) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    if ((it & 63u) == 0u) {
+      const uint64_t now = globaltimer_ns();
+      if (it == 0u) t0 = now;
+      else if (now - t0 > 1000000000ull) return false;
+    }
+    __nanosleep(256);
+  }
+  return false;
+}
+
+struct EpArgs {
+  uint8_t* const* peers;   // W window bases (device array; own window included)
+  uint8_t* win;            // this rank's window
+  EpWin off;
+  int W, El, rank, cap, d, epoch;
+};
+
+// Completion of a multi-CTA send: the last CTA to finish raises every peer's
+// flag (slot `rank` of the flag array at `flag_off`) to the epoch.
+__device__ __forceinline__ void ep_finish(const EpArgs& a, int* ctr, size_t flag_off) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(ctr, 1);
+    if (prev == (int)(gridDim.x * gridDim.y) - 1) {
+      *ctr = 0;
+      __threadfence_system();
+      for (int o = 0; o < a.W; ++o)
+        st_release_sys(reinterpret_cast<int*>(a.peers[o] + flag_off) + a.rank, a.epoch);
+    }
+  }
+}
+
+// Rows in this rank's expert-sorted order -> the owners' windows; counts and
+// base positions -> the owners' meta.  One warp per row.
+__global__ void __launch_bounds__(256)
+ep_send_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm, int k,
+               const int32_t* __restrict__ offsets, int P, EpArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = blockIdx.x * 8 + warp;
+  if (i < P) {
+    int o = 0;   // owner: last rank whose first row is <= i
+    for (int q = 1; q < a.W; ++q)
+      if (offsets[q * a.El] <= i) o = q;
+    const int j = i - offsets[o * a.El];
+    const float4* src = reinterpret_cast<const float4*>(x + (size_t)(perm[i] / k) * a.d);
+    float4* dst = reinterpret_cast<float4*>(
+        reinterpret_cast<float*>(a.peers[o] + a.off.recv_x) + ((size_t)a.rank * a.cap + j) * a.d);
+    for (int v = lane; v < a.d / 4; v += 32) dst[v] = __ldg(src + v);
+  }
+  if (blockIdx.x == 0) {
+    for (int v = threadIdx.x; v < a.W * (a.El + 1); v += blockDim.x) {
+      const int o = v / (a.El + 1), q = v - o * (a.El + 1);
+      const int val = q < a.El ? offsets[o * a.El + q + 1] - offsets[o * a.El + q]
+                               : offsets[o * a.El];
+      reinterpret_cast<int*>(a.peers[o] + a.off.meta)[a.rank * (a.El + 1) + q] = val;
+    }
+  }
+  ep_finish(a, reinterpret_cast<int*>(a.win + a.off.counters), a.off.recv_flag);
+}
+
+// Waits for every source, then: local_offsets / row_map of the received rows
+// in (local expert, source, source order) order, and the grouped experts' plan.
+__global__ void __launch_bounds__(1024)
+ep_recv_plan_kernel(EpArgs a, int32_t* __restrict__ loff, int32_t* __restrict__ row_map,
+                    int* __restrict__ n_active, int* __restrict__ active, int* __restrict__ goff,
+                    int* __restrict__ gexp, int* __restrict__ done, int max_groups,
+                    int* __restrict__ status) {
+  __shared__ int sh[33];
+  __shared__ int rc[1024];             // clamped counts [src][e]
+  __shared__ int start[1024];
+  __shared__ int dest[1024];
+  __shared__ int ok_s;
+  const int i = threadIdx.x;
+  if (i == 0) ok_s = 1;
+  __syncthreads();
+  if (i < a.W) {
+    if (!wait_flag_sys(reinterpret_cast<const int*>(a.win + a.off.recv_flag) + i, a.epoch))
+      ok_s = 0;
+  }
+  __syncthreads();
+  if (!ok_s && i == 0) set_status(status, MOE_STATUS_TIMEOUT);
+  const int* meta = reinterpret_cast<const int*>(a.win + a.off.meta);
+  const int WE = a.W * a.El;
+  // counts, clamped so that no source overruns its cap rows
+  int n = 0;
+  if (i < WE) {
+    const int src = i / a.El;
+    n = ok_s ? meta[src * (a.El + 1) + (i - src * a.El)] : 0;
+    n = n < 0 ? 0 : (n > a.cap ? a.cap : n);
+  }
+  // source-major prefix; minus the source's first entry = prefix within the
+  // source, so the receive position is s * cap + that
+  int tot;
+  const int st = block_excl_scan(n, sh, tot);
+  if (i < WE) {
+    start[i] = st;
+    rc[i] = n;
+  }
+  __syncthreads();
+  int within = 0;
+  if (i < WE) {
+    const int src = i / a.El;
+    within = st - start[src * a.El];
+    if (within + n > a.cap) within = a.cap - n;   // overrun guard (corrupt counts)
+  }
+  __syncthreads();
+  if (i < WE) start[i] = (i / a.El) * a.cap + within;
+  __syncthreads();
+  // expert-major order j = e * W + src
+  const int e = i / a.W, src = i - (i / a.W) * a.W;
+  const int nj = i < WE ? rc[src * a.El + e] : 0;
+  int tot2;
+  const int dj = block_excl_scan(nj, sh, tot2);
+  if (i < WE) dest[src * a.El + e] = dj;
+  __syncthreads();
+  const bool over = tot2 > a.W * a.cap;   // only with corrupt counts
+  if (over && i == 0) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+  if (i < a.El) loff[i] = over ? 0 : dest[i];
+  if (i == 0) loff[a.El] = over ? 0 : tot2;
+  if (!over) {
+    for (int b = 0; b < WE; ++b) {
+      const int cnt = rc[b];
+      for (int q = i; q < cnt; q += blockDim.x) row_map[dest[b] + q] = start[b] + q;
+    }
+  }
+  // plan of the grouped experts (as the dispatch kernel writes it)
+  const int el = i;
+  int ne = 0;
+  if (el < a.El && !over) {
+    for (int s2 = 0; s2 < a.W; ++s2) ne += rc[s2 * a.El + el];
+  }
+  const int ng = (ne + 3) / 4;
+  int tot_g, tot_a;
+  const int g0 = block_excl_scan(ng, sh, tot_g);
+  const int a0 = block_excl_scan(ne > 0 ? 1 : 0, sh, tot_a);
+  const bool overflow = tot_g > max_groups;
+  if (el < a.El) {
+    goff[el] = g0;
+    done[el] = 0;
+    if (ne > 0) active[a0] = el;
+    if (!overflow)
+      for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = el;
+  }
+  if (el == 0) {
+    goff[a.El] = tot_g;
+    *n_active = overflow ? 0 : tot_a;
+    if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+  }
+}
+
+// Expert outputs of the rows received from source s (in place in recv_x) ->
+// source s's ret_y at its sorted positions.  Grid (row chunks of 8, W).
+__global__ void __launch_bounds__(256)
+ep_return_kernel(EpArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int s = blockIdx.y;
+  const int i = blockIdx.x * 8 + warp;
+  const int* meta = reinterpret_cast<const int*>(a.win + a.off.meta) + s * (a.El + 1);
+  int rows = 0;
+  for (int e = 0; e < a.El; ++e) {
+    const int c = meta[e];
+    rows += c < 0 ? 0 : c;
+  }
+  rows = rows > a.cap ? a.cap : rows;
+  int base = meta[a.El];
+  base = base < 0 ? 0 : (base > a.cap - rows ? a.cap - rows : base);
+  if (i < rows) {
+    const float4* src = reinterpret_cast<const float4*>(
+        reinterpret_cast<const float*>(a.win + a.off.recv_x) + ((size_t)s * a.cap + i) * a.d);
+    float4* dst = reinterpret_cast<float4*>(
+        reinterpret_cast<float*>(a.peers[s] + a.off.ret_y) + (size_t)(base + i) * a.d);
+    for (int v = lane; v < a.d / 4; v += 32) dst[v] = src[v];
+  }
+  ep_finish(a, reinterpret_cast<int*>(a.win + a.off.counters) + 1, a.off.ret_flag);
+}
+
+// Waits until every owner has returned this step's outputs.
+__global__ void ep_wait_kernel(EpArgs a, int* __restrict__ status) {
+  if ((int)threadIdx.x < a.W &&
+      !wait_flag_sys(reinterpret_cast<const int*>(a.win + a.off.ret_flag) + threadIdx.x, a.epoch))
+    set_status(status, MOE_STATUS_TIMEOUT);
+}
+
+int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
+                  int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream, float* row_max);
+int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
+                            int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
+                            int* active, int* goff, int* gexp, int* done, int max_groups,
+                            cudaStream_t s);
+int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes);
+void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
+                         int** goff, int** gexp, int** done, int* mg);
+int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
+                int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
+                size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
+                bool planned, int rows_hint);
+int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
+                   const float* residual, int T, int k, int d, float* out, cudaStream_t s);
+
+struct EpWs {
+  int* status;
+  uint8_t* router_ws;
+  size_t router_bytes;
+  int32_t* ids;
+  float* wts;
+  int32_t* offsets;
+  int32_t* perm;
+  int32_t* inv;
+  int32_t* loff;
+  int32_t* row_map;
+  uint8_t* exp_ws;
+  size_t exp_bytes;
+  size_t bytes;
+};
+
+static EpWs carve_ep(void* ws, const moe_layer_weights* w, int W, int T) {
+  Carve c{static_cast<uint8_t*>(ws), 0, 0};
+  EpWs L;
+  const int El = w->E / W;
+  const size_t P = (size_t)T * w->k;
+  const int R = (int)(P * W);
+  L.status = c.take<int>(64);
+  moe_router_workspace_bytes(T, w->d, w->E, &L.router_bytes);
+  L.router_ws = c.take<uint8_t>(L.router_bytes);
+  L.ids = c.take<int32_t>(P);
+  L.wts = c.take<float>(P);
+  L.offsets = c.take<int32_t>(w->E + 1);
+  L.perm = c.take<int32_t>(P);
+  L.inv = c.take<int32_t>(P);
+  L.loff = c.take<int32_t>(El + 1);
+  L.row_map = c.take<int32_t>(R);
+  experts_workspace_hint(R, (int)P, El, w->d, w->F, &L.exp_bytes);
+  L.exp_ws = c.take<uint8_t>(L.exp_bytes);
+  L.bytes = align_up(c.used, 256);
+  return L;
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_ipc_alloc(size_t bytes, void** ptr) {
+  MOE_REQUIRE(ptr && bytes > 0, MOE_ERR_INVALID, "bad allocation request");
+  void* p = nullptr;
+  MOE_CUDA(cudaMalloc(&p, bytes));
+  MOE_CUDA(cudaMemset(p, 0, bytes));
+  MOE_CUDA(cudaDeviceSynchronize());
+  *ptr = p;
+  return MOE_OK;
+}
+
+int moe_ipc_free(void* ptr) {
+  if (ptr) MOE_CUDA(cudaFree(ptr));
+  return MOE_OK;
+}
+
+int moe_ipc_handle(void* ptr, void* handle) {
+  MOE_REQUIRE(ptr && handle, MOE_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  MOE_CUDA(cudaIpcGetMemHandle(&h, ptr));
+  memcpy(handle, &h, sizeof(h));
+  return MOE_OK;
+}
+
+int moe_ipc_open(const void* handle, void** ptr) {
+  MOE_REQUIRE(ptr && handle, MOE_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  MOE_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = p;
+  return MOE_OK;
+}
+
+int moe_ipc_close(void* ptr) {
+  if (ptr) MOE_CUDA(cudaIpcCloseMemHandle(ptr));
+  return MOE_OK;
+}
+
+int moe_ep_window_bytes(int W, int E, int T, int k, int d, size_t* bytes) {
+  MOE_REQUIRE(bytes, MOE_ERR_INVALID, "null output pointer");
+  MOE_REQUIRE(W > 0 && W <= moe::kEpMaxW && E % W == 0 && T > 0 && k > 0 && d > 0,
+              MOE_ERR_INVALID, "bad expert-parallel shape");
+  *bytes = moe::ep_win(W, E / W, T, k, d).bytes;
+  return MOE_OK;
+}
+
+int moe_ep_workspace_bytes(const moe_layer_weights* w, int W, int T, size_t* bytes) {
+  MOE_REQUIRE(w && bytes, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(W > 0 && w->E % W == 0 && T > 0, MOE_ERR_INVALID, "bad expert-parallel shape");
+  *bytes = moe::carve_ep(nullptr, w, W, T).bytes;
+  return MOE_OK;
+}
+
+int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* peers, void* window,
+                   const float* x, int T, float* out, const float* residual, int epoch,
+                   void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  using namespace moe;
+  MOE_REQUIRE(w && peers && window && x && out && workspace, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(W > 0 && W <= kEpMaxW && rank >= 0 && rank < W && w->E % W == 0,
+              MOE_ERR_INVALID, "bad expert-parallel shape (W=%d rank=%d E=%d)", W, rank, w->E);
+  MOE_REQUIRE(T > 0 && epoch > 0, MOE_ERR_INVALID, "T and epoch must be positive");
+  MOE_REQUIRE(!w->s_gate, MOE_ERR_UNSUPPORTED, "shared expert in the expert-parallel layer");
+  const int El = w->E / W;
+  MOE_REQUIRE(W * El <= 1024, MOE_ERR_UNSUPPORTED, "W * E_local must be <= 1024");
+  MOE_REQUIRE(w->d % 4 == 0, MOE_ERR_UNSUPPORTED, "d must be a multiple of 4");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  EpWs L = carve_ep(workspace, w, W, T);
+  MOE_REQUIRE(workspace_bytes >= L.bytes, MOE_ERR_WORKSPACE, "ep workspace %zu < %zu",
+              workspace_bytes, L.bytes);
+  const int P = T * w->k;
+  EpArgs a;
+  a.peers = reinterpret_cast<uint8_t* const*>(peers);
+  a.win = static_cast<uint8_t*>(window);
+  a.off = ep_win(W, El, T, w->k, w->d);
+  a.W = W;
+  a.El = El;
+  a.rank = rank;
+  a.cap = P;
+  a.d = w->d;
+  a.epoch = epoch;
+  MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
+                          L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr));
+  MOE_CHECK(launch_dispatch_planned(L.ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
+                                    nullptr, nullptr, nullptr, nullptr, nullptr, 0, s));
+  {
+    ::moe::ProfScope _prof(MOE_K_AUX, s);
+    ep_send_kernel<<<(P + 7) / 8, 256, 0, s>>>(x, L.perm, w->k, L.offsets, P, a);
+  }
+  MOE_CHECK(check_launch("ep_send"));
+  const int R = P * W;
+  int *n_active, *active, *goff, *gexp, *done, mg;
+  experts_plan_arrays(L.exp_ws, R, El, w->d, w->F, &n_active, &active, &goff, &gexp, &done, &mg);
+  {
+    ::moe::ProfScope _prof(MOE_K_AUX, s);
+    ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, gexp,
+                                           done, mg, L.status);
+  }
+  MOE_CHECK(check_launch("ep_recv_plan"));
+  float* recv = reinterpret_cast<float*>(a.win + a.off.recv_x);
+  MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.loff, El, R, recv, L.row_map,
+                        1, w->d, w->F, recv, L.row_map, L.exp_ws, L.exp_bytes, s, L.status,
+                        nullptr, true, P));
+  {
+    ::moe::ProfScope _prof(MOE_K_AUX, s);
+    ep_return_kernel<<<dim3((P + 7) / 8, W), 256, 0, s>>>(a);
+  }
+  MOE_CHECK(check_launch("ep_return"));
+  {
+    ::moe::ProfScope _prof(MOE_K_AUX, s);
+    ep_wait_kernel<<<1, 32, 0, s>>>(a, L.status);
+  }
+  MOE_CHECK(check_launch("ep_wait"));
+  return launch_combine(reinterpret_cast<const float*>(a.win + a.off.ret_y), L.inv, L.wts,
+                        nullptr, residual, T, w->k, w->d, out, s);
 }
 
 }  // extern "C"

@@ -887,11 +887,18 @@ static bool use_tc(int rows, int E, int d, int F) {
   return active > 0 && rows / active >= kTcMinMeanRows && tc_supported(rows, E, d, F);
 }
 
-int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
+// rows: the most rows a call may see (buffers); rows_hint: the rows it is
+// expected to see, which picks the GEMV or the tensor-core path.
+int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes) {
   size_t a = carve_experts(nullptr, rows, E, d, F).bytes;
-  if (use_tc(rows, E, d, F)) a = std::max(a, tc_workspace(rows, E, d, F));
+  if (use_tc(rows_hint > 0 ? rows_hint : rows, E, d, F))
+    a = std::max(a, tc_workspace(rows, E, d, F));
   *bytes = a;
   return MOE_OK;
+}
+
+int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
+  return experts_workspace_hint(rows, rows, E, d, F, bytes);
 }
 
 // Launch shape of the two GEMV kernels for a call.
@@ -1003,7 +1010,7 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
                 size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
-                bool planned) {
+                bool planned, int rows_hint) {
   MOE_REQUIRE(qtype_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
   MOE_REQUIRE(E > 0 && E <= kPlanThreads, MOE_ERR_UNSUPPORTED, "local expert count %d", E);
   MOE_REQUIRE(d > 0 && F > 0 && d % 64 == 0 && F % 64 == 0, MOE_ERR_UNSUPPORTED,
@@ -1015,7 +1022,7 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
   MOE_REQUIRE(x_div > 0, MOE_ERR_INVALID, "x_rows_div must be positive");
   MOE_REQUIRE(((uintptr_t)w_gate | (uintptr_t)w_up | (uintptr_t)w_down | (uintptr_t)x) % 16 == 0,
               MOE_ERR_INVALID, "weights and activations must be 16-byte aligned");
-  if (use_tc(rows, E, d, F))
+  if (use_tc(rows_hint > 0 ? rows_hint : rows, E, d, F))
     return run_experts_tc(w_gate, w_up, w_down, qtype, offsets, E, rows, x, x_rows, x_div,
                           x_row_max, d, F, y, y_rows, ws, ws_bytes, status, s);
   ExpertsWs w = carve_experts(ws, rows, E, d, F);
@@ -1046,7 +1053,7 @@ int moe_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 moe_stream_t stream) {
   return moe::run_experts(w_gate, w_up, w_down, qtype, expert_offsets, E_local, rows, x, x_rows,
                           x_rows_div, d, F, y, y_rows, workspace, workspace_bytes,
-                          reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, false);
+                          reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, false, 0);
 }
 
 }  // extern "C"

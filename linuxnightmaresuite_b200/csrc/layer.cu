@@ -8,7 +8,7 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
                 size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
-                bool planned);
+                bool planned, int rows_hint);
 void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
                          int** goff, int** gexp, int** done, int* mg);
 int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
@@ -113,7 +113,7 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
                                     n_active, active, goff, gexp, done, mg, s));
   MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
                         w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
-                        L.row_max, true));
+                        L.row_max, true, 0));
   if (w->s_gate) {
     {
       ::moe::ProfScope _prof(MOE_K_AUX, s);
@@ -122,7 +122,7 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
     MOE_CHECK(check_launch("fill_offsets"));
     MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
                           nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.exp_ws, L.exp_bytes, s,
-                          L.status, L.row_max, false));
+                          L.status, L.row_max, false, 0));
   }
   return launch_combine(L.y, L.inv, wts, L.s_y, residual, T, w->k, w->d, out, s);
 }

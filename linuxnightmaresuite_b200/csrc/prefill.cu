@@ -239,11 +239,12 @@ __device__ __forceinline__ void store_packed_tile(const PackedTile<QT>& p, int l
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 tc_prep_kernel(const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
-               const float* __restrict__ x_row_max, int P, int d, float* __restrict__ row_scale,
-               __half* __restrict__ planes) {
+               const float* __restrict__ x_row_max, int P, const int32_t* __restrict__ offsets,
+               int E, int d, float* __restrict__ row_scale, __half* __restrict__ planes) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * 8 + warp;
-  if (r >= P) return;
+  // P bounds the planes; the routed rows are offsets[E] <= P of them
+  if (r >= P || r >= offsets[E]) return;
   const int src = x_rows ? x_rows[r] / x_div : r;
   const float4* s4 = reinterpret_cast<const float4*>(x + (size_t)src * d);
   float m = 0.f;
@@ -625,8 +626,8 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   MOE_CHECK(check_launch("tc_tile_plan"));
   {
     ::moe::ProfScope _prof(MOE_K_XPREP, s);
-    tc_prep_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, x_rows, x_div, x_row_max, rows, d,
-                                                  w.row_scale, w.x_planes);
+    tc_prep_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, x_rows, x_div, x_row_max, rows, offsets, E,
+                                                  d, w.row_scale, w.x_planes);
   }
   MOE_CHECK(check_launch("tc_prep"));
   CUtensorMap xmap, hmap;

@@ -1,30 +1,26 @@
-"""Expert-parallel MoE layer over torch.distributed (NCCL on B200s).
+"""Expert-parallel MoE layer, one process per GPU of a node.
 
 Each of the W ranks owns a contiguous block of E / W experts and its own
-tokens.  One layer forward:
-
-1. route the rank's tokens with the full router (all E experts);
-2. stable-sort the (token, slot) pairs by expert (``moe_dispatch``); because
-   experts are contiguous per rank, the sorted rows are grouped by owner;
-3. exchange per-expert row counts (one small all-to-all) -- this fixes every
-   split of the payload exchange;
-4. all-to-all the routed activation rows to the experts' owners;
-5. run the owner's experts on the received rows, in expert order
-   (``moe_experts`` with a gather / scatter row map), writing each result back
-   into its received position;
-6. all-to-all the results back (the reverse splits);
-7. combine each token's k results in router order (``moe_combine``).
+tokens.  ``EPMoELayer`` runs one layer step as device work only, through
+``moe_ep_forward``: router -> dispatch -> the routed rows are stored straight
+into the owners' exchange windows over NVLink (CUDA IPC mappings) -> each owner
+runs its experts on the rows it received -> the outputs are stored straight
+back into the sources' windows -> combine.  Release/acquire flags carrying a
+step counter order the two exchanges; there is no host synchronisation and no
+collective library on the data path (torch.distributed only shares the IPC
+handles at set-up).
 
 The reference has no collective at all: its multi-GPU MoE uploads the token
 to every card and sums per-expert outputs on the host
 (nightmare_stream.py:4381-4449).
 
-The bookkeeping of steps 3-5 (``exchange_plan``, ``local_order``) is plain
-numpy so it can be checked on CPU ranks; ``EPMoELayer`` drives the device
-kernels.
+The bookkeeping of the exchange (``exchange_plan``, ``local_order``) is also
+written out in numpy, with a collective version (``ep_exchange``) that runs on
+CPU ranks (gloo); it states what the device kernels compute.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Sequence, Tuple
 
 import numpy as np
@@ -105,55 +101,120 @@ def ep_exchange(send: torch.Tensor, counts: torch.Tensor, expert_fn, group=None)
 
 
 class EPMoELayer:
-    """One MoE layer sharded over the ranks of ``group`` by expert."""
+    """One MoE layer sharded over the ranks of ``group`` by expert; this rank
+    holds experts ``expert_range(rank, W, E)`` and routes its own tokens."""
 
     def __init__(self, gate_weight, w_gate, w_up, w_down, qtype: int, top_k: int,
                  mode: int = 0, bias=None, group=None, device=None):
         from . import kernels as K
-        from .moe_forward import MoERouter, _to_dev_u8, _device
-        self.K = K
+        from . import _lib
+        from .moe_forward import _to_dev_u8, _device
+        self.K, self._lib = K, _lib
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.device = _device(device)
         d, E = int(gate_weight.shape[0]), int(gate_weight.shape[1])
-        self.d, self.E, self.k, self.qtype = d, E, top_k, qtype
+        self.d, self.E, self.k, self.qtype, self.mode = d, E, top_k, qtype, mode
         self.e0, self.e1 = expert_range(self.rank, self.world, E)
         self.F = int(w_gate.shape[1])
-        self.router = MoERouter(gate_weight, E, top_k, mode, bias, self.device)
+        dev = self.device
+        self.gate_w = torch.as_tensor(np.ascontiguousarray(gate_weight, dtype=np.float32)).to(dev)
+        self.bias = None if bias is None else torch.as_tensor(
+            np.ascontiguousarray(bias, dtype=np.float32)).to(dev)
         sl = slice(self.e0, self.e1)
         El = self.e1 - self.e0
-        self.w_gate = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_gate[sl]), self.device),
+        self.w_gate = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_gate[sl]), dev),
                                      qtype, El, self.F, d)
-        self.w_up = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_up[sl]), self.device),
+        self.w_up = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_up[sl]), dev),
                                    qtype, El, self.F, d)
-        self.w_down = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_down[sl]), self.device),
+        self.w_down = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_down[sl]), dev),
                                      qtype, El, d, self.F)
-        self._ws = None
-        self.last = {}
+        self.lw = K.LayerWeights(self.gate_w, self.w_gate, self.w_up, self.w_down, qtype, E,
+                                 top_k, d, self.F, mode, self.bias)
+        self._T = None
+        self._window = None
+        self._mapped = []
+        self.epoch = 0
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """All device work; one small device->host read per step (the row
-        counts, which NCCL needs as split sizes)."""
+    # ------------------------------------------------------------------ set-up
+    def _setup(self, T: int) -> None:
+        _lib, K = self._lib, self.K
+        self.close()
+        W, rank = self.world, self.rank
+        nbytes = ctypes.c_size_t(0)
+        _lib.call("moe_ep_window_bytes", W, self.E, T, self.k, self.d, ctypes.byref(nbytes))
+        win = ctypes.c_void_p(0)
+        _lib.call("moe_ipc_alloc", nbytes.value, ctypes.byref(win))
+        self._window = win.value
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.call("moe_ipc_handle", ctypes.c_void_p(self._window), ctypes.cast(handle, ctypes.c_void_p))
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        allh = [torch.empty_like(mine) for _ in range(W)]
+        dist.all_gather(allh, mine, group=self.group)
+        ptrs = []
+        for s_ in range(W):
+            if s_ == rank:
+                ptrs.append(self._window)
+                continue
+            h = (ctypes.c_uint8 * 64)(*allh[s_].cpu().tolist())
+            p = ctypes.c_void_p(0)
+            _lib.call("moe_ipc_open", ctypes.cast(h, ctypes.c_void_p), ctypes.byref(p))
+            self._mapped.append(p.value)
+            ptrs.append(p.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        wsb = ctypes.c_size_t(0)
+        _lib.call("moe_ep_workspace_bytes", ctypes.byref(self.lw.c), W, T, ctypes.byref(wsb))
+        self.ws = K.workspace(wsb.value, self.device)
+        self.ws[:256].zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._T = T
+        self.epoch = 0
+
+    def close(self) -> None:
+        """Unmap the peers' windows and free this rank's (collective)."""
+        if self._window is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._mapped:
+            self._lib.call("moe_ipc_close", ctypes.c_void_p(p))
+        self._mapped = []
+        dist.barrier(group=self.group)
+        self._lib.call("moe_ipc_free", ctypes.c_void_p(self._window))
+        self._window = None
+        self._T = None
+
+    # ------------------------------------------------------------------ step
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One expert-parallel step for this rank's tokens x (T, d); every rank
+        calls it with the same T.  Device work only."""
         K = self.K
-        ids, w = self.router.route_batch(x)
-        off, perm, inv = K.dispatch(ids, self.E)
-        counts = torch.diff(off).to(torch.int32).reshape(self.world, -1)
-        recv_counts = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts, counts, group=self.group)
-        send = K.gather_rows(x, perm, self.k)          # expert-sorted, owner-grouped
-        both = torch.stack([counts, recv_counts]).cpu().numpy()
-        send_rows = both[0].sum(axis=1)
-        recv_rows = both[1].sum(axis=1)
-        recv = all_to_all_rows(send, send_rows, recv_rows, self.group)
-        R = int(recv_rows.sum())
-        self.last = {"rows": R, "active": int(np.count_nonzero(both[1].sum(axis=0)))}
-        y_recv = torch.empty((R, self.d), dtype=torch.float32, device=x.device)
-        if R:
-            if self._ws is None or self._ws.device != x.device:
-                self._ws = torch.zeros(256, dtype=torch.uint8, device=x.device)
-            loff, row_map = K.ep_local_order(recv_counts, R, self._ws)
-            K.experts(self.w_gate, self.w_up, self.w_down, self.qtype, loff, recv, self.d, self.F,
-                      x_rows=row_map, x_rows_div=1, y=y_recv, y_rows=row_map, rows=R)
-        y_sorted = all_to_all_rows(y_recv, recv_rows, send_rows, self.group)
-        return K.combine(y_sorted, inv, w)
+        K._need(x, torch.float32, "x")
+        T = int(x.shape[0])
+        if self._T != T:
+            self._setup(T)
+        if out is None:
+            out = torch.empty_like(x)
+        self.epoch += 1
+        self._lib.call("moe_ep_forward", ctypes.byref(self.lw.c), self.world, self.rank,
+                       ctypes.c_void_p(self.peers.data_ptr()), ctypes.c_void_p(self._window),
+                       K._ptr(x), T, K._ptr(out), K._ptr(residual), self.epoch, K._ptr(self.ws),
+                       self.ws.numel(), K._stream())
+        return out
+
+    def device_status(self) -> int:
+        return self.K.read_status(self.ws) if self._window is not None else 0
+
+    def routing_stats(self, x: torch.Tensor) -> Tuple[int, int]:
+        """(active local experts, rows this rank's experts receive) for a step
+        on x: routes every rank's tokens and sums the per-expert counts over
+        the ranks (a collective with a host read; not for timed regions)."""
+        K = self.K
+        ids, _ = K.router(x, self.gate_w, self.k, self.mode, self.bias)
+        cnt = torch.bincount(ids.reshape(-1).long(), minlength=self.E).to(torch.int64)
+        dist.all_reduce(cnt, group=self.group)
+        local = cnt[self.e0:self.e1].cpu().numpy()
+        return int(np.count_nonzero(local)), int(local.sum())

@@ -1,4 +1,5 @@
-"""Expert-parallel layer on 2 GPUs over NCCL against the single-GPU layer.
+"""Expert-parallel layer on 2 GPUs (NVLink peer-memory exchange) against the
+single-GPU layer.
 
 Runs as child processes (one per GPU); skipped when fewer than 2 GPUs are
 visible.  NVLink multicast (NVLS) is off so a failing rank cannot leave a
@@ -45,7 +46,8 @@ def _worker(rank, world, port, out_q):
         x = torch.from_numpy(np.ascontiguousarray(data.x[rank * T:(rank + 1) * T])).to(dev)
         out = layer.forward(x).cpu().numpy()
         out2 = layer.forward(x).cpu().numpy()
-        out_q.put((rank, out, out2))
+        out_q.put((rank, out, out2, layer.device_status()))
+        layer.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -69,7 +71,8 @@ def test_ep_two_gpus_match_single_gpu():
         p.start()
     res = {}
     for _ in range(world):
-        r, out, out2 = q.get(timeout=300)
+        r, out, out2, st = q.get(timeout=300)
+        assert st == 0, (r, st)
         res[r] = (out, out2)
     for p in procs:
         p.join(timeout=120)
