@@ -131,21 +131,6 @@ __device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, float (&v)[32], int 
 // ---------------------------------------------------------------------------
 // weight dequantisation into the swizzled B tile
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void split_store8(uint8_t* hi_row, uint8_t* lo_row, int chunk,
-                                             const float (&w)[8]) {
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 hh = __floats2half2_rn(w[2 * i], w[2 * i + 1]);
-    const float2 hf = __half22float2(hh);
-    const __half2 ll = __floats2half2_rn(w[2 * i] - hf.x, w[2 * i + 1] - hf.y);
-    h[i] = *reinterpret_cast<const uint32_t*>(&hh);
-    l[i] = *reinterpret_cast<const uint32_t*>(&ll);
-  }
-  *reinterpret_cast<uint4*>(hi_row + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-  *reinterpret_cast<uint4*>(lo_row + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
-}
-
 // Registers of one packed 16-row x 64-column weight tile for one lane.
 template <int QT>
 struct PackedTile {
@@ -162,19 +147,27 @@ __device__ __forceinline__ void load_packed_tile(PackedTile<QT>& p, const uint8_
   p.sc = __ldg(reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + (lane >> 2) * 8));
 }
 
+// w = d * q split into fp16 hi = rn(w) and lo = rn(w - hi), two at a time:
+// the f16x2 multiply rounds the exact product, and the fused multiply-add
+// rounds the exact residual d*q - hi (d: fp16, q: small integer, so both are
+// what an f32 detour would give).
+__device__ __forceinline__ void split_mul2(uint32_t q2, uint32_t d2, uint32_t& hi, uint32_t& lo) {
+  asm("{\n .reg .b32 nh;\n mul.rn.f16x2 %0, %2, %3;\n neg.f16x2 nh, %0;\n"
+      " fma.rn.f16x2 %1, %2, %3, nh;\n}"
+      : "=r"(hi), "=r"(lo)
+      : "r"(q2), "r"(d2));
+}
+
 // One packed tile (registers) -> rows [r0, r0+16) of the swizzled hi / lo B
 // tiles.  Lane (g, t) owns rows g and g + 8 and, per 32-wide block, the
-// elements its fragment layout assigns to t.  Odd rows write their blocks in
-// the opposite order so the eight lanes of a store phase hit distinct 16-byte
-// chunks (no bank conflicts).
+// elements its fragment layout assigns to t.  Quants become exact fp16
+// integers (magic-number adds), then d * q is split in packed fp16 math.
+// Odd rows write their blocks in the opposite order so the lanes of a store
+// phase hit distinct 16-byte chunks (no bank conflicts).
 template <int QT>
 __device__ __forceinline__ void store_packed_tile(const PackedTile<QT>& p, int lane, uint8_t* bhi,
                                                   uint8_t* blo, int r0) {
   const int g = lane >> 2, t = lane & 3;
-  const float s[4] = {__half2float(__ushort_as_half((unsigned short)(p.sc.x & 0xFFFF))),
-                      __half2float(__ushort_as_half((unsigned short)(p.sc.x >> 16))),
-                      __half2float(__ushort_as_half((unsigned short)(p.sc.y & 0xFFFF))),
-                      __half2float(__ushort_as_half((unsigned short)(p.sc.y >> 16)))};
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int row = r0 + g + 8 * half;
@@ -183,51 +176,43 @@ __device__ __forceinline__ void store_packed_tile(const PackedTile<QT>& p, int l
 #pragma unroll
     for (int it = 0; it < 2; ++it) {
       const int b = it ^ (g & 1);
-      const float d = s[half * 2 + b];
+      const int j = half * 2 + b;                        // scale slot
+      const uint32_t sw = j < 2 ? p.sc.x : p.sc.y;
+      const uint32_t d2 = prmt(sw, sw, (j & 1) ? 0x3232u : 0x1010u);   // {d, d}
       if (QT == MOE_Q8_0) {
         const uint4& qv = p.q[QT == MOE_Q8_0 ? half : 0];   // row g: q[0], row g+8: q[1]
         const uint32_t w0 = b ? qv.z : qv.x, w1 = b ? qv.w : qv.y;
-        float w[8];
+        uint32_t q[4], h[4], l[4];
+        dequant_q8(w0, q[0], q[1]);
+        dequant_q8(w1, q[2], q[3]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const uint32_t word = i < 4 ? w0 : w1;
-          w[i] = d * (float)(int)(int8_t)((word >> (8 * (i & 3))) & 0xFF);
-        }
+        for (int i = 0; i < 4; ++i) split_mul2(q[i], d2, h[i], l[i]);
         // elements 32b + 8t .. +7 -> 16-byte chunk 4b + t, swizzled by row
-        split_store8(hr, lr, (4 * b + t) ^ (row & 7), w);
+        const int ch = (4 * b + t) ^ (row & 7);
+        *reinterpret_cast<uint4*>(hr + ch * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(lr + ch * 16) = make_uint4(l[0], l[1], l[2], l[3]);
       } else {
         const uint32_t word = half ? (b ? p.q[0].w : p.q[0].z) : (b ? p.q[0].y : p.q[0].x);
-        float lo4[4], hi4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t byte = (word >> (8 * i)) & 0xFF;
-          lo4[i] = d * (float)((int)(byte & 0xF) - 8);   // element 32b + 4t + i
-          hi4[i] = d * (float)((int)(byte >> 4) - 8);    // element 32b + 16 + 4t + i
-        }
+        // bytes i = 0..3 hold element 4t + i (low nibble) and 16 + 4t + i (high)
+        const uint32_t p01 = prmt(word, 0u, 0x4140u), p23 = prmt(word, 0u, 0x4342u);
+        const uint32_t kMagic = 0x64006400u, kSubLo = 0xE408E408u;   // 1024, -1032
+        const uint32_t kMulHi = 0x2C002C00u, kSubHi = 0xD480D480u;   // 1/16, -72
+        const uint32_t lq01 = hadd2_u(lop3_and_or(p01, 0x000F000Fu, kMagic), kSubLo);
+        const uint32_t lq23 = hadd2_u(lop3_and_or(p23, 0x000F000Fu, kMagic), kSubLo);
+        const uint32_t hq01 = hfma2_u(lop3_and_or(p01, 0x00F000F0u, kMagic), kMulHi, kSubHi);
+        const uint32_t hq23 = hfma2_u(lop3_and_or(p23, 0x00F000F0u, kMagic), kMulHi, kSubHi);
+        uint32_t h0, h1, l0, l1;
         const int ch_lo = (4 * b + (t >> 1)) ^ (row & 7);
         const int ch_hi = (4 * b + 2 + (t >> 1)) ^ (row & 7);
         const int off = (t & 1) * 8;
-        uint32_t h[2], l[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const __half2 hh = __floats2half2_rn(lo4[2 * i], lo4[2 * i + 1]);
-          const float2 hf = __half22float2(hh);
-          const __half2 ll = __floats2half2_rn(lo4[2 * i] - hf.x, lo4[2 * i + 1] - hf.y);
-          h[i] = *reinterpret_cast<const uint32_t*>(&hh);
-          l[i] = *reinterpret_cast<const uint32_t*>(&ll);
-        }
-        *reinterpret_cast<uint2*>(hr + ch_lo * 16 + off) = make_uint2(h[0], h[1]);
-        *reinterpret_cast<uint2*>(lr + ch_lo * 16 + off) = make_uint2(l[0], l[1]);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const __half2 hh = __floats2half2_rn(hi4[2 * i], hi4[2 * i + 1]);
-          const float2 hf = __half22float2(hh);
-          const __half2 ll = __floats2half2_rn(hi4[2 * i] - hf.x, hi4[2 * i + 1] - hf.y);
-          h[i] = *reinterpret_cast<const uint32_t*>(&hh);
-          l[i] = *reinterpret_cast<const uint32_t*>(&ll);
-        }
-        *reinterpret_cast<uint2*>(hr + ch_hi * 16 + off) = make_uint2(h[0], h[1]);
-        *reinterpret_cast<uint2*>(lr + ch_hi * 16 + off) = make_uint2(l[0], l[1]);
+        split_mul2(lq01, d2, h0, l0);
+        split_mul2(lq23, d2, h1, l1);
+        *reinterpret_cast<uint2*>(hr + ch_lo * 16 + off) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(lr + ch_lo * 16 + off) = make_uint2(l0, l1);
+        split_mul2(hq01, d2, h0, l0);
+        split_mul2(hq23, d2, h1, l1);
+        *reinterpret_cast<uint2*>(hr + ch_hi * 16 + off) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2*>(lr + ch_hi * 16 + off) = make_uint2(l0, l1);
       }
     }
   }
