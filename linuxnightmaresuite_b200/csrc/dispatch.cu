@@ -10,6 +10,8 @@
 // lowest lane of each group updates the warp's private counter for that
 // expert; counters are then prefix-summed over warps (in warp order) and over
 // experts, and a second pass ranks each pair inside its round.
+#include <algorithm>
+
 #include "moe_common.cuh"
 
 namespace moe {
@@ -135,15 +137,190 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
   }
 }
 
+// ---------------------------------------------------------------------------
+// Chunked dispatch for many pairs (prefill): the same stable order from three
+// launches.  Chunk c holds pairs [c * chunk, (c + 1) * chunk).
+//   count:   per-chunk expert counts (shared-memory integer adds; order-free)
+//   scan:    expert offsets, each chunk's first slot per expert, the plan
+//   scatter: per chunk, warp counts + in-warp ranks as in dispatch_kernel,
+//            placed after the chunk's first slot
+// ---------------------------------------------------------------------------
+constexpr int kChunkThreads = 256;
+constexpr int kChunkWarps = kChunkThreads / 32;
+constexpr int kChunkedMinPairs = 4096;   // below: the one-CTA kernel
+
+__global__ void __launch_bounds__(kChunkThreads)
+dispatch_count_kernel(const int32_t* __restrict__ ids, int P, int E, int chunk,
+                      int32_t* __restrict__ cta_counts, int32_t* __restrict__ inv_perm,
+                      int* __restrict__ status) {
+  pdl_wait();   // the router's ids
+  pdl_trigger();
+  extern __shared__ int cnt[];   // [E]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int p0 = blockIdx.x * chunk, p1 = min(P, p0 + chunk);
+  for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+    const int e = ids[p];
+    if (e < 0 || e >= E) {
+      set_status(status, MOE_STATUS_BAD_EXPERT_ID);
+      inv_perm[p] = -1;
+    } else {
+      atomicAdd(&cnt[e], 1);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cta_counts[(size_t)blockIdx.x * E + e] = cnt[e];
+}
+
+__global__ void __launch_bounds__(kDispThreads)
+dispatch_scan_kernel(const int32_t* __restrict__ cta_counts, int C, int E,
+                     int32_t* __restrict__ offsets, int32_t* __restrict__ cta_base,
+                     int* __restrict__ status, int* __restrict__ n_active,
+                     int* __restrict__ active, int* __restrict__ goff, int* __restrict__ gexp,
+                     int* __restrict__ done, int max_groups) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int sh[33];
+  const int e = threadIdx.x;
+  int run = 0;
+  if (e < E) {
+    for (int c = 0; c < C; ++c) {
+      const int v = cta_counts[(size_t)c * E + e];
+      cta_base[(size_t)c * E + e] = run;
+      run += v;
+    }
+  }
+  int total;
+  const int off = block_excl_scan(e < E ? run : 0, sh, total);
+  if (e < E) {
+    offsets[e] = off;
+    for (int c = 0; c < C; ++c) cta_base[(size_t)c * E + e] += off;
+  }
+  if (e == 0) offsets[E] = total;
+  if (n_active) {
+    const int n = e < E ? run : 0;
+    const int ng = (n + 3) / 4;
+    int tot_g, tot_a;
+    const int g0 = block_excl_scan(ng, sh, tot_g);
+    const int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
+    const bool overflow = tot_g > max_groups;
+    if (e < E) {
+      goff[e] = g0;
+      done[e] = 0;
+      if (n > 0) active[a0] = e;
+      if (!overflow)
+        for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
+    }
+    if (e == 0) {
+      goff[E] = tot_g;
+      *n_active = overflow ? 0 : tot_a;
+      if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kChunkThreads)
+dispatch_scatter_kernel(const int32_t* __restrict__ ids, int P, int E, int chunk,
+                        const int32_t* __restrict__ cta_base, int32_t* __restrict__ perm_rows,
+                        int32_t* __restrict__ inv_perm) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int wcnt[];   // [warps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int c = blockIdx.x;
+  const int wchunk = chunk / kChunkWarps;   // chunk is a multiple of 32 * warps
+  const int p0 = min(P, c * chunk + warp * wchunk), p1 = min(P, p0 + wchunk);
+  for (int i = threadIdx.x; i < kChunkWarps * E; i += blockDim.x) wcnt[i] = 0;
+  __syncthreads();
+  for (int base = p0; base < p1; base += 32) {
+    const int p = base + lane;
+    int e = p < p1 ? ids[p] : -1;
+    if (e >= E) e = -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (peers & lt_mask) == 0) wcnt[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = cta_base[(size_t)c * E + e];
+    for (int w = 0; w < kChunkWarps; ++w) {
+      const int v = wcnt[w * E + e];
+      wcnt[w * E + e] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  for (int base = p0; base < p1; base += 32) {
+    const int p = base + lane;
+    int e = p < p1 ? ids[p] : -1;
+    if (e >= E) e = -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      const int pos = wcnt[warp * E + e] + __popc(peers & lt_mask);
+      perm_rows[pos] = p;
+      inv_perm[p] = pos;
+    }
+    __syncwarp();
+    if (e >= 0 && (peers & lt_mask) == 0) wcnt[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+static int chunk_count(int P) {
+  const int want = std::max(1, std::min(2 * sm_count(), (P + kChunkThreads - 1) / kChunkThreads));
+  return want;
+}
+
+static int chunk_size(int P, int C) {
+  const int per = (P + C - 1) / C;
+  return (per + kChunkThreads - 1) / kChunkThreads * kChunkThreads;   // 32 per warp multiple
+}
+
+// Scratch of the chunked dispatch: cta_counts and cta_base, C x E each.
+size_t dispatch_scratch_bytes(int P, int E) {
+  if (P < kChunkedMinPairs) return 0;
+  return 2 * align_up((size_t)chunk_count(P) * E * sizeof(int32_t), 256);
+}
+
+static int launch_dispatch_chunked(const int32_t* ids, int P, int E, int32_t* offsets,
+                                   int32_t* perm_rows, int32_t* inv_perm, int* status,
+                                   int* n_active, int* active, int* goff, int* gexp, int* done,
+                                   int max_groups, int32_t* scratch, cudaStream_t s) {
+  int C = chunk_count(P);
+  const int chunk = chunk_size(P, C);
+  C = (P + chunk - 1) / chunk;
+  int32_t* cta_counts = scratch;
+  int32_t* cta_base = scratch + align_up((size_t)chunk_count(P) * E * sizeof(int32_t), 256) / 4;
+  const size_t smem_w = sizeof(int) * (size_t)kChunkWarps * E;
+  if (smem_w > 48 * 1024)
+    MOE_CUDA(cudaFuncSetAttribute(dispatch_scatter_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_w));
+  ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
+  MOE_CUDA(launch_pdl(dispatch_count_kernel, dim3(C), dim3(kChunkThreads), sizeof(int) * E, s, ids,
+                      P, E, chunk, cta_counts, inv_perm, status));
+  MOE_CUDA(launch_pdl(dispatch_scan_kernel, dim3(1), dim3(kDispThreads), 0, s,
+                      (const int32_t*)cta_counts, C, E, offsets, cta_base, status, n_active, active,
+                      goff, gexp, done, max_groups));
+  MOE_CUDA(launch_pdl(dispatch_scatter_kernel, dim3(C), dim3(kChunkThreads), smem_w, s, ids, P, E,
+                      chunk, (const int32_t*)cta_base, perm_rows, inv_perm));
+  return MOE_OK;
+}
+
 // moe_dispatch that also writes the grouped-expert plan (see plan_kernel).
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
                             int* active, int* goff, int* gexp, int* done, int max_groups,
-                            cudaStream_t s) {
+                            int32_t* scratch, cudaStream_t s) {
   MOE_REQUIRE(E > 0 && E <= kDispThreads, MOE_ERR_UNSUPPORTED, "expert count %d above %d", E,
               kDispThreads);
   const int P = T * k;
   MOE_REQUIRE(P > 0, MOE_ERR_INVALID, "no pairs");
+  if (P >= kChunkedMinPairs && scratch) {
+    MOE_CHECK(launch_dispatch_chunked(ids, P, E, offsets, perm_rows, inv_perm, status, n_active,
+                                      active, goff, gexp, done, max_groups, scratch, s));
+    return check_launch("dispatch");
+  }
   size_t smem = sizeof(int) * ((size_t)kDispWarps * E + E);
   if (smem > 48 * 1024) {
     MOE_CUDA(cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -164,10 +341,8 @@ extern "C" {
 
 int moe_dispatch_workspace_bytes(int T, int k, int E, size_t* bytes) {
   MOE_REQUIRE(bytes, MOE_ERR_INVALID, "null output pointer");
-  (void)T;
-  (void)k;
-  (void)E;
-  *bytes = 256;  // the status word
+  MOE_REQUIRE(T >= 0 && k > 0 && E > 0, MOE_ERR_INVALID, "bad shape");
+  *bytes = 256 + moe::dispatch_scratch_bytes(T * k, E);  // status word + chunk scratch
   return MOE_OK;
 }
 
@@ -187,6 +362,17 @@ int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offset
     return MOE_OK;
   }
   MOE_REQUIRE(ids && perm_rows && inv_perm, MOE_ERR_INVALID, "null pointer");
+  const size_t scratch = dispatch_scratch_bytes((int)P, E);
+  MOE_REQUIRE(workspace_bytes >= 256 + scratch, MOE_ERR_WORKSPACE,
+              "dispatch workspace %zu < %zu", workspace_bytes, 256 + scratch);
+  if (scratch) {
+    MOE_CHECK(launch_dispatch_chunked(ids, (int)P, E, expert_offsets, perm_rows, inv_perm,
+                                      static_cast<int*>(workspace), nullptr, nullptr, nullptr,
+                                      nullptr, nullptr, 0,
+                                      reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + 256),
+                                      s));
+    return check_launch("dispatch");
+  }
   size_t smem = sizeof(int) * ((size_t)kDispWarps * E + E);
   if (smem > 48 * 1024) {
     MOE_CUDA(cudaFuncSetAttribute(dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

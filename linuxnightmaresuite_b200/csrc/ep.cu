@@ -339,7 +339,8 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
                             int* active, int* goff, int* gexp, int* done, int max_groups,
-                            cudaStream_t s);
+                            int32_t* scratch, cudaStream_t s);
+size_t dispatch_scratch_bytes(int P, int E);
 int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes);
 void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
                          int** goff, int** gexp, int** done, int* mg);
@@ -360,6 +361,7 @@ struct EpWs {
   int32_t* offsets;
   int32_t* perm;
   int32_t* inv;
+  int32_t* disp_scratch;
   int32_t* loff;
   int32_t* row_map;
   uint8_t* exp_ws;
@@ -381,6 +383,7 @@ static EpWs carve_ep(void* ws, const moe_layer_weights* w, int W, int T) {
   L.offsets = c.take<int32_t>(w->E + 1);
   L.perm = c.take<int32_t>(P);
   L.inv = c.take<int32_t>(P);
+  L.disp_scratch = c.take<int32_t>(dispatch_scratch_bytes((int)P, w->E) / 4 + 1);
   L.loff = c.take<int32_t>(El + 1);
   L.row_map = c.take<int32_t>(R);
   experts_workspace_hint(R, (int)P, El, w->d, w->F, &L.exp_bytes);
@@ -476,7 +479,8 @@ int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* pee
   MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
                           L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr));
   MOE_CHECK(launch_dispatch_planned(L.ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
-                                    nullptr, nullptr, nullptr, nullptr, nullptr, 0, s));
+                                    nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                                    L.disp_scratch, s));
   {
     ::moe::ProfScope _prof(MOE_K_AUX, s);
     ep_send_kernel<<<(P + 7) / 8, 256, 0, s>>>(x, L.perm, w->k, L.offsets, P, a);

@@ -880,7 +880,10 @@ int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_
                    cudaStream_t s);
 
 // Rows per active expert from which the tcgen05 GEMM path is used.
-constexpr int kTcMinMeanRows = 64;
+#ifndef MOE_TC_MIN_MEAN_ROWS
+#define MOE_TC_MIN_MEAN_ROWS 64
+#endif
+constexpr int kTcMinMeanRows = MOE_TC_MIN_MEAN_ROWS;
 
 static bool use_tc(int rows, int E, int d, int F) {
   const int active = rows < E ? rows : E;

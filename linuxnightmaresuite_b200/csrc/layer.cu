@@ -17,7 +17,8 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
                             int* active, int* goff, int* gexp, int* done, int max_groups,
-                            cudaStream_t s);
+                            int32_t* scratch, cudaStream_t s);
+size_t dispatch_scratch_bytes(int P, int E);
 int experts_workspace(int rows, int E, int d, int F, size_t* bytes);
 int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
                    const float* residual, int T, int k, int d, float* out, cudaStream_t s);
@@ -38,6 +39,7 @@ struct LayerWs {
   int32_t* offsets;
   int32_t* perm;
   int32_t* inv;
+  int32_t* disp_scratch;
   uint8_t* exp_ws;
   size_t exp_bytes;
   float* y;
@@ -59,6 +61,7 @@ static LayerWs carve_layer(void* ws, const moe_layer_weights* w, int T) {
   L.offsets = c.take<int32_t>(w->E + 1);
   L.perm = c.take<int32_t>(P);
   L.inv = c.take<int32_t>(P);
+  L.disp_scratch = c.take<int32_t>(dispatch_scratch_bytes((int)P, w->E) / 4 + 1);
   size_t eb = 0, sb = 0;
   experts_workspace((int)P, w->E, w->d, w->F, &eb);
   if (w->s_gate) experts_workspace(T, 1, w->d, w->Fs, &sb);
@@ -110,7 +113,7 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
   experts_plan_arrays(L.exp_ws, P, w->E, w->d, w->F, &n_active, &active, &goff, &gexp, &done,
                       &mg);
   MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
-                                    n_active, active, goff, gexp, done, mg, s));
+                                    n_active, active, goff, gexp, done, mg, L.disp_scratch, s));
   MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
                         w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
                         L.row_max, true, 0));

@@ -107,7 +107,8 @@ def dispatch(ids: torch.Tensor, n_experts: int, ws: Optional[torch.Tensor] = Non
     perm = torch.empty(T * k, dtype=torch.int32, device=dev)
     inv = torch.empty(T * k, dtype=torch.int32, device=dev)
     if ws is None:
-        ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+        ws = workspace(_size_out("moe_dispatch_workspace_bytes", T, k, n_experts), dev)
+        ws[:256].zero_()
     call("moe_dispatch", _ptr(ids), T, k, n_experts, _ptr(off), _ptr(perm), _ptr(inv),
          _ptr(ws), ws.numel(), _stream())
     return off, perm, inv

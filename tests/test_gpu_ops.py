@@ -96,7 +96,9 @@ def test_router_exact_ties_take_higher_index_first():
 
 
 @pytest.mark.parametrize("T,k,E,skew", [(1, 8, 128, 0), (64, 8, 128, 0), (4096, 8, 128, 1),
-                                        (777, 2, 8, 1), (3, 4, 1024, 0), (5000, 1, 16, 2)])
+                                        (777, 2, 8, 1), (3, 4, 1024, 0), (5000, 1, 16, 2),
+                                        # >= 4096 pairs: the chunked (multi-CTA) dispatch
+                                        (1024, 4, 1024, 0), (8192, 8, 128, 0), (4099, 1, 8, 1)])
 def test_dispatch_matches_stable_counting_sort(T, k, E, skew):
     rng = np.random.default_rng(T + E)
     if skew == 1:
@@ -112,6 +114,25 @@ def test_dispatch_matches_stable_counting_sort(T, k, E, skew):
     assert np.array_equal(off.cpu().numpy(), e_off)
     assert np.array_equal(perm.cpu().numpy(), e_perm)
     assert np.array_equal(inv.cpu().numpy(), e_inv)
+
+
+def test_chunked_dispatch_flags_bad_expert_ids():
+    rng = np.random.default_rng(11)
+    T, k, E = 2048, 4, 64
+    ids = rng.integers(0, E, size=(T, k)).astype(np.int32)
+    ids[5, 1], ids[1000, 3], ids[2047, 0] = E, -3, 99
+    nbytes = K._size_out("moe_dispatch_workspace_bytes", T, k, E)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    off, perm, inv = K.dispatch(cuda(ids), E, ws)
+    assert K.read_status(ws) & _lib.MOE_STATUS_BAD_EXPERT_ID
+    good = (ids >= 0) & (ids < E)
+    inv = inv.cpu().numpy()
+    assert (inv[~good.reshape(-1)] == -1).all()
+    # the valid pairs keep the stable order of the valid ids
+    flat = ids.reshape(-1)
+    order = np.argsort(np.where(good.reshape(-1), flat, E), kind="stable")[:good.sum()]
+    assert np.array_equal(perm.cpu().numpy()[:good.sum()], order)
+    assert off.cpu().numpy()[-1] == good.sum()
 
 
 def test_dispatch_flags_bad_expert_ids():
