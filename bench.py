@@ -47,13 +47,17 @@ METRIC = "MoE layer tokens/s"
 UNIT = "tokens/s"
 FLUSH_BYTES = 512 << 20
 
+# name -> (config, tokens, tokens split over the ranks?, layers)
+#   split False: each rank routes `tokens` of its own (weak scaling);
+#   split True:  the step's `tokens` are divided over the ranks (strong scaling)
 WORKLOADS = {
-    "decode_t64": ("decode_t64", 64),
-    "decode_t8": ("decode_t8", 8),
-    "decode_t1": ("decode_t1", 1),
-    "prefill": ("prefill", 4096),
-    "ep": ("ep", 8192),
-    "stacked_layer": ("stacked", 256),
+    "decode_t64": ("decode_t64", 64, False, 1),
+    "decode_t8": ("decode_t8", 8, False, 1),
+    "decode_t1": ("decode_t1", 1, False, 1),
+    "prefill": ("prefill", 4096, False, 1),
+    "ep": ("ep", 8192, True, 1),
+    "stacked_layer": ("stacked", 256, False, 1),
+    "stacked": ("stacked", 256, True, 30),
 }
 
 
@@ -125,12 +129,12 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    name, T = WORKLOADS[args.workload]
+    name, T, _, n_layers = WORKLOADS[args.workload]
     cfg = synth.CONFIGS[name]
     data = synth.make_layer(cfg, args.seed, tokens=T)
     sample = min(T, 16)
     times, dq = cpu_layer_timing(data, sample, args.steps, args.warmup)
-    ms = 1e3 * float(np.mean(times))
+    ms = 1e3 * float(np.mean(times)) * n_layers   # a stacked step: one layer's time per layer
     value = sample / (ms / 1e3)
     cores = cpu_threads()
     line = {
@@ -138,7 +142,8 @@ def run_reference(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": workload_desc(cfg, T), "sample_tokens_per_step": sample,
+        "config": {"workload": workload_desc(cfg, T) + (f" x {n_layers} layers" if n_layers > 1 else ""),
+                   "sample_tokens_per_step": sample,
                    "path": "oracle restatement of moe_forward.MoELayer.forward (numpy/OpenBLAS)",
                    "dequant_s_untimed": dq},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
@@ -254,9 +259,30 @@ def run_b200(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    name, T = WORKLOADS[args.workload]
+    name, T_step, split, n_layers = WORKLOADS[args.workload]
     cfg = synth.CONFIGS[name]
-    if world == 1:
+    if split and T_step % world:
+        raise SystemExit(f"{T_step} tokens do not split over {world} ranks")
+    T = T_step // world if split else T_step        # tokens per rank
+    stacked = n_layers > 1
+    model = None
+    if stacked:
+        # 30 layers, seed + layer index; every layer has a shared expert,
+        # RMSNorm and the residual in between
+        from linuxnightmaresuite_b200.stacked import StackedEP, StackedMoE
+        if world == 1:
+            E = cfg.n_experts
+            model = StackedMoE.from_layers(
+                (synth.make_layer_slice(cfg, args.seed + li, T, 0, E) for li in range(n_layers)),
+                device=dev)
+            layer = model.layers[0]
+        else:
+            model = StackedEP.build(cfg, args.seed, T, device=dev)
+            layer = model.layers[0]
+        x_np = np.ascontiguousarray(
+            synth.make_layer_slice(cfg, args.seed, T * world, 0, 0).x[rank * T:(rank + 1) * T])
+        data = None
+    elif world == 1:
         data = synth.make_layer(cfg, args.seed, tokens=T)
         layer = build_layer(data, dev)
         x_np = data.x
@@ -273,6 +299,8 @@ def run_b200(args):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def step(inp=x):
+        if model is not None:
+            return model.forward(inp, out=out)
         if world == 1:
             return layer.forward_batch(inp, out=out)
         return layer.forward(inp)
@@ -284,8 +312,14 @@ def run_b200(args):
     if world == 1 and layer.device_status() != 0:
         raise RuntimeError("device status error during warm-up")
 
-    # routing statistics of this batch (unique experts -> algorithmic bytes)
-    if world == 1:
+    # routing statistics of this batch (unique experts -> algorithmic bytes);
+    # for the stacked step, those of its first layer
+    if world == 1 and stacked:
+        ids, _ = layer.router.route_batch(x)
+        ids = ids.cpu().numpy()
+        uniq = int(np.unique(ids).size)
+        rows = int(ids.size)
+    elif world == 1:
         _, ids, _ = layer.forward_batch(x, out=out, return_routing=True)
         ids = ids.cpu().numpy()
         uniq = int(np.unique(ids).size)
@@ -329,7 +363,7 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = float(ms_t.item())
-    value = T * world / (ms / 1e3)
+    value = T * world / (ms / 1e3)    # tokens of the whole job per second
     launches = sum(c for _, c in prof.values())
 
     # end to end through the public API with host buffers
@@ -371,6 +405,9 @@ def run_b200(args):
     gu_launch_ms = gu_ms / gu_n if gu_n else None
     dn_launch_ms = dn_ms / dn_n if dn_n else None
     layer_bytes = uniq * 3 * mat + d * cfg.n_experts * 4 + T * d * 8  # this rank's share
+    if cfg.shared_ffn:
+        layer_bytes += 3 * cfg.shared_ffn * d // 32 * synth.block_bytes(cfg.shared_qtype)
+    layer_bytes *= n_layers
     tensor_bound = rows / max(1, uniq) >= 64      # the tcgen05 GEMM path
     if tensor_bound:
         # gate/up GEMM: 2 * rows * d * 2F algorithmic flops (the three split-operand
@@ -415,7 +452,7 @@ def run_b200(args):
                                 "achieved": dn_bytes / (dn_launch_ms / 1e3) / 1e9}
 
     cpu_base = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and data is not None:
         sample = min(T, 16)
         times, dq = cpu_layer_timing(data, sample, 3, 1)
         cms = float(np.median(times))
@@ -424,16 +461,18 @@ def run_b200(args):
                               f"pre-dequantised ({dq:.1f} s, untimed)"}
 
     if world > 1:
-        layer.close()
+        (model if model is not None else layer).close()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if split else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_desc(cfg, T), "tokens_per_rank": T,
+        "config": {"workload": workload_desc(cfg, T_step) + (f" x {n_layers} layers" if stacked else ""),
+                   "tokens_per_rank": T, "layers": n_layers,
                    "unique_experts": uniq, "routed_rows": rows,
                    "parallelism": f"ep{world}" if world > 1 else "single",
                    "experts_per_rank": cfg.n_experts // world,

@@ -265,7 +265,8 @@ int moe_ipc_open(const void* handle, void** ptr);      /* a peer's window */
 int moe_ipc_close(void* ptr);
 int moe_ep_window_bytes(int W, int E, int T, int k, int d, size_t* bytes);
 /* w: router over all E experts; expert weights of this rank's E / W experts
- * (experts rank * E/W .. (rank+1) * E/W - 1).  No shared expert. */
+ * (experts rank * E/W .. (rank+1) * E/W - 1); an optional shared expert runs
+ * on this rank's own tokens (replicated weights, no exchange). */
 int moe_ep_workspace_bytes(const moe_layer_weights* w, int W, int T, size_t* bytes);
 /* peers: device array of the W window pointers (own window at index rank,
  * peers' as mapped by moe_ipc_open); window: this rank's window; x, out (T, d)

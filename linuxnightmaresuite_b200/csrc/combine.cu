@@ -64,7 +64,7 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm
 __global__ void __launch_bounds__(256)
 rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ weight, float eps, int d,
                 float* __restrict__ out) {
-  extern __shared__ float sq[];
+  extern __shared__ float sq[];       // [d] squares, then the pairwise leaves
   __shared__ float s_den;
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * d;
@@ -73,8 +73,9 @@ rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ weight, f
     sq[i] = __fmul_rn(v, v);
   }
   __syncthreads();
+  const float sum = np_pairwise_sum_cta(sq, d, sq + d);
   if (threadIdx.x == 0) {
-    float ms = np_pairwise_sum(sq, d) / (float)d;
+    float ms = sum / (float)d;
     ms = ms + eps;
     s_den = sqrtf(ms);
   }
@@ -116,7 +117,8 @@ int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, f
   MOE_REQUIRE(T >= 0 && d > 0, MOE_ERR_INVALID, "bad shape");
   if (T == 0) return MOE_OK;
   MOE_REQUIRE(x && weight && out, MOE_ERR_INVALID, "null pointer");
-  size_t smem = (size_t)d * sizeof(float);
+  // squares + one float per pairwise leaf (every leaf holds more than 32 terms)
+  size_t smem = ((size_t)d + d / 32 + 2) * sizeof(float);
   MOE_REQUIRE(smem <= 200 * 1024, MOE_ERR_UNSUPPORTED, "d=%d too large", d);
   if (smem > 48 * 1024)
     MOE_CUDA(cudaFuncSetAttribute(moe::rms_norm_kernel,

@@ -352,6 +352,13 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
 int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
                    const float* residual, int T, int k, int d, float* out, cudaStream_t s);
 
+__global__ void ep_fill_two(int32_t* off, int n) {
+  if (threadIdx.x == 0) {
+    off[0] = 0;
+    off[1] = n;
+  }
+}
+
 struct EpWs {
   int* status;
   uint8_t* router_ws;
@@ -366,6 +373,10 @@ struct EpWs {
   int32_t* row_map;
   uint8_t* exp_ws;
   size_t exp_bytes;
+  int32_t* s_off;      // shared expert: [0, T]
+  float* s_y;          // shared expert output (T, d)
+  uint8_t* s_ws;       // shared expert workspace (its own plan and buffers)
+  size_t s_bytes;
   size_t bytes;
 };
 
@@ -388,6 +399,11 @@ static EpWs carve_ep(void* ws, const moe_layer_weights* w, int W, int T) {
   L.row_map = c.take<int32_t>(R);
   experts_workspace_hint(R, (int)P, El, w->d, w->F, &L.exp_bytes);
   L.exp_ws = c.take<uint8_t>(L.exp_bytes);
+  L.s_off = c.take<int32_t>(2);
+  L.s_y = w->s_gate ? c.take<float>((size_t)T * w->d) : nullptr;
+  L.s_bytes = 0;
+  if (w->s_gate) experts_workspace_hint(T, T, 1, w->d, w->Fs, &L.s_bytes);
+  L.s_ws = c.take<uint8_t>(L.s_bytes > 0 ? L.s_bytes : 256);
   L.bytes = align_up(c.used, 256);
   return L;
 }
@@ -457,7 +473,8 @@ int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* pee
   MOE_REQUIRE(W > 0 && W <= kEpMaxW && rank >= 0 && rank < W && w->E % W == 0,
               MOE_ERR_INVALID, "bad expert-parallel shape (W=%d rank=%d E=%d)", W, rank, w->E);
   MOE_REQUIRE(T > 0 && epoch > 0, MOE_ERR_INVALID, "T and epoch must be positive");
-  MOE_REQUIRE(!w->s_gate, MOE_ERR_UNSUPPORTED, "shared expert in the expert-parallel layer");
+  MOE_REQUIRE(!w->s_gate || (w->s_up && w->s_down && w->Fs > 0), MOE_ERR_INVALID,
+              "incomplete shared expert");
   const int El = w->E / W;
   MOE_REQUIRE(W * El <= 1024, MOE_ERR_UNSUPPORTED, "W * E_local must be <= 1024");
   MOE_REQUIRE(w->d % 4 == 0, MOE_ERR_UNSUPPORTED, "d must be a multiple of 4");
@@ -504,13 +521,25 @@ int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* pee
     ep_return_kernel<<<dim3((P + 7) / 8, W), 256, 0, s>>>(a);
   }
   MOE_CHECK(check_launch("ep_return"));
+  if (w->s_gate) {
+    // the shared expert runs on this rank's own tokens (replicated weights)
+    // while the other ranks finish their experts and returns
+    {
+      ::moe::ProfScope _prof(MOE_K_AUX, s);
+      ep_fill_two<<<1, 32, 0, s>>>(L.s_off, T);
+    }
+    MOE_CHECK(check_launch("ep_fill_two"));
+    MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
+                          nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.s_ws, L.s_bytes, s, L.status,
+                          nullptr, false, T));
+  }
   {
     ::moe::ProfScope _prof(MOE_K_AUX, s);
     ep_wait_kernel<<<1, 32, 0, s>>>(a, L.status);
   }
   MOE_CHECK(check_launch("ep_wait"));
   return launch_combine(reinterpret_cast<const float*>(a.win + a.off.ret_y), L.inv, L.wts,
-                        nullptr, residual, T, w->k, w->d, out, s);
+                        L.s_y, residual, T, w->k, w->d, out, s);
 }
 
 }  // extern "C"

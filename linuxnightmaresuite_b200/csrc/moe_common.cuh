@@ -233,6 +233,61 @@ static __device__ float np_pairwise_sum(const float* a, int n) {
   return np_pairwise_sum(a, n2) + np_pairwise_sum(a + n2, n - n2);
 }
 
+// The same sum computed by a CTA: the leaves of the pairwise tree (runs of at
+// most 128 terms) are summed by separate threads, then thread 0 adds them along
+// the tree.  Bit-identical to np_pairwise_sum.  Call from every thread; scratch
+// holds one float per leaf (np_pairwise_leaves(n)); the result is valid in
+// thread 0 after the call returns (the call ends with a barrier).
+static __device__ int np_pairwise_leaves(int n) {
+  if (n <= 128) return 1;
+  int n2 = n / 2;
+  n2 -= n2 % 8;
+  return np_pairwise_leaves(n2) + np_pairwise_leaves(n - n2);
+}
+
+static __device__ void np_pairwise_leaf(int n, int idx, int& start, int& len) {
+  start = 0;
+  len = n;
+  while (len > 128) {
+    int n2 = len / 2;
+    n2 -= n2 % 8;
+    const int left = np_pairwise_leaves(n2);
+    if (idx < left) {
+      len = n2;
+    } else {
+      idx -= left;
+      start += n2;
+      len -= n2;
+    }
+  }
+}
+
+static __device__ float np_pairwise_combine(const float* leaf, int n, int& next) {
+  if (n <= 128) return leaf[next++];
+  int n2 = n / 2;
+  n2 -= n2 % 8;
+  const float l = np_pairwise_combine(leaf, n2, next);
+  const float r = np_pairwise_combine(leaf, n - n2, next);
+  return l + r;
+}
+
+static __device__ float np_pairwise_sum_cta(const float* a, int n, float* scratch) {
+  const int L = np_pairwise_leaves(n);
+  for (int t = threadIdx.x; t < L; t += blockDim.x) {
+    int st, len;
+    np_pairwise_leaf(n, t, st, len);
+    scratch[t] = np_pairwise_sum(a + st, len);
+  }
+  __syncthreads();
+  float res = 0.f;
+  if (threadIdx.x == 0) {
+    int next = 0;
+    res = np_pairwise_combine(scratch, n, next);
+  }
+  __syncthreads();
+  return res;
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier + bulk-copy (TMA, 1-D) helpers
 // ---------------------------------------------------------------------------

@@ -100,12 +100,90 @@ def ep_exchange(send: torch.Tensor, counts: torch.Tensor, expert_fn, group=None)
     return all_to_all_rows(y_recv, recv_rows, send_rows, group)
 
 
+class EPExchange:
+    """The exchange window of this rank (and the mapped windows of the other
+    ranks), a step workspace and the step counter.  Layers of the same shape
+    can share one: each step's exchange completes before the next starts."""
+
+    def __init__(self, group, device):
+        from . import kernels as K
+        from . import _lib
+        self.K, self._lib = K, _lib
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device
+        self.key = None
+        self.window = None
+        self._mapped = []
+        self.epoch = 0
+
+    def ensure(self, lw, T: int) -> None:
+        """(Re)build the windows for steps of T tokens (collective)."""
+        key = (lw.E, lw.k, lw.d, lw.F, lw.Fs, T)
+        if self.key == key:
+            return
+        _lib, K = self._lib, self.K
+        self.close()
+        W, rank = self.world, self.rank
+        nbytes = ctypes.c_size_t(0)
+        _lib.call("moe_ep_window_bytes", W, lw.E, T, lw.k, lw.d, ctypes.byref(nbytes))
+        win = ctypes.c_void_p(0)
+        _lib.call("moe_ipc_alloc", nbytes.value, ctypes.byref(win))
+        self.window = win.value
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.call("moe_ipc_handle", ctypes.c_void_p(self.window), ctypes.cast(handle, ctypes.c_void_p))
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        allh = [torch.empty_like(mine) for _ in range(W)]
+        dist.all_gather(allh, mine, group=self.group)
+        ptrs = []
+        for s_ in range(W):
+            if s_ == rank:
+                ptrs.append(self.window)
+                continue
+            h = (ctypes.c_uint8 * 64)(*allh[s_].cpu().tolist())
+            p = ctypes.c_void_p(0)
+            _lib.call("moe_ipc_open", ctypes.cast(h, ctypes.c_void_p), ctypes.byref(p))
+            self._mapped.append(p.value)
+            ptrs.append(p.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        wsb = ctypes.c_size_t(0)
+        _lib.call("moe_ep_workspace_bytes", ctypes.byref(lw.c), W, T, ctypes.byref(wsb))
+        self.ws = K.workspace(wsb.value, self.device)
+        self.ws[:256].zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self.key = key
+        self.epoch = 0
+
+    def close(self) -> None:
+        """Unmap the peers' windows and free this rank's (collective)."""
+        if self.window is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._mapped:
+            self._lib.call("moe_ipc_close", ctypes.c_void_p(p))
+        self._mapped = []
+        dist.barrier(group=self.group)
+        self._lib.call("moe_ipc_free", ctypes.c_void_p(self.window))
+        self.window = None
+        self.key = None
+
+
 class EPMoELayer:
     """One MoE layer sharded over the ranks of ``group`` by expert; this rank
-    holds experts ``expert_range(rank, W, E)`` and routes its own tokens."""
+    holds experts ``expert_range(rank, W, E)`` and routes its own tokens.
+
+    w_gate / w_up / w_down: raw block stacks of all E experts, or of this
+    rank's experts only with ``local=True``.  ``shared``: an always-on shared
+    expert (three raw block arrays), run on this rank's own tokens.
+    ``exchange``: an ``EPExchange`` to share with other layers."""
 
     def __init__(self, gate_weight, w_gate, w_up, w_down, qtype: int, top_k: int,
-                 mode: int = 0, bias=None, group=None, device=None):
+                 mode: int = 0, bias=None, group=None, device=None, shared=None,
+                 shared_qtype: int = 8, local: bool = False,
+                 exchange: Optional[EPExchange] = None):
         from . import kernels as K
         from . import _lib
         from .moe_forward import _to_dev_u8, _device
@@ -122,91 +200,52 @@ class EPMoELayer:
         self.gate_w = torch.as_tensor(np.ascontiguousarray(gate_weight, dtype=np.float32)).to(dev)
         self.bias = None if bias is None else torch.as_tensor(
             np.ascontiguousarray(bias, dtype=np.float32)).to(dev)
-        sl = slice(self.e0, self.e1)
         El = self.e1 - self.e0
+        sl = slice(0, El) if local else slice(self.e0, self.e1)
+        if local and int(w_gate.shape[0]) != El:
+            raise ValueError(f"local weights hold {w_gate.shape[0]} experts, rank owns {El}")
         self.w_gate = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_gate[sl]), dev),
                                      qtype, El, self.F, d)
         self.w_up = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_up[sl]), dev),
                                    qtype, El, self.F, d)
         self.w_down = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_down[sl]), dev),
                                      qtype, El, d, self.F)
+        sh, Fs = None, 0
+        if shared is not None:
+            sg, su, sd = shared
+            Fs = int(np.asarray(sg).shape[-2])
+            sh = (K.pack_weights(_to_dev_u8(np.ascontiguousarray(sg), dev), shared_qtype, 1, Fs, d),
+                  K.pack_weights(_to_dev_u8(np.ascontiguousarray(su), dev), shared_qtype, 1, Fs, d),
+                  K.pack_weights(_to_dev_u8(np.ascontiguousarray(sd), dev), shared_qtype, 1, d, Fs))
         self.lw = K.LayerWeights(self.gate_w, self.w_gate, self.w_up, self.w_down, qtype, E,
-                                 top_k, d, self.F, mode, self.bias)
-        self._T = None
-        self._window = None
-        self._mapped = []
-        self.epoch = 0
-
-    # ------------------------------------------------------------------ set-up
-    def _setup(self, T: int) -> None:
-        _lib, K = self._lib, self.K
-        self.close()
-        W, rank = self.world, self.rank
-        nbytes = ctypes.c_size_t(0)
-        _lib.call("moe_ep_window_bytes", W, self.E, T, self.k, self.d, ctypes.byref(nbytes))
-        win = ctypes.c_void_p(0)
-        _lib.call("moe_ipc_alloc", nbytes.value, ctypes.byref(win))
-        self._window = win.value
-        handle = (ctypes.c_uint8 * 64)()
-        _lib.call("moe_ipc_handle", ctypes.c_void_p(self._window), ctypes.cast(handle, ctypes.c_void_p))
-        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
-        allh = [torch.empty_like(mine) for _ in range(W)]
-        dist.all_gather(allh, mine, group=self.group)
-        ptrs = []
-        for s_ in range(W):
-            if s_ == rank:
-                ptrs.append(self._window)
-                continue
-            h = (ctypes.c_uint8 * 64)(*allh[s_].cpu().tolist())
-            p = ctypes.c_void_p(0)
-            _lib.call("moe_ipc_open", ctypes.cast(h, ctypes.c_void_p), ctypes.byref(p))
-            self._mapped.append(p.value)
-            ptrs.append(p.value)
-        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
-        wsb = ctypes.c_size_t(0)
-        _lib.call("moe_ep_workspace_bytes", ctypes.byref(self.lw.c), W, T, ctypes.byref(wsb))
-        self.ws = K.workspace(wsb.value, self.device)
-        self.ws[:256].zero_()
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        self._T = T
-        self.epoch = 0
+                                 top_k, d, self.F, mode, self.bias, shared=sh,
+                                 shared_qtype=shared_qtype, Fs=Fs)
+        self.exchange = exchange if exchange is not None else EPExchange(group, dev)
 
     def close(self) -> None:
-        """Unmap the peers' windows and free this rank's (collective)."""
-        if self._window is None:
-            return
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        for p in self._mapped:
-            self._lib.call("moe_ipc_close", ctypes.c_void_p(p))
-        self._mapped = []
-        dist.barrier(group=self.group)
-        self._lib.call("moe_ipc_free", ctypes.c_void_p(self._window))
-        self._window = None
-        self._T = None
+        self.exchange.close()
 
     # ------------------------------------------------------------------ step
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                 residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One expert-parallel step for this rank's tokens x (T, d); every rank
         calls it with the same T.  Device work only."""
-        K = self.K
+        K, ex = self.K, self.exchange
         K._need(x, torch.float32, "x")
         T = int(x.shape[0])
-        if self._T != T:
-            self._setup(T)
+        ex.ensure(self.lw, T)
         if out is None:
             out = torch.empty_like(x)
-        self.epoch += 1
+        ex.epoch += 1
         self._lib.call("moe_ep_forward", ctypes.byref(self.lw.c), self.world, self.rank,
-                       ctypes.c_void_p(self.peers.data_ptr()), ctypes.c_void_p(self._window),
-                       K._ptr(x), T, K._ptr(out), K._ptr(residual), self.epoch, K._ptr(self.ws),
-                       self.ws.numel(), K._stream())
+                       ctypes.c_void_p(ex.peers.data_ptr()), ctypes.c_void_p(ex.window),
+                       K._ptr(x), T, K._ptr(out), K._ptr(residual), ex.epoch, K._ptr(ex.ws),
+                       ex.ws.numel(), K._stream())
         return out
 
     def device_status(self) -> int:
-        return self.K.read_status(self.ws) if self._window is not None else 0
+        ex = self.exchange
+        return self.K.read_status(ex.ws) if ex.window is not None else 0
 
     def routing_stats(self, x: torch.Tensor) -> Tuple[int, int]:
         """(active local experts, rows this rank's experts receive) for a step

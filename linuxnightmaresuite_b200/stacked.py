@@ -48,3 +48,53 @@ class StackedMoE:
             layer.forward_batch(xn, residual=cur, out=dst)
             cur = dst
         return cur
+
+
+class StackedEP:
+    """The stacked step with every layer expert-parallel over ``group``: the
+    layers share one exchange window; RMSNorm and the residual are local."""
+
+    def __init__(self, layers, norms, eps: float = 1e-6):
+        self.layers = list(layers)
+        self.norms = list(norms)
+        self.eps = eps
+        self._buf: Optional[torch.Tensor] = None
+
+    @classmethod
+    def build(cls, cfg, seed: int, tokens: int, group=None, device=None, eps: float = 1e-6,
+              layers: Optional[int] = None) -> "StackedEP":
+        """Synthetic layers (seed + layer index); each rank generates and packs
+        only its own experts."""
+        import torch.distributed as dist
+        from . import synth
+        from .ep import EPExchange, EPMoELayer, expert_range
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        e0, e1 = expert_range(rank, world, cfg.n_experts)
+        ex = EPExchange(group, device)
+        ls, ns = [], []
+        for li in range(cfg.n_layers if layers is None else layers):
+            data = synth.make_layer_slice(cfg, seed + li, tokens * world, e0, e1)
+            shared = (data.s_gate, data.s_up, data.s_down) if cfg.shared_ffn else None
+            layer = EPMoELayer(data.gate_w, data.w_gate, data.w_up, data.w_down, cfg.qtype,
+                               cfg.top_k, cfg.route_mode, None, group=group, device=device,
+                               shared=shared, shared_qtype=cfg.shared_qtype, local=True,
+                               exchange=ex)
+            ls.append(layer)
+            ns.append(torch.from_numpy(data.norm_w).to(layer.device))
+        return cls(ls, ns, eps)
+
+    def close(self) -> None:
+        if self.layers:
+            self.layers[0].exchange.close()
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        cur = x
+        if self._buf is None or self._buf.shape != x.shape:
+            self._buf = torch.empty_like(x)
+        xn = self._buf
+        for i, (layer, nw) in enumerate(zip(self.layers, self.norms)):
+            K.rms_norm(cur, nw, self.eps, out=xn)
+            dst = out if (out is not None and i == len(self.layers) - 1) else torch.empty_like(x)
+            layer.forward(xn, out=dst, residual=cur)
+            cur = dst
+        return cur

@@ -184,6 +184,36 @@ def make_layer(cfg: MoEConfig, seed: int = 0, tokens: Optional[int] = None,
     return data
 
 
+def make_layer_slice(cfg: MoEConfig, seed: int, tokens: int, e0: int, e1: int) -> MoELayerData:
+    """One layer whose experts are drawn from per-expert generators (seed, e),
+    so a rank can build just its experts [e0, e1) and every rank agrees on
+    them; the router, tokens, shared expert and norm come from (seed, E) and
+    are the same on every rank.  w_* hold experts e0..e1-1 only."""
+    d, E, F = cfg.d_model, cfg.n_experts, cfg.ffn
+    rng = np.random.default_rng([seed, E])
+    gate_w = (rng.standard_normal((d, E), dtype=np.float32) * np.float32(cfg.router_std))
+    x = rng.standard_normal((tokens, d), dtype=np.float32)
+    mats = []
+    for e in range(e0, e1):
+        re = np.random.default_rng([seed, e, 7])
+        mats.append((quant_matrix(re, cfg.qtype, 1, F, d, cfg.qscale),
+                     quant_matrix(re, cfg.qtype, 1, F, d, cfg.qscale),
+                     quant_matrix(re, cfg.qtype, 1, d, F, cfg.qscale)))
+    def stack(j, rows, cols):
+        if not mats:
+            return np.zeros((0, rows, row_bytes(cfg.qtype, cols)), np.uint8)
+        return np.concatenate([m[j] for m in mats])
+
+    data = MoELayerData(cfg, x, gate_w, None, stack(0, F, d), stack(1, F, d), stack(2, d, F))
+    if cfg.shared_ffn:
+        Fs = cfg.shared_ffn
+        data.s_gate = quant_matrix(rng, cfg.shared_qtype, 1, Fs, d, cfg.shared_qscale)
+        data.s_up = quant_matrix(rng, cfg.shared_qtype, 1, Fs, d, cfg.shared_qscale)
+        data.s_down = quant_matrix(rng, cfg.shared_qtype, 1, d, Fs, cfg.shared_qscale)
+    data.norm_w = (1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+    return data
+
+
 def tune_zipf_scale(x: np.ndarray, gate_w: np.ndarray, unit_bias: np.ndarray, k: int,
                     target_max: int) -> float:
     """Bisection on the bias scale so the busiest expert receives about
