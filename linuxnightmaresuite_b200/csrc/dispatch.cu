@@ -23,8 +23,8 @@ __global__ void __launch_bounds__(kDispThreads)
 dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restrict__ offsets,
                 int32_t* __restrict__ perm_rows, int32_t* __restrict__ inv_perm,
                 int* __restrict__ status, int* __restrict__ n_active, int* __restrict__ active,
-                int* __restrict__ goff, int* __restrict__ gexp, int* __restrict__ done,
-                int max_groups) {
+                int* __restrict__ goff, int* __restrict__ coff, int* __restrict__ done,
+                int max_groups, int rpc) {
   pdl_wait();   // the router's ids
   pdl_trigger();
   extern __shared__ int sm[];
@@ -70,27 +70,10 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
   }
   __syncthreads();
   if (n_active) {
-    // plan of the grouped expert kernels: active experts (ascending), offsets
-    // of 4-row groups, group -> expert map (E <= blockDim.x)
+    // plan of the grouped expert kernels (E <= blockDim.x)
     const int e = threadIdx.x;
-    const int n = e < E ? etot[e] : 0;
-    const int ng = (n + 3) / 4;
-    int tot_g, tot_a;
-    const int g0 = block_excl_scan(ng, sh, tot_g);
-    const int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
-    const bool overflow = tot_g > max_groups;
-    if (e < E) {
-      goff[e] = g0;
-      done[e] = 0;
-      if (n > 0) active[a0] = e;
-      if (!overflow)
-        for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
-    }
-    if (e == 0) {
-      goff[E] = tot_g;
-      *n_active = overflow ? 0 : tot_a;
-      if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
-    }
+    write_expert_plan(e < E ? etot[e] : 0, e, E, rpc, max_groups, sh, n_active, active, goff, coff,
+                      done, status);
     __syncthreads();
   }
   // exclusive scan of etot over experts (single warp; E is small)
@@ -176,8 +159,8 @@ __global__ void __launch_bounds__(kDispThreads)
 dispatch_scan_kernel(const int32_t* __restrict__ cta_counts, int C, int E,
                      int32_t* __restrict__ offsets, int32_t* __restrict__ cta_base,
                      int* __restrict__ status, int* __restrict__ n_active,
-                     int* __restrict__ active, int* __restrict__ goff, int* __restrict__ gexp,
-                     int* __restrict__ done, int max_groups) {
+                     int* __restrict__ active, int* __restrict__ goff, int* __restrict__ coff,
+                     int* __restrict__ done, int max_groups, int rpc) {
   pdl_wait();
   pdl_trigger();
   __shared__ int sh[33];
@@ -197,26 +180,9 @@ dispatch_scan_kernel(const int32_t* __restrict__ cta_counts, int C, int E,
     for (int c = 0; c < C; ++c) cta_base[(size_t)c * E + e] += off;
   }
   if (e == 0) offsets[E] = total;
-  if (n_active) {
-    const int n = e < E ? run : 0;
-    const int ng = (n + 3) / 4;
-    int tot_g, tot_a;
-    const int g0 = block_excl_scan(ng, sh, tot_g);
-    const int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
-    const bool overflow = tot_g > max_groups;
-    if (e < E) {
-      goff[e] = g0;
-      done[e] = 0;
-      if (n > 0) active[a0] = e;
-      if (!overflow)
-        for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
-    }
-    if (e == 0) {
-      goff[E] = tot_g;
-      *n_active = overflow ? 0 : tot_a;
-      if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
-    }
-  }
+  if (n_active)
+    write_expert_plan(e < E ? run : 0, e, E, rpc, max_groups, sh, n_active, active, goff, coff,
+                      done, status);
 }
 
 __global__ void __launch_bounds__(kChunkThreads)
@@ -285,8 +251,8 @@ size_t dispatch_scratch_bytes(int P, int E) {
 
 static int launch_dispatch_chunked(const int32_t* ids, int P, int E, int32_t* offsets,
                                    int32_t* perm_rows, int32_t* inv_perm, int* status,
-                                   int* n_active, int* active, int* goff, int* gexp, int* done,
-                                   int max_groups, int32_t* scratch, cudaStream_t s) {
+                                   int* n_active, int* active, int* goff, int* coff, int* done,
+                                   int max_groups, int rpc, int32_t* scratch, cudaStream_t s) {
   int C = chunk_count(P);
   const int chunk = chunk_size(P, C);
   C = (P + chunk - 1) / chunk;
@@ -301,7 +267,7 @@ static int launch_dispatch_chunked(const int32_t* ids, int P, int E, int32_t* of
                       P, E, chunk, cta_counts, inv_perm, status));
   MOE_CUDA(launch_pdl(dispatch_scan_kernel, dim3(1), dim3(kDispThreads), 0, s,
                       (const int32_t*)cta_counts, C, E, offsets, cta_base, status, n_active, active,
-                      goff, gexp, done, max_groups));
+                      goff, coff, done, max_groups, rpc));
   MOE_CUDA(launch_pdl(dispatch_scatter_kernel, dim3(C), dim3(kChunkThreads), smem_w, s, ids, P, E,
                       chunk, (const int32_t*)cta_base, perm_rows, inv_perm));
   return MOE_OK;
@@ -310,15 +276,15 @@ static int launch_dispatch_chunked(const int32_t* ids, int P, int E, int32_t* of
 // moe_dispatch that also writes the grouped-expert plan (see plan_kernel).
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
-                            int* active, int* goff, int* gexp, int* done, int max_groups,
-                            int32_t* scratch, cudaStream_t s) {
+                            int* active, int* goff, int* coff, int* done, int max_groups,
+                            int rpc, int32_t* scratch, cudaStream_t s) {
   MOE_REQUIRE(E > 0 && E <= kDispThreads, MOE_ERR_UNSUPPORTED, "expert count %d above %d", E,
               kDispThreads);
   const int P = T * k;
   MOE_REQUIRE(P > 0, MOE_ERR_INVALID, "no pairs");
   if (P >= kChunkedMinPairs && scratch) {
     MOE_CHECK(launch_dispatch_chunked(ids, P, E, offsets, perm_rows, inv_perm, status, n_active,
-                                      active, goff, gexp, done, max_groups, scratch, s));
+                                      active, goff, coff, done, max_groups, rpc, scratch, s));
     return check_launch("dispatch");
   }
   size_t smem = sizeof(int) * ((size_t)kDispWarps * E + E);
@@ -329,8 +295,8 @@ int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* of
   {
     ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
     MOE_CUDA(launch_pdl(dispatch_kernel, dim3(1), dim3(kDispThreads), smem, s, ids, P, E, offsets,
-                        perm_rows, inv_perm, status, n_active, active, goff, gexp, done,
-                        max_groups));
+                        perm_rows, inv_perm, status, n_active, active, goff, coff, done,
+                        max_groups, rpc));
   }
   return check_launch("dispatch");
 }
@@ -368,7 +334,7 @@ int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offset
   if (scratch) {
     MOE_CHECK(launch_dispatch_chunked(ids, (int)P, E, expert_offsets, perm_rows, inv_perm,
                                       static_cast<int*>(workspace), nullptr, nullptr, nullptr,
-                                      nullptr, nullptr, 0,
+                                      nullptr, nullptr, 0, 1,
                                       reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + 256),
                                       s));
     return check_launch("dispatch");
@@ -383,7 +349,7 @@ int moe_dispatch(const int32_t* ids, int T, int k, int E, int32_t* expert_offset
     MOE_CUDA(launch_pdl(dispatch_kernel, dim3(1), dim3(kDispThreads), smem, s, ids, (int)P, E,
                         expert_offsets, perm_rows, inv_perm, static_cast<int*>(workspace),
                         (int*)nullptr, (int*)nullptr, (int*)nullptr, (int*)nullptr,
-                        (int*)nullptr, 0));
+                        (int*)nullptr, 0, 1));
   }
   return check_launch("dispatch");
 }

@@ -215,7 +215,7 @@ ep_send_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm, in
 __global__ void __launch_bounds__(1024)
 ep_recv_plan_kernel(EpArgs a, int32_t* __restrict__ loff, int32_t* __restrict__ row_map,
                     int* __restrict__ n_active, int* __restrict__ active, int* __restrict__ goff,
-                    int* __restrict__ gexp, int* __restrict__ done, int max_groups,
+                    int* __restrict__ coff, int* __restrict__ done, int max_groups, int rpc,
                     int* __restrict__ status) {
   __shared__ int sh[33];
   __shared__ int rc[1024];             // clamped counts [src][e]
@@ -276,28 +276,11 @@ ep_recv_plan_kernel(EpArgs a, int32_t* __restrict__ loff, int32_t* __restrict__ 
     }
   }
   // plan of the grouped experts (as the dispatch kernel writes it)
-  const int el = i;
   int ne = 0;
-  if (el < a.El && !over) {
-    for (int s2 = 0; s2 < a.W; ++s2) ne += rc[s2 * a.El + el];
+  if (i < a.El && !over) {
+    for (int s2 = 0; s2 < a.W; ++s2) ne += rc[s2 * a.El + i];
   }
-  const int ng = (ne + 3) / 4;
-  int tot_g, tot_a;
-  const int g0 = block_excl_scan(ng, sh, tot_g);
-  const int a0 = block_excl_scan(ne > 0 ? 1 : 0, sh, tot_a);
-  const bool overflow = tot_g > max_groups;
-  if (el < a.El) {
-    goff[el] = g0;
-    done[el] = 0;
-    if (ne > 0) active[a0] = el;
-    if (!overflow)
-      for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = el;
-  }
-  if (el == 0) {
-    goff[a.El] = tot_g;
-    *n_active = overflow ? 0 : tot_a;
-    if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
-  }
+  write_expert_plan(ne, i, a.El, rpc, max_groups, sh, n_active, active, goff, coff, done, status);
 }
 
 // Expert outputs of the rows received from source s (in place in recv_x) ->
@@ -338,12 +321,13 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
                   size_t workspace_bytes, cudaStream_t stream, float* row_max);
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
-                            int* active, int* goff, int* gexp, int* done, int max_groups,
-                            int32_t* scratch, cudaStream_t s);
+                            int* active, int* goff, int* coff, int* done, int max_groups,
+                            int rpc, int32_t* scratch, cudaStream_t s);
+int experts_rows_per_chunk(int qtype, int rows, int E, int d, int F);
 size_t dispatch_scratch_bytes(int P, int E);
 int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes);
 void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
-                         int** goff, int** gexp, int** done, int* mg);
+                         int** goff, int** coff, int** done, int* mg);
 int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
                 const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
@@ -496,7 +480,7 @@ int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* pee
   MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
                           L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr));
   MOE_CHECK(launch_dispatch_planned(L.ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
-                                    nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                                    nullptr, nullptr, nullptr, nullptr, nullptr, 0, 1,
                                     L.disp_scratch, s));
   {
     ::moe::ProfScope _prof(MOE_K_AUX, s);
@@ -504,12 +488,13 @@ int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* pee
   }
   MOE_CHECK(check_launch("ep_send"));
   const int R = P * W;
-  int *n_active, *active, *goff, *gexp, *done, mg;
-  experts_plan_arrays(L.exp_ws, R, El, w->d, w->F, &n_active, &active, &goff, &gexp, &done, &mg);
+  int *n_active, *active, *goff, *coff, *done, mg;
+  experts_plan_arrays(L.exp_ws, R, El, w->d, w->F, &n_active, &active, &goff, &coff, &done, &mg);
+  const int rpc = experts_rows_per_chunk(w->qtype, R, El, w->d, w->F);
   {
     ::moe::ProfScope _prof(MOE_K_AUX, s);
-    ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, gexp,
-                                           done, mg, L.status);
+    ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, coff,
+                                           done, mg, rpc, L.status);
   }
   MOE_CHECK(check_launch("ep_recv_plan"));
   float* recv = reinterpret_cast<float*>(a.win + a.off.recv_x);

@@ -78,9 +78,9 @@ __device__ __forceinline__ void frag_pos(int e, int& t, int& i) {
 // plan: active experts, group offsets, group -> expert map
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kPlanThreads)
-plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups,
+plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups, int rpc,
             int* __restrict__ n_active, int* __restrict__ active, int* __restrict__ goff,
-            int* __restrict__ gexp, int* __restrict__ done, int* __restrict__ status) {
+            int* __restrict__ coff, int* __restrict__ done, int* __restrict__ status) {
   __shared__ int sh[33];
   const int e = threadIdx.x;
   int n = 0;
@@ -91,23 +91,7 @@ plan_kernel(const int32_t* __restrict__ offsets, int E, int rows, int max_groups
       n = 0;
     }
   }
-  int ng = (n + 3) / 4;
-  int tot_g, tot_a;
-  int g0 = block_excl_scan(ng, sh, tot_g);
-  int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
-  bool overflow = tot_g > max_groups;
-  if (overflow && e == 0) set_status(status, MOE_STATUS_ROW_OVERFLOW);
-  if (e < E) {
-    goff[e] = g0;
-    done[e] = 0;
-    if (n > 0) active[a0] = e;
-    if (!overflow)
-      for (int gi = 0; gi < ng; ++gi) gexp[g0 + gi] = e;
-  }
-  if (e == 0) {
-    goff[E] = tot_g;
-    *n_active = overflow ? 0 : tot_a;
-  }
+  write_expert_plan(n, e, E, rpc, max_groups, sh, n_active, active, goff, coff, done, status);
 }
 
 // ---------------------------------------------------------------------------
@@ -253,6 +237,17 @@ __device__ __forceinline__ bool wait_count(const int* p, int target) {
     __nanosleep(128);
   }
   return false;
+}
+
+// Work item `item` (a chunk of rpc rows of one expert) -> expert e and the
+// chunk's first row c0 inside the expert; false past the last item.
+__device__ __forceinline__ bool chunk_of(int item, const int* __restrict__ citem, int rpc,
+                                         int& e, int& c0) {
+  const int v = citem[item];
+  if (v < 0) return false;
+  e = v >> 16;
+  c0 = (v & 0xFFFF) * rpc;
+  return true;
 }
 
 // Per-CTA state of a gate/up work item.
@@ -572,9 +567,10 @@ __global__ void __launch_bounds__(kGuWarps * 32, 1)
 gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t mat_bytes,
               int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
               const int* __restrict__ active, const int* __restrict__ goff,
-              const float* __restrict__ x, const int32_t* __restrict__ x_rows, int x_div,
-              const float* __restrict__ x_row_max, uint8_t* __restrict__ hfrag, int ks, int cgp,
-              int nst, int* __restrict__ done, int* __restrict__ status) {
+              const int* __restrict__ citem, const float* __restrict__ x,
+              const int32_t* __restrict__ x_rows, int x_div, const float* __restrict__ x_row_max,
+              uint8_t* __restrict__ hfrag, int ks, int cgp, int nst, int* __restrict__ done,
+              int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SMAX = Ring<QT>::kGuStages;
@@ -598,9 +594,9 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   const int spc = kGuWarps / ks;
   const int strips = F / 16;
   const int cpe = (strips + spc - 1) / spc;
-  const int a = blockIdx.x / cpe;
-  if (a >= *n_active) return;
-  const int e = active[a];
+  const int item = blockIdx.x / cpe;      // one chunk of 4 * cgp rows of one expert
+  int e, c0;
+  if (!chunk_of(item, citem, 4 * cgp, e, c0)) return;
   c.ks = ks;
   c.kp = warp % ks;
   c.s = (blockIdx.x % cpe) * spc + warp / ks;
@@ -626,22 +622,18 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   }
   __syncwarp();
   uint32_t parity = 0u;
-  bool ok = true;
-  for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
-    const int ncg = min(cgp, (c.n - c0 + 3) / 4);
-    if (ok) gu_prefetch<QT>(c);
-    build_x_stage<QT>(smem, rs_s, rmax_s, x, x_rows, x_div, x_row_max, c.row0, c0, c.n, ncg, d);
-    __syncthreads();
-    if (ncg == 1) ok = gu_chunk<QT, 1>(c, parity, c0, ok);
-    else ok = gu_chunk<QT, 2>(c, parity, c0, ok);
-    __syncthreads();  // x stage and rings are rewritten by the next chunk
-  }
-  // this CTA's hidden fragments are complete: count it for the expert (the
-  // down kernel's CTAs of expert e start once all of e's CTAs have counted)
+  const int ncg = min(cgp, (c.n - c0 + 3) / 4);
+  gu_prefetch<QT>(c);
+  build_x_stage<QT>(smem, rs_s, rmax_s, x, x_rows, x_div, x_row_max, c.row0, c0, c.n, ncg, d);
+  __syncthreads();
+  if (ncg == 1) gu_chunk<QT, 1>(c, parity, c0, true);
+  else gu_chunk<QT, 2>(c, parity, c0, true);
+  // this CTA's hidden fragments of the chunk are complete: count it (the down
+  // kernel's CTAs of the chunk start once all of its gate/up CTAs have)
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0)
-    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + e) : "memory");
+    asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(done + item) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -773,7 +765,7 @@ __global__ void __launch_bounds__(kDnWarps * 32, 2)
 down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
             const int* __restrict__ active, const int* __restrict__ goff,
-            const uint8_t* __restrict__ hfrag, float* __restrict__ y,
+            const int* __restrict__ citem, const uint8_t* __restrict__ hfrag, float* __restrict__ y,
             const int32_t* __restrict__ y_rows, int cgp, int nst, const int* __restrict__ done,
             int gu_cpe, int* __restrict__ status) {
   using Tr = QTraits<QT>;
@@ -790,11 +782,11 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   c.ring = smem + xbytes + kBarArea + warp * nst * dn_stage_bytes<QT>();
   const int strips = d / 16;
   const int cpe = (strips + kDnWarps - 1) / kDnWarps;
-  const int a = blockIdx.x / cpe;
-  if (a >= *n_active) return;
+  const int item = blockIdx.x / cpe;      // the same chunk as the gate/up CTAs that wrote it
+  int e, c0;
+  if (!chunk_of(item, citem, 4 * cgp, e, c0)) return;
   c.s = (blockIdx.x % cpe) * kDnWarps + warp;
   c.strip_ok = c.s < strips;
-  const int e = active[a];
   c.JT = F / 64;
   c.row0 = offsets[e];
   c.n = offsets[e + 1] - c.row0;
@@ -816,28 +808,23 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   uint32_t parity = 0u;
   dn_prefetch<QT>(c);
   // Launched as a programmatic dependent of the gate/up kernel, which may still
-  // be running: wait (bounded) until every gate/up CTA of expert e has counted
-  // its hidden fragments as written.  The plan read above is complete (gate/up
-  // lets this grid start only after its own wait for the plan).
-  if (threadIdx.x == 0) *ok_s = wait_count(done + e, gu_cpe) ? 1 : 0;
+  // be running: wait (bounded) until every gate/up CTA of this chunk has
+  // counted its hidden fragments as written.  The plan read above is complete
+  // (gate/up lets this grid start only after its own wait for the plan).
+  if (threadIdx.x == 0) *ok_s = wait_count(done + item, gu_cpe) ? 1 : 0;
   __syncthreads();
-  bool ok = *ok_s != 0;
-  if (!ok && threadIdx.x == 0) set_status(status, MOE_STATUS_TIMEOUT);
-  ok = true;   // stream regardless, so every issued copy is consumed
+  if (*ok_s == 0 && threadIdx.x == 0) set_status(status, MOE_STATUS_TIMEOUT);
   pdl_trigger();
-  for (int c0 = 0; c0 < c.n; c0 += 4 * cgp) {
-    const int ncg = min(cgp, (c.n - c0 + 3) / 4);
-    if (c0 > 0 && ok) dn_prefetch<QT>(c);
-    // hidden fragments of the chunk's groups: plain loads (they were written by
-    // other CTAs' plain stores, ordered by the counter's release / acquire)
-    const uint4* src = reinterpret_cast<const uint4*>(hfrag + (size_t)(G0 + c0 / 4) * c.nbF * 512);
-    uint4* dst = reinterpret_cast<uint4*>(smem);
-    for (int i = threadIdx.x; i < ncg * c.nbF * 32; i += kDnWarps * 32) dst[i] = src[i];
-    __syncthreads();
-    if (ncg == 1) ok = dn_chunk<QT, 1>(c, parity, c0, ok);
-    else ok = dn_chunk<QT, 2>(c, parity, c0, ok);
-    __syncthreads();  // the staged hidden fragments are rewritten by the next chunk
-  }
+  const int ncg = min(cgp, (c.n - c0 + 3) / 4);
+  // hidden fragments of the chunk's groups: plain loads (they were written by
+  // other CTAs' plain stores, ordered by the counter's release / acquire); the
+  // rings are streamed regardless of a timeout so every issued copy is consumed
+  const uint4* src = reinterpret_cast<const uint4*>(hfrag + (size_t)(G0 + c0 / 4) * c.nbF * 512);
+  uint4* dst = reinterpret_cast<uint4*>(smem);
+  for (int i = threadIdx.x; i < ncg * c.nbF * 32; i += kDnWarps * 32) dst[i] = src[i];
+  __syncthreads();
+  if (ncg == 1) dn_chunk<QT, 1>(c, parity, c0, true);
+  else dn_chunk<QT, 2>(c, parity, c0, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -848,8 +835,8 @@ struct ExpertsWs {
   int* n_active;
   int* active;
   int* goff;
-  int* gexp;
-  int* done;    // per expert: gate/up CTAs finished
+  int* coff;    // work items: (expert << 16) | chunk, -1 past the last
+  int* done;    // per chunk: gate/up CTAs finished
   uint8_t* hfrag;
   size_t bytes;
 };
@@ -864,8 +851,8 @@ static ExpertsWs carve_experts(void* ws, int rows, int E, int d, int F) {
   w.n_active = c.take<int>(64);
   w.active = c.take<int>(E);
   w.goff = c.take<int>(E + 1);
-  w.gexp = c.take<int>(mg);
-  w.done = c.take<int>(E);
+  w.coff = c.take<int>(mg);
+  w.done = c.take<int>(mg);
   w.hfrag = c.take<uint8_t>((size_t)mg * F * 16);
   w.bytes = align_up(c.used, 256);
   return w;
@@ -921,7 +908,6 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
     p.ks *= 2;
   const int spc = kGuWarps / p.ks;
   p.cpe_gu = (strips_f + spc - 1) / spc;
-  p.grid_gu = est_active * p.cpe_gu;
   // column groups per pass: about twice the mean rows of an expert
   const int mean_rows = (rows + est_active - 1) / est_active;
   const int want_cg = std::max(1, std::min(kMaxCG, (2 * mean_rows + 3) / 4));
@@ -943,10 +929,14 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   const int dn_u = Ring<QT>::kDnU;
   p.nst_dn = std::max(1, std::min(Ring<QT>::kDnStages, (F / 64 + dn_u - 1) / dn_u));
   const int ring_dn = kDnWarps * p.nst_dn * dn_stage_bytes<QT>();
-  p.cgp_dn = std::min(std::min(want_cg, kGuMaxCG), (kMaxSmem - kBarArea - ring_dn) / x_stage_bytes(F, 1));
-  if (p.cgp_dn < 1) return false;
+  // both kernels work on the same chunks of 4 * cgp rows
+  p.cgp_dn = p.cgp_gu;
+  if ((kMaxSmem - kBarArea - ring_dn) / x_stage_bytes(F, 1) < p.cgp_dn) return false;
   p.smem_dn = x_stage_bytes(F, p.cgp_dn) + kBarArea + ring_dn;
-  p.grid_dn = est_active * ((strips_d + kDnWarps - 1) / kDnWarps);
+  // work items: chunks of 4 * cgp rows, at most rows / (4 cgp) + one per expert
+  const int items = std::min(max_groups(rows, E), rows / (4 * p.cgp_gu) + est_active);
+  p.grid_gu = items * p.cpe_gu;
+  p.grid_dn = items * ((strips_d + kDnWarps - 1) / kDnWarps);
   return true;
 }
 
@@ -974,8 +964,8 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   const int mg = max_groups(rows, E);
   if (!planned) {
     ::moe::ProfScope _prof(MOE_K_PLAN, s);
-    plan_kernel<<<1, kPlanThreads, 0, s>>>(offsets, E, rows, mg, w.n_active, w.active, w.goff,
-                                           w.gexp, w.done, w.status);
+    plan_kernel<<<1, kPlanThreads, 0, s>>>(offsets, E, rows, mg, 4 * p.cgp_gu, w.n_active,
+                                           w.active, w.goff, w.coff, w.done, w.status);
   }
   MOE_CHECK(check_launch("plan"));
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
@@ -983,28 +973,37 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
     MOE_CUDA(launch_pdl(gateup_kernel<QT>, dim3(p.grid_gu), dim3(kGuWarps * 32), p.smem_gu, s,
                         w_gate, w_up, mat_bytes, d, F, offsets, (const int*)w.n_active,
-                        (const int*)w.active, (const int*)w.goff, x, x_rows, x_div, x_row_max,
-                        w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.done, w.status));
+                        (const int*)w.active, (const int*)w.goff, (const int*)w.coff, x, x_rows,
+                        x_div, x_row_max, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.done, w.status));
   }
   MOE_CHECK(check_launch("gateup"));
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
     MOE_CUDA(launch_pdl(down_kernel<QT>, dim3(p.grid_dn), dim3(kDnWarps * 32), p.smem_dn, s,
                         w_down, mat_bytes, d, F, offsets, (const int*)w.n_active,
-                        (const int*)w.active, (const int*)w.goff, (const uint8_t*)w.hfrag, y,
-                        y_rows, p.cgp_dn, p.nst_dn, (const int*)w.done, p.cpe_gu, w.status));
+                        (const int*)w.active, (const int*)w.goff, (const int*)w.coff,
+                        (const uint8_t*)w.hfrag, y, y_rows, p.cgp_dn, p.nst_dn,
+                        (const int*)w.done, p.cpe_gu, w.status));
   }
   return check_launch("down");
 }
 
 // Plan arrays inside an experts workspace, for a dispatch that writes them.
+// Rows per work item (chunk) of the GEMV kernels for a call's shape.
+int experts_rows_per_chunk(int qtype, int rows, int E, int d, int F) {
+  ExpertsPlan p;
+  const bool ok = qtype == MOE_Q4_0 ? plan_experts<MOE_Q4_0>(rows, E, d, F, p)
+                                    : plan_experts<MOE_Q8_0>(rows, E, d, F, p);
+  return ok ? 4 * p.cgp_gu : 4;
+}
+
 void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
-                         int** goff, int** gexp, int** done, int* mg) {
+                         int** goff, int** coff, int** done, int* mg) {
   ExpertsWs w = carve_experts(ws, rows, E, d, F);
   *n_active = w.n_active;
   *active = w.active;
   *goff = w.goff;
-  *gexp = w.gexp;
+  *coff = w.coff;
   *done = w.done;
   *mg = max_groups(rows, E);
 }

@@ -10,14 +10,15 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
                 bool planned, int rows_hint);
 void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
-                         int** goff, int** gexp, int** done, int* mg);
+                         int** goff, int** coff, int** done, int* mg);
+int experts_rows_per_chunk(int qtype, int rows, int E, int d, int F);
 int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
                   int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
                   size_t workspace_bytes, cudaStream_t stream, float* row_max);
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
                             int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
-                            int* active, int* goff, int* gexp, int* done, int max_groups,
-                            int32_t* scratch, cudaStream_t s);
+                            int* active, int* goff, int* coff, int* done, int max_groups,
+                            int rpc, int32_t* scratch, cudaStream_t s);
 size_t dispatch_scratch_bytes(int P, int E);
 int experts_workspace(int rows, int E, int d, int F, size_t* bytes);
 int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
@@ -109,11 +110,13 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
   const int P = T * w->k;
   MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
                           ids, wts, L.router_ws, L.router_bytes, s, L.row_max));
-  int *n_active, *active, *goff, *gexp, *done, mg;
-  experts_plan_arrays(L.exp_ws, P, w->E, w->d, w->F, &n_active, &active, &goff, &gexp, &done,
+  int *n_active, *active, *goff, *coff, *done, mg;
+  experts_plan_arrays(L.exp_ws, P, w->E, w->d, w->F, &n_active, &active, &goff, &coff, &done,
                       &mg);
+  const int rpc = experts_rows_per_chunk(w->qtype, P, w->E, w->d, w->F);
   MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
-                                    n_active, active, goff, gexp, done, mg, L.disp_scratch, s));
+                                    n_active, active, goff, coff, done, mg, rpc, L.disp_scratch,
+                                    s));
   MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
                         w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
                         L.row_max, true, 0));

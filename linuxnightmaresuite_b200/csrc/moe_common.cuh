@@ -233,7 +233,7 @@ static __device__ float np_pairwise_sum(const float* a, int n) {
   return np_pairwise_sum(a, n2) + np_pairwise_sum(a + n2, n - n2);
 }
 
-// The same sum computed by a CTA: the leaves of the pairwise tree (runs of at
+// The same sum computed by a CTA: the leaves of the pairwise tree// The same sum computed by a CTA: the leaves of the pairwise tree (runs of at
 // most 128 terms) are summed by separate threads, then thread 0 adds them along
 // the tree.  Bit-identical to np_pairwise_sum.  Call from every thread; scratch
 // holds one float per leaf (np_pairwise_leaves(n)); the result is valid in
@@ -385,6 +385,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+__device__ __forceinline__ void set_status(int* status, int bit) {
+  if (status) atomicOr(status, bit);
+}
+
 // Exclusive scan of one int per thread over the block (<= 1024 threads);
 // sh needs 33 ints.
 static __device__ int block_excl_scan(int v, int* sh, int& total) {
@@ -415,6 +419,42 @@ static __device__ int block_excl_scan(int v, int* sh, int& total) {
   return res;
 }
 
+// Grouped-expert plan from per-expert row counts, written by one CTA whose
+// thread e (< E <= blockDim.x) holds expert e's row count n (0 for e >= E).
+// Every thread calls.  Writes: active experts in ascending order and their
+// count n_active; 4-row group offsets goff[E+1]; the work items of the GEMV
+// kernels, one per chunk of rpc rows of an expert, citem[i] = (e << 16) | j
+// (chunk j of expert e) for i < items and -1 up to max_groups; done[i] = 0.
+// More groups than max_groups sets MOE_STATUS_ROW_OVERFLOW and no items.
+static __device__ void write_expert_plan(int n, int e, int E, int rpc, int max_groups, int* sh,
+                                         int* n_active, int* active, int* goff, int* citem,
+                                         int* done, int* status) {
+  const int ng = (n + 3) / 4;
+  const int nch = n > 0 ? (n + rpc - 1) / rpc : 0;
+  int tot_g, tot_a, tot_c;
+  const int g0 = block_excl_scan(ng, sh, tot_g);
+  const int a0 = block_excl_scan(n > 0 ? 1 : 0, sh, tot_a);
+  const int c0 = block_excl_scan(nch, sh, tot_c);
+  const bool overflow = tot_g > max_groups;
+  if (e < E) {
+    goff[e] = g0;
+    if (n > 0) active[a0] = e;
+    if (!overflow)
+      for (int j = 0; j < nch; ++j) citem[c0 + j] = (e << 16) | j;
+  }
+  if (threadIdx.x == 0) {
+    goff[E] = tot_g;
+    *n_active = overflow ? 0 : tot_a;
+    if (overflow) set_status(status, MOE_STATUS_ROW_OVERFLOW);
+  }
+  const int items = overflow ? 0 : tot_c;
+  for (int i = threadIdx.x; i < max_groups; i += blockDim.x) {
+    if (i >= items) citem[i] = -1;
+    else done[i] = 0;
+  }
+}
+
+
 // Programmatic dependent launch: wait for the previous kernel's completion
 // (no-op when launched normally) / allow the next kernel to start.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -422,8 +462,5 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-__device__ __forceinline__ void set_status(int* status, int bit) {
-  if (status) atomicOr(status, bit);
-}
 
 }  // namespace moe
