@@ -903,14 +903,23 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   const int strips_f = F / 16, strips_d = d / 16;
   const int JT = d / 64;
   const int target = sm_count() * kGuWarps;  // one full CTA per SM
-  p.ks = 1;
-  while (p.ks < 8 && (long long)est_active * strips_f * p.ks < target && JT / (2 * p.ks) >= 2)
-    p.ks *= 2;
-  const int spc = kGuWarps / p.ks;
-  p.cpe_gu = (strips_f + spc - 1) / spc;
   // column groups per pass: about twice the mean rows of an expert
   const int mean_rows = (rows + est_active - 1) / est_active;
   const int want_cg = std::max(1, std::min(kMaxCG, (2 * mean_rows + 3) / 4));
+  // split K over 2, 4 or 8 warps of a strip until the chunks' strips fill the
+  // GPU with one CTA per SM (every CTA builds its chunk's activations for all
+  // of K, so fewer, longer CTAs are preferred)
+#ifndef MOE_KS_BY_ITEMS
+#define MOE_KS_BY_ITEMS 1
+#endif
+  const int cg_est = std::min(want_cg, kGuMaxCG);
+  const int items_est = MOE_KS_BY_ITEMS ? std::max(est_active, (rows + 4 * cg_est - 1) / (4 * cg_est))
+                                        : est_active;
+  p.ks = 1;
+  while (p.ks < 8 && (long long)items_est * strips_f * p.ks < target && JT / (2 * p.ks) >= 2)
+    p.ks *= 2;
+  const int spc = kGuWarps / p.ks;
+  p.cpe_gu = (strips_f + spc - 1) / spc;
   // gate/up: stages for the tiles a warp streams (clamped), then the largest
   // column-group count that fits; fewer stages before fewer groups
   const int gu_u = Ring<QT>::kGuU;
