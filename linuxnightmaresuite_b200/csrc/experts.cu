@@ -198,7 +198,7 @@ __device__ __forceinline__ void block_mma(float2 (&acc)[2], const uint32_t (&a0)
 // The split-K reduction buffer (NCG KB per warp) aliases a gate/up ring.
 template <int QT> struct Ring;
 template <> struct Ring<MOE_Q4_0> {
-  static constexpr int kGuU = 2, kGuStages = 3, kDnU = 4, kDnStages = 3;
+  static constexpr int kGuU = 3, kGuStages = 2, kDnU = 4, kDnStages = 3;
 };
 template <> struct Ring<MOE_Q8_0> {
   static constexpr int kGuU = 2, kGuStages = 2, kDnU = 2, kDnStages = 3;
