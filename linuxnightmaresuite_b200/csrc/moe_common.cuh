@@ -357,6 +357,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
+  {
+    // fast path: the phase is often complete already
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
   uint64_t t0 = 0;
   for (uint32_t it = 0; it < (1u << 24); ++it) {
     uint32_t done;

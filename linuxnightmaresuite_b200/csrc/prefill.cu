@@ -4,19 +4,22 @@
 // (moe_forward.py:129-133) are dense GEMMs:
 //   GEMM1  [rows x d] x [d x 2F]  -> h = silu(gate) * up      (rows x F)
 //   GEMM2  [rows x F] x [F x d]   -> y                        (rows x d)
-// Each CTA computes one 128-row x 128-column tile with tcgen05.mma
-// (kind::f16, fp32 accumulator in tensor memory):
+// The output is cut into 128-row x 128-column tiles (rows of one expert); a
+// persistent CTA per SM walks its share of the tiles with tcgen05.mma
+// (kind::f16, fp32 accumulators in tensor memory):
 //   * the activation tile (fp16 hi and lo planes, see below) arrives by 2-D TMA
-//     with 128-byte swizzle;
-//   * four producer warps dequantise the packed Q4_0 / Q8_0 weight tiles into the
-//     same swizzled layout as fp16 hi + lo (w = d * q exactly, w_hi = fp16(w),
-//     w_lo = fp16(w - w_hi));
+//     with 128-byte swizzle, and is prefetched into L2 several stages ahead;
+//   * eight producer warps dequantise the packed Q4_0 / Q8_0 weight tiles into
+//     the same swizzled layout as fp16 hi + lo (w = d * q exactly, w_hi =
+//     fp16(w), w_lo = fp16(w - w_hi));
 //   * one thread issues three MMAs per 16-wide k step -- x_hi*w_hi + x_hi*w_lo
-//     + x_lo*w_hi -- so operands keep ~22 bits (the reference's f32 tolerance
-//     needs more than one fp16 rounding);
-//   * stage reuse is ordered by mbarriers (TMA transaction counts, producer
-//     arrivals, tcgen05.commit), every wait is bounded;
-//   * four epilogue warps read the accumulator with tcgen05.ld: GEMM1 applies
+//     + x_lo*w_hi -- so operands keep ~22 bits (outputs reach ~1e3 and the
+//     reference's f32 tolerance is absolute);
+//   * the stage ring runs on across tiles; stage reuse is ordered by mbarriers
+//     (TMA transaction counts, producer arrivals, tcgen05.commit), and every
+//     wait is bounded;
+//   * tensor memory holds two accumulator buffers: four epilogue warps read
+//     tile i with tcgen05.ld while the MMAs of tile i + 1 run.  GEMM1 applies
 //     SiLU(gate) * up and writes the hidden hi/lo planes, GEMM2 writes f32 rows.
 // Rows of a 128-row tile past the expert's range are computed and discarded.
 #include <cuda.h>
@@ -24,6 +27,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "moe_common.cuh"
 
@@ -33,16 +37,29 @@ constexpr int kTcM = 128;        // rows (tokens) per tile
 constexpr int kTcN = 128;        // output columns per tile
 constexpr int kTcK = 64;         // k per stage (one packed tile column, 128 B of fp16)
 constexpr int kTcStages = 3;
-constexpr int kTcThreads = 384;  // 12 warps: 0 TMA, 1 MMA, 0-3 epilogue, 4-11 weight producers
+// Warps: 0 TMA (lane 0), 1 MMA (lane 0), 2-17 weight producers (two per
+// 16-row strip, one per half of each packed tile), 18-21 epilogue.
+constexpr int kTcProd0 = 2;
+constexpr int kTcProducers = 16;
+constexpr int kTcEpi0 = kTcProd0 + kTcProducers;
+constexpr int kTcThreads = (kTcEpi0 + 4) * 32;
 constexpr int kTileHalf = kTcM * kTcK * 2;            // one 128 x 64 fp16 tile: 16 KB
 constexpr int kStageBytes = 4 * kTileHalf;            // A hi, A lo, B hi, B lo
 constexpr int kTcSmem = kTcStages * kStageBytes + 1024 + 1024;  // + barriers, + alignment
 constexpr float kTcHScale = 1.0f / 256.0f;            // hidden planes are stored / 256
-// The K range is spread over kTcAcc accumulators (consecutive stage ranges), summed
-// with round-to-nearest in the epilogue: the tensor core's fp32 accumulation
-// truncates, and a 2816-long K otherwise drifts by ~1e-5 relative.
-constexpr int kTcAcc = 4;
-constexpr int kTcCols = kTcAcc * kTcN;                // tensor-memory columns (all 512)
+// Two accumulator buffers (tile i's epilogue overlaps tile i + 1's MMAs), each a
+// "big" accumulator for x_hi*w_hi and a "small" one for the two correction
+// products, added with round-to-nearest in the epilogue: the tensor core's fp32
+// accumulation truncates, and keeping the corrections apart leaves the big
+// accumulator one addition per 16-wide k step.
+constexpr int kTcBufCols = 2 * kTcN;
+constexpr int kTcCols = 2 * kTcBufCols;               // tensor-memory columns (all 512)
+// activation tiles are prefetched into L2 this many stages ahead of their TMA load,
+// weight tiles this many stages ahead of their register load
+#ifndef MOE_TC_L2_AHEAD
+#define MOE_TC_L2_AHEAD 6
+#endif
+constexpr int kTcL2Ahead = MOE_TC_L2_AHEAD;
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -93,6 +110,18 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, 
       : "memory");
 }
 
+// Same MMA with both descriptors given as (low word, shared high word): the
+// stage and k offsets only ever change the 14-bit start-address field.
+__device__ __forceinline__ void tc_mma_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                          uint32_t desc_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n .reg .b64 da, db;\n setp.ne.b32 p, %5, 0;\n"
+      " mov.b64 da, {%1, %3};\n mov.b64 db, {%2, %3};\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(desc_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -100,51 +129,60 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// sum of the same 32 columns of the first n accumulators (kTcN columns apart),
-// in accumulator order
-__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, float (&v)[32], int n) {
-  tmem_ld32(taddr, v);
-  for (int j = 1; j < n; ++j) {
-    float w[32];
-    tmem_ld32(taddr + (uint32_t)(j * kTcN), w);
+// big + small accumulator (kTcN columns apart), 16 columns from taddr
+__device__ __forceinline__ void tmem_ld_pair(uint32_t taddr, float (&v)[16]) {
+  float w[16];
+  tmem_ld16(taddr, v);
+  tmem_ld16(taddr + (uint32_t)kTcN, w);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], w[i]);
-  }
+  for (int i = 0; i < 16; ++i) v[i] = __fadd_rn(v[i], w[i]);
+}
+
+// L2 prefetch of one 128 x 64 box of a tensor map (no shared-memory write)
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 // ---------------------------------------------------------------------------
 // weight dequantisation into the swizzled B tile
 // ---------------------------------------------------------------------------
-// Registers of one packed 16-row x 64-column weight tile for one lane.
+// Registers of one half of a packed 16-row x 64-column weight tile for one
+// lane: half 0 holds the lane's row g, half 1 its row g + 8 (lane = 4g + t).
 template <int QT>
-struct PackedTile {
-  uint4 q[QT == MOE_Q8_0 ? 2 : 1];
-  uint2 sc;
+struct PackedHalf {
+  typename std::conditional<QT == MOE_Q8_0, uint4, uint2>::type q;
+  uint32_t sc;   // the two fp16 block scales of that row
 };
 
 template <int QT>
-__device__ __forceinline__ void load_packed_tile(PackedTile<QT>& p, const uint8_t* tile, int lane) {
+__device__ __forceinline__ void load_packed_half(PackedHalf<QT>& p, const uint8_t* tile, int lane,
+                                                 int half) {
   using Tr = QTraits<QT>;
   const uint8_t* qp = tile + lane * Tr::kLaneBytes;
-  p.q[0] = __ldg(reinterpret_cast<const uint4*>(qp));
-  if (QT == MOE_Q8_0) p.q[QT == MOE_Q8_0 ? 1 : 0] = __ldg(reinterpret_cast<const uint4*>(qp + 16));
-  p.sc = __ldg(reinterpret_cast<const uint2*>(tile + Tr::kTileQuant + (lane >> 2) * 8));
+  if constexpr (QT == MOE_Q8_0) p.q = __ldg(reinterpret_cast<const uint4*>(qp + 16 * half));
+  else p.q = __ldg(reinterpret_cast<const uint2*>(qp + 8 * half));
+  p.sc = __ldg(reinterpret_cast<const uint32_t*>(tile + Tr::kTileQuant + (lane >> 2) * 8 +
+                                                 4 * half));
 }
 
 // w = d * q split into fp16 hi = rn(w) and lo = rn(w - hi), two at a time:
@@ -158,62 +196,56 @@ __device__ __forceinline__ void split_mul2(uint32_t q2, uint32_t d2, uint32_t& h
       : "r"(q2), "r"(d2));
 }
 
-// One packed tile (registers) -> rows [r0, r0+16) of the swizzled hi / lo B
-// tiles.  Lane (g, t) owns rows g and g + 8 and, per 32-wide block, the
-// elements its fragment layout assigns to t.  Quants become exact fp16
-// integers (magic-number adds), then d * q is split in packed fp16 math.
-// Odd rows write their blocks in the opposite order so the lanes of a store
-// phase hit distinct 16-byte chunks (no bank conflicts).
+// One packed half tile (registers) -> row r0 + g + 8 * half of the swizzled hi
+// / lo B tiles.  Lane (g, t) owns, per 32-wide block, the elements its fragment
+// layout assigns to t.  Quants become exact fp16 integers (magic-number adds),
+// then d * q is split in packed fp16 math.  Odd rows write their blocks in the
+// opposite order so the lanes of a store phase hit distinct 16-byte chunks (no
+// bank conflicts).
 template <int QT>
-__device__ __forceinline__ void store_packed_tile(const PackedTile<QT>& p, int lane, uint8_t* bhi,
-                                                  uint8_t* blo, int r0) {
+__device__ __forceinline__ void store_packed_half(const PackedHalf<QT>& p, int lane, int half,
+                                                  uint8_t* bhi, uint8_t* blo, int r0) {
   const int g = lane >> 2, t = lane & 3;
+  const int row = r0 + g + 8 * half;
+  uint8_t* hr = bhi + row * 128;
+  uint8_t* lr = blo + row * 128;
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int row = r0 + g + 8 * half;
-    uint8_t* hr = bhi + row * 128;
-    uint8_t* lr = blo + row * 128;
+  for (int it = 0; it < 2; ++it) {
+    const int b = it ^ (g & 1);
+    const uint32_t d2 = prmt(p.sc, p.sc, b ? 0x3232u : 0x1010u);   // {d, d}
+    if constexpr (QT == MOE_Q8_0) {
+      const uint32_t w0 = b ? p.q.z : p.q.x, w1 = b ? p.q.w : p.q.y;
+      uint32_t q[4], h[4], l[4];
+      dequant_q8(w0, q[0], q[1]);
+      dequant_q8(w1, q[2], q[3]);
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int b = it ^ (g & 1);
-      const int j = half * 2 + b;                        // scale slot
-      const uint32_t sw = j < 2 ? p.sc.x : p.sc.y;
-      const uint32_t d2 = prmt(sw, sw, (j & 1) ? 0x3232u : 0x1010u);   // {d, d}
-      if (QT == MOE_Q8_0) {
-        const uint4& qv = p.q[QT == MOE_Q8_0 ? half : 0];   // row g: q[0], row g+8: q[1]
-        const uint32_t w0 = b ? qv.z : qv.x, w1 = b ? qv.w : qv.y;
-        uint32_t q[4], h[4], l[4];
-        dequant_q8(w0, q[0], q[1]);
-        dequant_q8(w1, q[2], q[3]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) split_mul2(q[i], d2, h[i], l[i]);
-        // elements 32b + 8t .. +7 -> 16-byte chunk 4b + t, swizzled by row
-        const int ch = (4 * b + t) ^ (row & 7);
-        *reinterpret_cast<uint4*>(hr + ch * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(lr + ch * 16) = make_uint4(l[0], l[1], l[2], l[3]);
-      } else {
-        const uint32_t word = half ? (b ? p.q[0].w : p.q[0].z) : (b ? p.q[0].y : p.q[0].x);
-        // bytes i = 0..3 hold element 4t + i (low nibble) and 16 + 4t + i (high)
-        const uint32_t p01 = prmt(word, 0u, 0x4140u), p23 = prmt(word, 0u, 0x4342u);
-        const uint32_t kMagic = 0x64006400u, kSubLo = 0xE408E408u;   // 1024, -1032
-        const uint32_t kMulHi = 0x2C002C00u, kSubHi = 0xD480D480u;   // 1/16, -72
-        const uint32_t lq01 = hadd2_u(lop3_and_or(p01, 0x000F000Fu, kMagic), kSubLo);
-        const uint32_t lq23 = hadd2_u(lop3_and_or(p23, 0x000F000Fu, kMagic), kSubLo);
-        const uint32_t hq01 = hfma2_u(lop3_and_or(p01, 0x00F000F0u, kMagic), kMulHi, kSubHi);
-        const uint32_t hq23 = hfma2_u(lop3_and_or(p23, 0x00F000F0u, kMagic), kMulHi, kSubHi);
-        uint32_t h0, h1, l0, l1;
-        const int ch_lo = (4 * b + (t >> 1)) ^ (row & 7);
-        const int ch_hi = (4 * b + 2 + (t >> 1)) ^ (row & 7);
-        const int off = (t & 1) * 8;
-        split_mul2(lq01, d2, h0, l0);
-        split_mul2(lq23, d2, h1, l1);
-        *reinterpret_cast<uint2*>(hr + ch_lo * 16 + off) = make_uint2(h0, h1);
-        *reinterpret_cast<uint2*>(lr + ch_lo * 16 + off) = make_uint2(l0, l1);
-        split_mul2(hq01, d2, h0, l0);
-        split_mul2(hq23, d2, h1, l1);
-        *reinterpret_cast<uint2*>(hr + ch_hi * 16 + off) = make_uint2(h0, h1);
-        *reinterpret_cast<uint2*>(lr + ch_hi * 16 + off) = make_uint2(l0, l1);
-      }
+      for (int i = 0; i < 4; ++i) split_mul2(q[i], d2, h[i], l[i]);
+      // elements 32b + 8t .. +7 -> 16-byte chunk 4b + t, swizzled by row
+      const int ch = (4 * b + t) ^ (row & 7);
+      *reinterpret_cast<uint4*>(hr + ch * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4*>(lr + ch * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+    } else {
+      const uint32_t word = b ? p.q.y : p.q.x;
+      // bytes i = 0..3 hold element 4t + i (low nibble) and 16 + 4t + i (high)
+      const uint32_t p01 = prmt(word, 0u, 0x4140u), p23 = prmt(word, 0u, 0x4342u);
+      const uint32_t kMagic = 0x64006400u, kSubLo = 0xE408E408u;   // 1024, -1032
+      const uint32_t kMulHi = 0x2C002C00u, kSubHi = 0xD480D480u;   // 1/16, -72
+      const uint32_t lq01 = hadd2_u(lop3_and_or(p01, 0x000F000Fu, kMagic), kSubLo);
+      const uint32_t lq23 = hadd2_u(lop3_and_or(p23, 0x000F000Fu, kMagic), kSubLo);
+      const uint32_t hq01 = hfma2_u(lop3_and_or(p01, 0x00F000F0u, kMagic), kMulHi, kSubHi);
+      const uint32_t hq23 = hfma2_u(lop3_and_or(p23, 0x00F000F0u, kMagic), kMulHi, kSubHi);
+      uint32_t h0, h1, l0, l1;
+      const int ch_lo = (4 * b + (t >> 1)) ^ (row & 7);
+      const int ch_hi = (4 * b + 2 + (t >> 1)) ^ (row & 7);
+      const int off = (t & 1) * 8;
+      split_mul2(lq01, d2, h0, l0);
+      split_mul2(lq23, d2, h1, l1);
+      *reinterpret_cast<uint2*>(hr + ch_lo * 16 + off) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(lr + ch_lo * 16 + off) = make_uint2(l0, l1);
+      split_mul2(hq01, d2, h0, l0);
+      split_mul2(hq23, d2, h1, l1);
+      *reinterpret_cast<uint2*>(hr + ch_hi * 16 + off) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(lr + ch_hi * 16 + off) = make_uint2(l0, l1);
     }
   }
 }
@@ -308,6 +340,46 @@ struct TcArgs {
   int* status;
 };
 
+// Tile t of a launch: m-tile t / n_tiles_n (128 sorted rows of one expert) and
+// n-tile t % n_tiles_n.  CTA c of the persistent grid takes tiles c, c + grid, ...
+struct TcTile {
+  int e, row0, nt;
+};
+
+__device__ __forceinline__ TcTile tc_tile(const TcArgs& a, int t) {
+  const int mt = t / a.n_tiles_n;
+  TcTile r;
+  r.nt = t - mt * a.n_tiles_n;
+  r.e = a.tile_e[mt];
+  r.row0 = a.tile_r0[mt];
+  return r;
+}
+
+// First packed weight tile of B strip `strip` (16 B rows) of a tile; the tiles
+// of consecutive k stages follow it.
+template <int QT, int MODE>
+__device__ __forceinline__ const uint8_t* tc_strip_tiles(const TcArgs& a, const TcTile& tt,
+                                                         int strip, int ksteps) {
+  using Tr = QTraits<QT>;
+  const uint8_t* mat;
+  int wstrip;
+  if (MODE == 0) {
+    mat = (strip < 4 ? a.w0 : a.w1) + (size_t)tt.e * a.mat_bytes;
+    wstrip = tt.nt * 4 + (strip & 3);                 // 64 F-rows per tile
+  } else {
+    mat = a.w0 + (size_t)tt.e * a.mat_bytes;
+    wstrip = tt.nt * 8 + strip;                       // 128 d-rows per tile
+  }
+  return mat + (size_t)wstrip * ksteps * Tr::kTileBytes;
+}
+
+// lane 0 waits, the warp follows its verdict
+__device__ __forceinline__ bool warp_mbar_wait(uint64_t* bar, uint32_t parity, int lane) {
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait(bar, parity);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
 template <int QT, int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
@@ -320,9 +392,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
   uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kTcStages * kStageBytes);
   uint64_t* full_b = full_a + kTcStages;
   uint64_t* empty = full_b + kTcStages;
-  uint64_t* acc_full = empty + kTcStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  int* flag = reinterpret_cast<int*>(tmem_slot + 1);
+  uint64_t* tfull = empty + kTcStages;    // [2] accumulator buffer written
+  uint64_t* tempty = tfull + 2;           // [2] accumulator buffer read out
+  uint64_t* drain = tempty + 2;           // the issuer's last MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Programmatic dependent launches: gate/up waits for the tile plan before
@@ -331,21 +405,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
   // only in its activation producer, so its weight producers start early.
   if (MODE == 0) pdl_wait();
   pdl_trigger();
-  const int mt = blockIdx.x / args.n_tiles_n;
-  const int nt = blockIdx.x % args.n_tiles_n;
-  if (mt >= *args.n_mtiles) return;
-  const int e = args.tile_e[mt];
-  const int row0 = args.tile_r0[mt];
-  const int row_end = args.offsets[e + 1];
+  const int n_tiles = *args.n_mtiles * args.n_tiles_n;
+  if ((int)blockIdx.x >= n_tiles) return;
+  const int my_tiles = (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1;
   const int ksteps = args.K / kTcK;
+  const int total = my_tiles * ksteps;    // stages this CTA runs, over all its tiles
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], 8);
+      mbar_init(&full_b[s], kTcProducers);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
     *flag = 0;
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
@@ -362,148 +438,256 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // activation producer: hi and lo planes of the stage's 128 x 64 tile
-    if (MODE == 1) pdl_wait();
-    for (int kk = 0; kk < ksteps; ++kk) {
-      const int s = kk % kTcStages, round = kk / kTcStages;
-      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
-        *flag = 1;
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // activation producer: hi and lo planes of each stage's 128 x 64 tile;
+      // the L2 prefetch cursor runs kTcL2Ahead stages ahead of the loads
+      if (MODE == 1) pdl_wait();
+      int pf = 0, pf_i = 0, pf_k = 0;
+      int pf_row = tc_tile(args, blockIdx.x).row0;
+      auto l2_step = [&]() {
+        tma_prefetch_2d(&amap, pf_k * kTcK, pf_row);
+        tma_prefetch_2d(&amap, pf_k * kTcK, args.P + pf_row);
+        ++pf;
+        if (++pf_k == ksteps) {
+          pf_k = 0;
+          if (++pf_i < my_tiles) pf_row = tc_tile(args, blockIdx.x + pf_i * gridDim.x).row0;
+        }
+      };
+      while (pf < total && pf < kTcL2Ahead) l2_step();
+      int it = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int row0 = tc_tile(args, blockIdx.x + i * gridDim.x).row0;
+        for (int kk = 0; kk < ksteps; ++kk) {
+          const int s = it % kTcStages, round = it / kTcStages;
+          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+            *flag = 1;
+            set_status(args.status, MOE_STATUS_TIMEOUT);
+            ok = false;
+            break;
+          }
+          if (*flag) {
+            ok = false;
+            break;
+          }
+          if (pf < total) l2_step();
+          uint8_t* st = stage_base + s * kStageBytes;
+          mbar_expect_tx(&full_a[s], 2 * kTileHalf);
+          tma_load_2d(st, &amap, kk * kTcK, row0, &full_a[s]);
+          tma_load_2d(st + kTileHalf, &amap, kk * kTcK, args.P + row0, &full_a[s]);
+          ++it;
+        }
       }
-      uint8_t* st = stage_base + s * kStageBytes;
-      mbar_expect_tx(&full_a[s], 2 * kTileHalf);
-      tma_load_2d(st, &amap, kk * kTcK, row0, &full_a[s]);
-      tma_load_2d(st + kTileHalf, &amap, kk * kTcK, args.P + row0, &full_a[s]);
+      // the copies this thread issued land before the CTA exits (bounded)
+      for (int s = 0; s < kTcStages; ++s)
+        if (it > s) mbar_wait(&full_a[s], ((it - 1 - s) / kTcStages) & 1);
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    const uint32_t idesc = tc_idesc(kTcM, kTcN);
-    bool ok = true;
-    for (int kk = 0; kk < ksteps && ok; ++kk) {
-      const int s = kk % kTcStages, round = kk / kTcStages;
-      if (!mbar_wait(&full_a[s], round & 1) || !mbar_wait(&full_b[s], round & 1)) {
-        *flag = 1;
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint8_t* st = stage_base + s * kStageBytes;
-      const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + kTileHalf);
-      const uint64_t bhi = sw128_desc(st + 2 * kTileHalf), blo = sw128_desc(st + 3 * kTileHalf);
-      // accumulator j = kk * nacc / ksteps takes a consecutive run of stages
-      const int nacc = ksteps < kTcAcc ? ksteps : kTcAcc;
-      const int j = kk * nacc / ksteps;
-      const bool first = kk == 0 || (kk - 1) * nacc / ksteps != j;
-      const uint32_t dacc = tmem + (uint32_t)(j * kTcN);
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer: tile i accumulates into buffer i & 1 once the epilogue has
+      // read that buffer's previous tile
+      const uint32_t idesc = tc_idesc(kTcM, kTcN);
+      // descriptor of stage 0's A-hi tile; every other operand tile of every
+      // stage differs from it only in the start-address field (addr >> 4 < 2^14)
+      const uint64_t d0 = sw128_desc(stage_base);
+      const uint32_t d0_lo = (uint32_t)d0, d_hi = (uint32_t)(d0 >> 32);
+      constexpr uint32_t kHalf16 = kTileHalf >> 4, kStage16 = kStageBytes >> 4;
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int b = i & 1, use = i >> 1;
+        if (use > 0 && !mbar_wait(&tempty[b], (use - 1) & 1)) {
+          *flag = 1;
+          set_status(args.status, MOE_STATUS_TIMEOUT);
+          ok = false;
+        }
+        // the epilogue's tensor-memory reads of buffer b precede these MMAs
+        tc_fence_after();
+        const uint32_t dbig = tmem + (uint32_t)(b * kTcBufCols);
+        const uint32_t dsmall = dbig + (uint32_t)kTcN;
+        for (int kk = 0; kk < ksteps && ok; ++kk) {
+          // the weight tile (producer warps) usually completes after the TMA copy;
+          // the barriers order the producers' proxy-fenced stores and the TMA
+          // bytes before the MMAs' shared-memory reads
+          if (!mbar_wait(&full_b[s], phase) || !mbar_wait(&full_a[s], phase)) {
+            *flag = 1;
+            set_status(args.status, MOE_STATUS_TIMEOUT);
+            ok = false;
+            break;
+          }
+          const uint32_t ahi = d0_lo + (uint32_t)s * kStage16, alo = ahi + kHalf16;
+          const uint32_t bhi = ahi + 2 * kHalf16, blo = ahi + 3 * kHalf16;
 #pragma unroll
-      for (int k16 = 0; k16 < kTcK / 16; ++k16) {
-        const uint64_t adv = (uint64_t)((k16 * 32) >> 4);   // +32 bytes per k16
-        const uint32_t acc0 = (!first || k16 > 0) ? 1u : 0u;
-        tc_mma(dacc, ahi + adv, bhi + adv, idesc, acc0);
-        tc_mma(dacc, ahi + adv, blo + adv, idesc, 1u);
-        tc_mma(dacc, alo + adv, bhi + adv, idesc, 1u);
+          for (int k16 = 0; k16 < kTcK / 16; ++k16) {
+            const uint32_t adv = (uint32_t)((k16 * 32) >> 4);   // +32 bytes per k16
+            const uint32_t acc = (kk > 0 || k16 > 0) ? 1u : 0u;
+            tc_mma_lo(dbig, ahi + adv, bhi + adv, d_hi, idesc, acc);
+            tc_mma_lo(dsmall, ahi + adv, blo + adv, d_hi, idesc, acc);
+            tc_mma_lo(dsmall, alo + adv, bhi + adv, d_hi, idesc, 1u);
+          }
+          tc_commit(&empty[s]);   // stage s free once these MMAs complete
+          if (++s == kTcStages) {
+            s = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(&tfull[b]);     // buffer b complete (or abandoned: the flag is set)
       }
-      tc_commit(&empty[s]);   // stage s free once these MMAs complete
+      // every MMA issued here completes before the tensor memory is released
+      tc_commit(drain);
+      mbar_wait(drain, 0);
     }
-    tc_commit(acc_full);      // accumulator complete (or abandoned)
-  } else if (warp >= 4) {
-    // weight producers: warp 4 + i dequantises strip i (16 B-rows) of every
-    // stage; the next stage's packed tile is loaded before this one is stored
-    const int strip = warp - 4;                       // 0..7 -> B rows 16*strip
-    const uint8_t* mat;
-    int wstrip;
-    if (MODE == 0) {
-      mat = (strip < 4 ? args.w0 : args.w1) + (size_t)e * args.mat_bytes;
-      wstrip = nt * 4 + (strip & 3);                  // 64 F-rows per tile
-    } else {
-      mat = args.w0 + (size_t)e * args.mat_bytes;
-      wstrip = nt * 8 + strip;                        // 128 d-rows per tile
-    }
-    const uint8_t* tiles = mat + (size_t)wstrip * ksteps * Tr::kTileBytes;
-    // three packed tiles in flight per lane: the load of stage kk + 3 is issued
-    // as soon as stage kk has been stored
-    PackedTile<QT> p[3];
+  } else if (warp < kTcEpi0) {
+    // weight producers: warps 2s + 2 and 2s + 3 dequantise the two halves of
+    // strip s (16 B-rows) of every stage.  The register cursor loads stage
+    // it + 3 as soon as stage it is stored; the L2 cursor (half 0 only) runs
+    // kTcL2Ahead stages ahead of it.
+    const int strip = (warp - kTcProd0) >> 1;         // 0..7 -> B rows 16*strip
+    const int half = (warp - kTcProd0) & 1;
+    auto strip_of = [&](int i) {
+      return tc_strip_tiles<QT, MODE>(args, tc_tile(args, blockIdx.x + i * gridDim.x), strip,
+                                      ksteps);
+    };
+    int li = 0, lk = 0;
+    const uint8_t* lp = strip_of(0);
+    int qn = 0, qi = 0, qk = 0;
+    const uint8_t* qp = lp;
+    constexpr int kLines = (Tr::kTileBytes + 127) / 128;
+    auto l2_step = [&]() {
+      const uint8_t* t = qp + (size_t)qk * Tr::kTileBytes;
+      if (lane < kLines) prefetch_l2(t + lane * 128);
+      else if (lane == kLines) prefetch_l2(t + Tr::kTileBytes - 1);
+      ++qn;
+      if (++qk == ksteps) {
+        qk = 0;
+        if (++qi < my_tiles) qp = strip_of(qi);
+      }
+    };
+    auto load_next = [&](PackedHalf<QT>& p) {
+      load_packed_half<QT>(p, lp + (size_t)lk * Tr::kTileBytes, lane, half);
+      if (++lk == ksteps) {
+        lk = 0;
+        if (++li < my_tiles) lp = strip_of(li);
+      }
+    };
+    PackedHalf<QT> p[3];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
-      if (i < ksteps) load_packed_tile<QT>(p[i], tiles + (size_t)i * Tr::kTileBytes, lane);
+      if (i < total) load_next(p[i]);
+    if (half == 0)
+      while (qn < total && qn < 3 + kTcL2Ahead) l2_step();
     bool ok = true;
-    for (int k0 = 0; k0 < ksteps && ok; k0 += 3) {
+    for (int it0 = 0; it0 < total && ok; it0 += 3) {
 #pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        const int kk = k0 + i;
-        if (kk < ksteps && ok) {
-          const int s = kk % kTcStages, round = kk / kTcStages;
-          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
-            if (lane == 0) *flag = 1;
+      for (int j = 0; j < 3; ++j) {
+        const int it = it0 + j;
+        if (it < total && ok) {
+          const int s = it % kTcStages, round = it / kTcStages;
+          if (round > 0 && !warp_mbar_wait(&empty[s], (round - 1) & 1, lane)) {
+            if (lane == 0) {
+              *flag = 1;
+              set_status(args.status, MOE_STATUS_TIMEOUT);
+            }
             ok = false;
+          } else if ((it & 15) == 0 && __shfl_sync(0xffffffffu, *flag, 0)) {
+            ok = false;   // another role gave up
           } else {
             uint8_t* st = stage_base + s * kStageBytes;
-            store_packed_tile<QT>(p[i], lane, st + 2 * kTileHalf, st + 3 * kTileHalf, strip * 16);
-            if (kk + 3 < ksteps)
-              load_packed_tile<QT>(p[i], tiles + (size_t)(kk + 3) * Tr::kTileBytes, lane);
+            store_packed_half<QT>(p[j], lane, half, st + 2 * kTileHalf, st + 3 * kTileHalf,
+                                  strip * 16);
             fence_proxy_async_smem();   // generic stores -> visible to the tensor core
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_b[s]);
+            // the next loads go out after the fence, which would otherwise wait for them
+            if (it + 3 < total) {
+              load_next(p[j]);
+              if (half == 0 && qn < total) l2_step();
+            }
           }
         }
       }
+    }
+  } else if (warp >= kTcEpi0) {
+    // epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (= tile rows)
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    for (int i = 0; i < my_tiles; ++i) {
+      const TcTile tt = tc_tile(args, blockIdx.x + i * gridDim.x);
+      const int row = tt.row0 + r;
+      const bool valid = row < args.offsets[tt.e + 1];
+      float rs = 0.f;
+      int orow = 0;
+      if (MODE == 0) rs = valid ? args.row_scale[row] : 0.f;
+      else orow = valid ? (args.y_rows ? args.y_rows[row] : row) : 0;
+      const int b = i & 1, use = i >> 1;
+      const bool got = warp_mbar_wait(&tfull[b], use & 1, lane);
+      tc_fence_after();
+      if (!got) {
+        if (lane == 0) {
+          *flag = 1;
+          set_status(args.status, MOE_STATUS_TIMEOUT);
+        }
+        break;
+      }
+      if (__shfl_sync(0xffffffffu, *flag, 0)) break;
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kTcBufCols);
+      if (MODE == 0) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {           // gate columns [16c, 16c+16), up [64+16c, ..)
+          float g[16], u[16];
+          tmem_ld_pair(taddr + 16 * c, g);
+          tmem_ld_pair(taddr + 64 + 16 * c, u);
+          if (valid) {
+            __half* hi = args.h_planes + (size_t)row * args.F + tt.nt * 64 + 16 * c;
+            __half* lo = args.h_planes + ((size_t)args.P + row) * args.F + tt.nt * 64 + 16 * c;
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              float hv[2];
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                const float h = silu_f(g[j + k] * rs) * (u[j + k] * rs);
+                hv[k] = h * kTcHScale;
+                if (!(fabsf(hv[k]) <= 65504.f)) set_status(args.status, MOE_STATUS_ROW_OVERFLOW);
+              }
+              const __half2 hh = __floats2half2_rn(hv[0], hv[1]);
+              const float2 hf = __half22float2(hh);
+              const __half2 ll = __floats2half2_rn(hv[0] - hf.x, hv[1] - hf.y);
+              hw[j / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+              lw[j / 2] = *reinterpret_cast<const uint32_t*>(&ll);
+            }
+            reinterpret_cast<uint4*>(hi)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            reinterpret_cast<uint4*>(hi)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            reinterpret_cast<uint4*>(lo)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            reinterpret_cast<uint4*>(lo)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float v[16];
+          tmem_ld_pair(taddr + 16 * c, v);
+          if (valid) {
+            float4* dst = reinterpret_cast<float4*>(args.y + (size_t)orow * args.d +
+                                                    tt.nt * kTcN + 16 * c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_float4(v[4 * j] * (1.f / kTcHScale), v[4 * j + 1] * (1.f / kTcHScale),
+                                   v[4 * j + 2] * (1.f / kTcHScale),
+                                   v[4 * j + 3] * (1.f / kTcHScale));
+          }
+        }
+      }
+      // buffer b may take tile i + 2 once every epilogue warp has read it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
     }
   }
 
-  // epilogue: warps 0-3 own TMEM lanes 32w .. 32w+31 (= tile rows)
   __syncwarp();
-  if (warp < 4) {
-    const bool ok = mbar_wait(acc_full, 0) && *flag == 0;
-    tc_fence_after();
-    const int r = 32 * warp + lane;
-    const int row = row0 + r;
-    const bool valid = ok && row < row_end;
-    const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
-    const int acc_used = ksteps < kTcAcc ? ksteps : kTcAcc;
-    if (!ok && lane == 0) set_status(args.status, MOE_STATUS_TIMEOUT);
-    if (MODE == 0) {
-      const float rs = valid ? args.row_scale[row] : 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {           // gate columns [32c, 32c+32), up [64+32c, ..)
-        float g[32], u[32];
-        tmem_ld_sum(taddr + 32 * c, g, acc_used);
-        tmem_ld_sum(taddr + 64 + 32 * c, u, acc_used);
-        if (valid) {
-          __half* hi = args.h_planes + (size_t)row * args.F + nt * 64 + 32 * c;
-          __half* lo = args.h_planes + ((size_t)args.P + row) * args.F + nt * 64 + 32 * c;
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float hv[2];
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const float h = silu_f(g[j + q] * rs) * (u[j + q] * rs);
-              hv[q] = h * kTcHScale;
-              if (!(fabsf(hv[q]) <= 65504.f)) set_status(args.status, MOE_STATUS_ROW_OVERFLOW);
-            }
-            const __half2 hh = __floats2half2_rn(hv[0], hv[1]);
-            const float2 hf = __half22float2(hh);
-            reinterpret_cast<__half2*>(hi)[j / 2] = hh;
-            reinterpret_cast<__half2*>(lo)[j / 2] = __floats2half2_rn(hv[0] - hf.x, hv[1] - hf.y);
-          }
-        }
-      }
-    } else {
-      const int orow = valid ? (args.y_rows ? args.y_rows[row] : row) : 0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld_sum(taddr + 32 * c, v, acc_used);
-        if (valid) {
-          float4* dst = reinterpret_cast<float4*>(args.y + (size_t)orow * args.d + nt * kTcN + 32 * c);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(v[4 * j] * (1.f / kTcHScale), v[4 * j + 1] * (1.f / kTcHScale),
-                                 v[4 * j + 2] * (1.f / kTcHScale), v[4 * j + 3] * (1.f / kTcHScale));
-        }
-      }
-    }
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -602,6 +786,10 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
     attr_set |= 1ull << (dev & 63);
   }
+  static int sm_count[64] = {};
+  if (!sm_count[dev & 63])
+    MOE_CUDA(cudaDeviceGetAttribute(&sm_count[dev & 63], cudaDevAttrMultiProcessorCount, dev));
+  const int sms = sm_count[dev & 63];
   const int max_tiles = tc_max_tiles(rows, E);
   {
     ::moe::ProfScope _prof(MOE_K_PLAN, s);
@@ -637,8 +825,9 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   a1.status = status;
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
-    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 0>, dim3(max_tiles * a1.n_tiles_n), dim3(kTcThreads),
-                        kTcSmem, s, xmap, a1));
+    // persistent: one CTA per SM at most, each walking its share of the tiles
+    const int grid = std::min(max_tiles * a1.n_tiles_n, sms);
+    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 0>, dim3(grid), dim3(kTcThreads), kTcSmem, s, xmap, a1));
   }
   MOE_CHECK(check_launch("tc_gemm gate/up"));
   TcArgs a2 = a1;
@@ -650,8 +839,8 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   a2.y_rows = y_rows;
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
-    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 1>, dim3(max_tiles * a2.n_tiles_n), dim3(kTcThreads),
-                        kTcSmem, s, hmap, a2));
+    const int grid = std::min(max_tiles * a2.n_tiles_n, sms);
+    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 1>, dim3(grid), dim3(kTcThreads), kTcSmem, s, hmap, a2));
   }
   return check_launch("tc_gemm down");
 }
