@@ -34,26 +34,27 @@
 namespace moe {
 
 constexpr int kTcM = 128;        // rows (tokens) per tile
-constexpr int kTcN = 128;        // output columns per tile
+constexpr int kTcNMax = 256;     // output columns per tile (a last, narrower tile has 128)
 constexpr int kTcK = 64;         // k per stage (one packed tile column, 128 B of fp16)
-constexpr int kTcStages = 3;
-// Warps: 0 TMA (lane 0), 1 MMA (lane 0), 2-17 weight producers (two per
-// 16-row strip, one per half of each packed tile), 18-21 epilogue.
+constexpr int kTcStages = 2;
+// Warps: 0 TMA (lane 0), 1 MMA (lane 0), 2-17 weight producers (one per
+// 16-row strip of the B tile), 18-21 epilogue.
 constexpr int kTcProd0 = 2;
-constexpr int kTcProducers = 16;
+constexpr int kTcProducers = kTcNMax / 16;
 constexpr int kTcEpi0 = kTcProd0 + kTcProducers;
 constexpr int kTcThreads = (kTcEpi0 + 4) * 32;
-constexpr int kTileHalf = kTcM * kTcK * 2;            // one 128 x 64 fp16 tile: 16 KB
-constexpr int kStageBytes = 4 * kTileHalf;            // A hi, A lo, B hi, B lo
+constexpr int kATile = kTcM * kTcK * 2;               // one 128 x 64 fp16 plane tile: 16 KB
+constexpr int kBTile = kTcNMax * kTcK * 2;            // one 256 x 64 fp16 plane tile: 32 KB
+constexpr int kStageBytes = 2 * kATile + 2 * kBTile;  // A hi, A lo, B hi, B lo: 96 KB
 constexpr int kTcSmem = kTcStages * kStageBytes + 1024 + 1024;  // + barriers, + alignment
 constexpr float kTcHScale = 1.0f / 256.0f;            // hidden planes are stored / 256
-// Two accumulator buffers (tile i's epilogue overlaps tile i + 1's MMAs), each a
-// "big" accumulator for x_hi*w_hi and a "small" one for the two correction
-// products, added with round-to-nearest in the epilogue: the tensor core's fp32
-// accumulation truncates, and keeping the corrections apart leaves the big
-// accumulator one addition per 16-wide k step.
-constexpr int kTcBufCols = 2 * kTcN;
-constexpr int kTcCols = 2 * kTcBufCols;               // tensor-memory columns (all 512)
+// Tensor memory: a "big" accumulator for x_hi*w_hi in columns [0, 256) and a
+// "small" one for the two correction products in [256, 512), added with
+// round-to-nearest in the epilogue.  The tensor core's fp32 accumulation
+// truncates; keeping the corrections apart leaves the big accumulator one
+// addition per 16-wide k step.
+constexpr int kTcSmallCol = kTcNMax;
+constexpr int kTcCols = 2 * kTcNMax;                  // all 512 columns
 // activation tiles are prefetched into L2 this many stages ahead of their TMA load,
 // weight tiles this many stages ahead of their register load
 #ifndef MOE_TC_L2_AHEAD
@@ -143,11 +144,11 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// big + small accumulator (kTcN columns apart), 16 columns from taddr
+// big + small accumulator, 16 columns from taddr
 __device__ __forceinline__ void tmem_ld_pair(uint32_t taddr, float (&v)[16]) {
   float w[16];
   tmem_ld16(taddr, v);
-  tmem_ld16(taddr + (uint32_t)kTcN, w);
+  tmem_ld16(taddr + (uint32_t)kTcSmallCol, w);
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __fadd_rn(v[i], w[i]);
 }
@@ -318,8 +319,10 @@ tc_tile_plan_kernel(const int32_t* __restrict__ offsets, int E, int max_tiles,
 }
 
 // ---------------------------------------------------------------------------
-// the GEMM.  MODE 0: gate/up (B rows 0-63 from W_gate, 64-127 from W_up, the
-// same 64 F-rows), epilogue SiLU(gate)*up -> hidden planes.  MODE 1: down.
+// the GEMMs.  MODE 0 (gate/up): an n-tile covers 64 F-rows -- B rows 0-63 from
+// W_gate, 64-127 from W_up -- and the epilogue writes SiLU(gate) * up to the
+// hidden planes.  MODE 1 (down): an n-tile covers min(256, d - 256 nt) output
+// columns.
 // ---------------------------------------------------------------------------
 struct TcArgs {
   const uint8_t* w0;       // MODE 0: W_gate stack; MODE 1: W_down stack
@@ -340,35 +343,52 @@ struct TcArgs {
   int* status;
 };
 
+constexpr int kGuFRows = 64;   // F-rows per gate/up tile
+
 // Tile t of a launch: m-tile t / n_tiles_n (128 sorted rows of one expert) and
 // n-tile t % n_tiles_n.  CTA c of the persistent grid takes tiles c, c + grid, ...
 struct TcTile {
-  int e, row0, nt;
+  int e, row0;
+  int n0;   // MODE 0: first F-row; MODE 1: first output column
+  int nr;   // MODE 0: F-rows (64); MODE 1: output columns (128 or 256)
 };
 
+template <int MODE>
 __device__ __forceinline__ TcTile tc_tile(const TcArgs& a, int t) {
   const int mt = t / a.n_tiles_n;
+  const int nt = t - mt * a.n_tiles_n;
   TcTile r;
-  r.nt = t - mt * a.n_tiles_n;
   r.e = a.tile_e[mt];
   r.row0 = a.tile_r0[mt];
+  if (MODE == 0) {
+    r.n0 = nt * kGuFRows;
+    r.nr = kGuFRows;
+  } else {
+    r.n0 = nt * kTcNMax;
+    r.nr = min(kTcNMax, a.d - r.n0);
+  }
   return r;
 }
 
-// First packed weight tile of B strip `strip` (16 B rows) of a tile; the tiles
-// of consecutive k stages follow it.
+// First packed weight tile of B strip `strip` (rows 16 strip .. + 15) of a
+// tile, or null if the tile is narrower; the tiles of consecutive k stages
+// follow it.
 template <int QT, int MODE>
 __device__ __forceinline__ const uint8_t* tc_strip_tiles(const TcArgs& a, const TcTile& tt,
                                                          int strip, int ksteps) {
   using Tr = QTraits<QT>;
+  const int row = 16 * strip;
   const uint8_t* mat;
   int wstrip;
   if (MODE == 0) {
-    mat = (strip < 4 ? a.w0 : a.w1) + (size_t)tt.e * a.mat_bytes;
-    wstrip = tt.nt * 4 + (strip & 3);                 // 64 F-rows per tile
+    if (row >= 2 * tt.nr) return nullptr;
+    const bool up = row >= tt.nr;
+    mat = (up ? a.w1 : a.w0) + (size_t)tt.e * a.mat_bytes;
+    wstrip = (tt.n0 + row - (up ? tt.nr : 0)) / 16;
   } else {
+    if (row >= tt.nr) return nullptr;
     mat = a.w0 + (size_t)tt.e * a.mat_bytes;
-    wstrip = tt.nt * 8 + strip;                       // 128 d-rows per tile
+    wstrip = (tt.n0 + row) / 16;
   }
   return mat + (size_t)wstrip * ksteps * Tr::kTileBytes;
 }
@@ -380,55 +400,163 @@ __device__ __forceinline__ bool warp_mbar_wait(uint64_t* bar, uint32_t parity, i
   return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
-template <int QT, int MODE>
-__global__ void __launch_bounds__(kTcThreads, 1)
-tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
-  using Tr = QTraits<QT>;
-  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
-  // 1024-byte alignment for the swizzled tiles
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* stage_base = smem;
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kTcStages * kStageBytes);
-  uint64_t* full_b = full_a + kTcStages;
-  uint64_t* empty = full_b + kTcStages;
-  uint64_t* tfull = empty + kTcStages;    // [2] accumulator buffer written
-  uint64_t* tempty = tfull + 2;           // [2] accumulator buffer read out
-  uint64_t* drain = tempty + 2;           // the issuer's last MMAs
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+__device__ __forceinline__ void tc_fail(volatile int* flag, int* status) {
+  *flag = 1;
+  set_status(status, MOE_STATUS_TIMEOUT);
+}
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Programmatic dependent launches: gate/up waits for the tile plan before
-  // anything else; down reads the plan at once (complete, because gate/up
-  // triggers only after its own wait) and waits for gate/up's hidden planes
-  // only in its activation producer, so its weight producers start early.
-  if (MODE == 0) pdl_wait();
-  pdl_trigger();
-  const int n_tiles = *args.n_mtiles * args.n_tiles_n;
-  if ((int)blockIdx.x >= n_tiles) return;
-  const int my_tiles = (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1;
-  const int ksteps = args.K / kTcK;
-  const int total = my_tiles * ksteps;    // stages this CTA runs, over all its tiles
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], kTcProducers);
-      mbar_init(&empty[s], 1);
+// Activation producer (one thread): hi and lo planes of each stage's 128 x 64
+// A tile by TMA; an L2 prefetch cursor runs kTcL2Ahead stages ahead of the
+// loads.  Before returning it waits (bounded) for the copies it issued.
+template <int MODE, int STAGES, int STAGE_BYTES>
+__device__ __forceinline__ void tc_tma_role(const CUtensorMap* amap, const TcArgs& args,
+                                            int my_tiles, int ksteps, uint8_t* stage_base,
+                                            uint64_t* full_a, uint64_t* empty,
+                                            volatile int* flag) {
+  const int total = my_tiles * ksteps;
+  int pf = 0, pf_i = 0, pf_k = 0;
+  int pf_row = tc_tile<MODE>(args, blockIdx.x).row0;
+  auto l2_step = [&]() {
+    tma_prefetch_2d(amap, pf_k * kTcK, pf_row);
+    tma_prefetch_2d(amap, pf_k * kTcK, args.P + pf_row);
+    ++pf;
+    if (++pf_k == ksteps) {
+      pf_k = 0;
+      if (++pf_i < my_tiles) pf_row = tc_tile<MODE>(args, blockIdx.x + pf_i * gridDim.x).row0;
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+  };
+  while (pf < total && pf < kTcL2Ahead) l2_step();
+  int it = 0;
+  bool ok = true;
+  for (int i = 0; i < my_tiles && ok; ++i) {
+    const int row0 = tc_tile<MODE>(args, blockIdx.x + i * gridDim.x).row0;
+    for (int kk = 0; kk < ksteps; ++kk) {
+      const int s = it % STAGES, round = it / STAGES;
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
+        tc_fail(flag, args.status);
+        ok = false;
+        break;
+      }
+      if (*flag) {
+        ok = false;
+        break;
+      }
+      if (pf < total) l2_step();
+      uint8_t* st = stage_base + s * STAGE_BYTES;
+      mbar_expect_tx(&full_a[s], 2 * kATile);
+      tma_load_2d(st, amap, kk * kTcK, row0, &full_a[s]);
+      tma_load_2d(st + kATile, amap, kk * kTcK, args.P + row0, &full_a[s]);
+      ++it;
     }
-    mbar_init(drain, 1);
-    *flag = 0;
-    fence_mbar_init();
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
   }
+  for (int s = 0; s < STAGES; ++s)
+    if (it > s) mbar_wait(&full_a[s], ((it - 1 - s) / STAGES) & 1);
+}
+
+// One producer's registers for one stage: both halves of its packed tile, or
+// nothing (tile narrower than the producer's strip).
+template <int QT>
+struct StripStage {
+  PackedHalf<QT> h[2];
+  bool active;
+};
+
+// Weight producer (one warp): dequantises B rows 16 strip .. + 15 of every
+// stage (both halves of one packed tile) into the hi / lo planes at B_OFF and
+// B_OFF + B_PLANE.  The register ring loads stage it + STAGES as soon as stage
+// it is stored; the L2 cursor runs kTcL2Ahead stages ahead of it.
+template <int QT, int MODE, int STAGES, int STAGE_BYTES, int B_OFF, int B_PLANE>
+__device__ __forceinline__ void tc_producer_role(const TcArgs& args, int strip, int lane,
+                                                 int my_tiles, int ksteps, uint8_t* stage_base,
+                                                 uint64_t* full_b, uint64_t* empty,
+                                                 volatile int* flag) {
+  using Tr = QTraits<QT>;
+  const int total = my_tiles * ksteps;
+  auto strip_of = [&](int i) {
+    return tc_strip_tiles<QT, MODE>(args, tc_tile<MODE>(args, blockIdx.x + i * gridDim.x), strip,
+                                    ksteps);
+  };
+  int li = 0, lk = 0;
+  const uint8_t* lp = strip_of(0);
+  int qn = 0, qi = 0, qk = 0;
+  const uint8_t* qp = lp;
+  constexpr int kLines = (Tr::kTileBytes + 127) / 128;
+  auto l2_step = [&]() {
+    if (qp) {
+      const uint8_t* t = qp + (size_t)qk * Tr::kTileBytes;
+      if (lane < kLines) prefetch_l2(t + lane * 128);
+      else if (lane == kLines) prefetch_l2(t + Tr::kTileBytes - 1);
+    }
+    ++qn;
+    if (++qk == ksteps) {
+      qk = 0;
+      if (++qi < my_tiles) qp = strip_of(qi);
+    }
+  };
+  auto load_next = [&](StripStage<QT>& p) {
+    p.active = lp != nullptr;
+    if (p.active) {
+      const uint8_t* t = lp + (size_t)lk * Tr::kTileBytes;
+      load_packed_half<QT>(p.h[0], t, lane, 0);
+      load_packed_half<QT>(p.h[1], t, lane, 1);
+    }
+    if (++lk == ksteps) {
+      lk = 0;
+      if (++li < my_tiles) lp = strip_of(li);
+    }
+  };
+  StripStage<QT> p[STAGES];
+#pragma unroll
+  for (int i = 0; i < STAGES; ++i)
+    if (i < total) load_next(p[i]);
+  while (qn < total && qn < STAGES + kTcL2Ahead) l2_step();
+  bool ok = true;
+  for (int it0 = 0; it0 < total && ok; it0 += STAGES) {
+#pragma unroll
+    for (int j = 0; j < STAGES; ++j) {
+      const int it = it0 + j;
+      if (it < total && ok) {
+        const int round = it / STAGES;   // slot = j
+        if (round > 0 && !warp_mbar_wait(&empty[j], (round - 1) & 1, lane)) {
+          if (lane == 0) tc_fail(flag, args.status);
+          ok = false;
+        } else if ((it & 15) == 0 && __shfl_sync(0xffffffffu, *flag, 0)) {
+          ok = false;   // another role gave up
+        } else {
+          if (p[j].active) {
+            uint8_t* bt = stage_base + j * STAGE_BYTES + B_OFF;
+            store_packed_half<QT>(p[j].h[0], lane, 0, bt, bt + B_PLANE, strip * 16);
+            store_packed_half<QT>(p[j].h[1], lane, 1, bt, bt + B_PLANE, strip * 16);
+            fence_proxy_async_smem();   // generic stores -> visible to the tensor core
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full_b[j]);
+          // the next loads go out after the fence, which would otherwise wait for them
+          if (it + STAGES < total) {
+            load_next(p[j]);
+            if (qn < total) l2_step();
+          }
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tc_dealloc_all(uint32_t tmem, int warp) {
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTcCols)
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ uint32_t tc_alloc_all(uint32_t* slot, int warp) {
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
+                     smem_u32(slot)),
                  "n"(kTcCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -436,89 +564,319 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  return *slot;
+}
+
+// ---------------------------------------------------------------------------
+// gate/up: 128 x 128 tiles, 3 stages of 64 KB.  The x_hi * w_hi products of
+// each kGuPeriod-stage period go to a fresh partial accumulator (P0 / P1 in
+// tensor memory, alternating); eight promoter warps add each finished partial
+// into fp32 registers with round-to-nearest, so the tensor core's truncating
+// accumulation never runs over more than 4 * kGuPeriod k16 steps.  The
+// correction products accumulate over the whole tile in S0 / S1 (alternating
+// per tile; they are ~2^-11 of the result).  Warps: 0 TMA, 1 MMA, 2-9 weight
+// producers, 10-17 promoters + epilogue (two per tensor-memory lane quarter,
+// each owning 32 gate and the matching 32 up columns).
+// ---------------------------------------------------------------------------
+constexpr int kGuN = 2 * kGuFRows;                        // 128 B rows
+constexpr int kGuStages = 3;
+constexpr int kGuBTile = kGuN * kTcK * 2;                 // 16 KB
+constexpr int kGuStageBytes = 2 * kATile + 2 * kGuBTile;  // 64 KB
+constexpr int kGuProducers = kGuN / 16;                   // 8
+constexpr int kGuProm0 = 2 + kGuProducers;
+constexpr int kGuPromoters = 8;
+constexpr int kGuThreads = (kGuProm0 + kGuPromoters) * 32;
+constexpr int kGuSmem = kGuStages * kGuStageBytes + 1024 + 1024;
+constexpr int kGuPeriod = 2;                              // stages per partial
+constexpr int kGuSCol = 2 * kGuN;                         // S0 at 256, S1 at 384
+
+template <int QT>
+__global__ void __launch_bounds__(kGuThreads, 1)
+tc_gateup_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kGuStages * kGuStageBytes);
+  uint64_t* full_b = full_a + kGuStages;
+  uint64_t* empty = full_b + kGuStages;
+  uint64_t* pfull = empty + kGuStages;    // [2] partial written
+  uint64_t* pempty = pfull + 2;           // [2] partial added to the registers
+  uint64_t* sfull = pempty + 2;           // [2] corrections of a tile written
+  uint64_t* sempty = sfull + 2;           // [2] corrections read
+  uint64_t* drain = sempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();       // the tile plan and activation planes
+  pdl_trigger();
+  const int n_tiles = *args.n_mtiles * args.n_tiles_n;
+  if ((int)blockIdx.x >= n_tiles) return;
+  const int my_tiles = (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1;
+  const int ksteps = args.K / kTcK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGuStages; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_b[s], kGuProducers);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], kGuPromoters);
+      mbar_init(&sfull[b], 1);
+      mbar_init(&sempty[b], kGuPromoters);
+    }
+    mbar_init(drain, 1);
+    *flag = 0;
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
+  }
+  const uint32_t tmem = tc_alloc_all(tmem_slot, warp);
 
   if (warp == 0) {
-    if (lane == 0) {
-      // activation producer: hi and lo planes of each stage's 128 x 64 tile;
-      // the L2 prefetch cursor runs kTcL2Ahead stages ahead of the loads
-      if (MODE == 1) pdl_wait();
-      int pf = 0, pf_i = 0, pf_k = 0;
-      int pf_row = tc_tile(args, blockIdx.x).row0;
-      auto l2_step = [&]() {
-        tma_prefetch_2d(&amap, pf_k * kTcK, pf_row);
-        tma_prefetch_2d(&amap, pf_k * kTcK, args.P + pf_row);
-        ++pf;
-        if (++pf_k == ksteps) {
-          pf_k = 0;
-          if (++pf_i < my_tiles) pf_row = tc_tile(args, blockIdx.x + pf_i * gridDim.x).row0;
-        }
-      };
-      while (pf < total && pf < kTcL2Ahead) l2_step();
-      int it = 0;
-      bool ok = true;
-      for (int i = 0; i < my_tiles && ok; ++i) {
-        const int row0 = tc_tile(args, blockIdx.x + i * gridDim.x).row0;
-        for (int kk = 0; kk < ksteps; ++kk) {
-          const int s = it % kTcStages, round = it / kTcStages;
-          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1)) {
-            *flag = 1;
-            set_status(args.status, MOE_STATUS_TIMEOUT);
-            ok = false;
-            break;
-          }
-          if (*flag) {
-            ok = false;
-            break;
-          }
-          if (pf < total) l2_step();
-          uint8_t* st = stage_base + s * kStageBytes;
-          mbar_expect_tx(&full_a[s], 2 * kTileHalf);
-          tma_load_2d(st, &amap, kk * kTcK, row0, &full_a[s]);
-          tma_load_2d(st + kTileHalf, &amap, kk * kTcK, args.P + row0, &full_a[s]);
-          ++it;
-        }
-      }
-      // the copies this thread issued land before the CTA exits (bounded)
-      for (int s = 0; s < kTcStages; ++s)
-        if (it > s) mbar_wait(&full_a[s], ((it - 1 - s) / kTcStages) & 1);
-    }
+    if (lane == 0)
+      tc_tma_role<0, kGuStages, kGuStageBytes>(&amap, args, my_tiles, ksteps, stage_base, full_a,
+                                               empty, flag);
   } else if (warp == 1) {
     if (lane == 0) {
-      // MMA issuer: tile i accumulates into buffer i & 1 once the epilogue has
-      // read that buffer's previous tile
-      const uint32_t idesc = tc_idesc(kTcM, kTcN);
-      // descriptor of stage 0's A-hi tile; every other operand tile of every
-      // stage differs from it only in the start-address field (addr >> 4 < 2^14)
+      const uint32_t idesc = tc_idesc(kTcM, kGuN);
       const uint64_t d0 = sw128_desc(stage_base);
       const uint32_t d0_lo = (uint32_t)d0, d_hi = (uint32_t)(d0 >> 32);
-      constexpr uint32_t kHalf16 = kTileHalf >> 4, kStage16 = kStageBytes >> 4;
-      int s = 0;
+      constexpr uint32_t kA16 = kATile >> 4, kB16 = kGuBTile >> 4, kStage16 = kGuStageBytes >> 4;
+      int s = 0, pc = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int i = 0; i < my_tiles && ok; ++i) {
         const int b = i & 1, use = i >> 1;
-        if (use > 0 && !mbar_wait(&tempty[b], (use - 1) & 1)) {
-          *flag = 1;
-          set_status(args.status, MOE_STATUS_TIMEOUT);
+        if (use > 0 && !mbar_wait(&sempty[b], (use - 1) & 1)) {
+          tc_fail(flag, args.status);
           ok = false;
         }
-        // the epilogue's tensor-memory reads of buffer b precede these MMAs
+        const uint32_t dsmall = tmem + (uint32_t)(kGuSCol + b * kGuN);
+        uint32_t dpart = tmem;
+        int c = 0;
+        for (int kk = 0; kk < ksteps && ok; ++kk) {
+          if (kk % kGuPeriod == 0) {
+            c = pc & 1;
+            const int n = pc >> 1;
+            if (n > 0 && !mbar_wait(&pempty[c], (n - 1) & 1)) {
+              tc_fail(flag, args.status);
+              ok = false;
+              break;
+            }
+            dpart = tmem + (uint32_t)(c * kGuN);
+            // the promoters' reads of this partial (and of S) precede the MMAs
+            tc_fence_after();
+          }
+          if (!mbar_wait(&full_b[s], phase) || !mbar_wait(&full_a[s], phase)) {
+            tc_fail(flag, args.status);
+            ok = false;
+            break;
+          }
+          const uint32_t ahi = d0_lo + (uint32_t)s * kStage16, alo = ahi + kA16;
+          const uint32_t bhi = ahi + 2 * kA16, blo = bhi + kB16;
+          const bool first_p = kk % kGuPeriod == 0;
+#pragma unroll
+          for (int k16 = 0; k16 < kTcK / 16; ++k16) {
+            const uint32_t adv = (uint32_t)((k16 * 32) >> 4);   // +32 bytes per k16
+            tc_mma_lo(dpart, ahi + adv, bhi + adv, d_hi, idesc, (!first_p || k16 > 0) ? 1u : 0u);
+            tc_mma_lo(dsmall, ahi + adv, blo + adv, d_hi, idesc, (kk > 0 || k16 > 0) ? 1u : 0u);
+            tc_mma_lo(dsmall, alo + adv, bhi + adv, d_hi, idesc, 1u);
+          }
+          tc_commit(&empty[s]);   // stage s free once these MMAs complete
+          if (++s == kGuStages) {
+            s = 0;
+            phase ^= 1u;
+          }
+          if (kk % kGuPeriod == kGuPeriod - 1 || kk == ksteps - 1) {
+            tc_commit(&pfull[c]);
+            ++pc;
+          }
+        }
+        if (!ok) tc_commit(&pfull[c]);   // wake the promoters; they see the flag
+        tc_commit(&sfull[b]);
+      }
+      tc_commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else if (warp < kGuProm0) {
+    tc_producer_role<QT, 0, kGuStages, kGuStageBytes, 2 * kATile, kGuBTile>(
+        args, warp - 2, lane, my_tiles, ksteps, stage_base, full_b, empty, flag);
+  } else {
+    // promoters: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (tile rows)
+    // and owns gate columns [32 hh, 32 hh + 32) and the matching up columns
+    const int q = warp & 3, hh = (warp - kGuProm0) >> 2;
+    const int r = 32 * q + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+    const int nper = (ksteps + kGuPeriod - 1) / kGuPeriod;
+    int pc = 0;
+    bool ok = true;
+    for (int i = 0; i < my_tiles && ok; ++i) {
+      const TcTile tt = tc_tile<0>(args, blockIdx.x + i * gridDim.x);
+      const int row = tt.row0 + r;
+      const bool valid = row < args.offsets[tt.e + 1];
+      const float rs = valid ? args.row_scale[row] : 0.f;
+      float acc[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+      // adds 64 columns of tensor memory at `base` (32 gate, 32 up) into acc
+      auto gather = [&](uint32_t base) {
+#pragma unroll
+        for (int part = 0; part < 4; ++part) {
+          const uint32_t col = (part < 2 ? 0u : (uint32_t)kGuFRows) + 32u * hh + 16u * (part & 1);
+          float v[16];
+          tmem_ld16(base + col, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[16 * part + j] = __fadd_rn(acc[16 * part + j], v[j]);
+        }
+      };
+      for (int per = 0; per < nper; ++per) {
+        const int c = pc & 1, n = pc >> 1;
+        if (!warp_mbar_wait(&pfull[c], n & 1, lane)) {
+          if (lane == 0) tc_fail(flag, args.status);
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t dbig = tmem + (uint32_t)(b * kTcBufCols);
-        const uint32_t dsmall = dbig + (uint32_t)kTcN;
+        if (__shfl_sync(0xffffffffu, *flag, 0)) {
+          ok = false;
+          break;
+        }
+        gather(lane_base + (uint32_t)(c * kGuN));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[c]);
+        ++pc;
+      }
+      if (!ok) break;
+      const int b = i & 1, use = i >> 1;
+      if (!warp_mbar_wait(&sfull[b], use & 1, lane)) {
+        if (lane == 0) tc_fail(flag, args.status);
+        break;
+      }
+      tc_fence_after();
+      if (__shfl_sync(0xffffffffu, *flag, 0)) break;
+      gather(lane_base + (uint32_t)(kGuSCol + b * kGuN));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[b]);
+      if (valid) {
+        __half* hi = args.h_planes + (size_t)row * args.F + tt.n0 + 32 * hh;
+        __half* lo = args.h_planes + ((size_t)args.P + row) * args.F + tt.n0 + 32 * hh;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            float hv[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const int col = 8 * c8 + j + k;
+              const float h = silu_f(acc[col] * rs) * (acc[32 + col] * rs);
+              hv[k] = h * kTcHScale;
+              if (!(fabsf(hv[k]) <= 65504.f)) set_status(args.status, MOE_STATUS_ROW_OVERFLOW);
+            }
+            const __half2 hh2 = __floats2half2_rn(hv[0], hv[1]);
+            const float2 hf = __half22float2(hh2);
+            const __half2 ll = __floats2half2_rn(hv[0] - hf.x, hv[1] - hf.y);
+            hw[j / 2] = *reinterpret_cast<const uint32_t*>(&hh2);
+            lw[j / 2] = *reinterpret_cast<const uint32_t*>(&ll);
+          }
+          reinterpret_cast<uint4*>(hi)[c8] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          reinterpret_cast<uint4*>(lo)[c8] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
+    }
+  }
+  tc_dealloc_all(tmem, warp);
+}
+
+// ---------------------------------------------------------------------------
+// down: 128 x 256 tiles (128 x 128 for a last, narrower one), 2 stages of
+// 96 KB, a "big" accumulator for x_hi * w_hi in tensor-memory columns
+// [0, 256) and a "small" one for the corrections in [256, 512), added with
+// round-to-nearest in the epilogue.  Warps: 0 TMA, 1 MMA, 2-17 weight
+// producers (one per 16-row strip), 18-21 epilogue.
+// ---------------------------------------------------------------------------
+template <int QT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kTcStages * kStageBytes);
+  uint64_t* full_b = full_a + kTcStages;
+  uint64_t* empty = full_b + kTcStages;
+  uint64_t* tfull = empty + kTcStages;    // accumulators written
+  uint64_t* tempty = tfull + 1;           // accumulators read out
+  uint64_t* drain = tempty + 1;           // the issuer's last MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Down reads the tile plan at once (complete, because gate/up triggers only
+  // after its own wait) and waits for gate/up's hidden planes only in its
+  // activation producer, so its weight producers start early.
+  pdl_trigger();
+  const int n_tiles = *args.n_mtiles * args.n_tiles_n;
+  if ((int)blockIdx.x >= n_tiles) return;
+  const int my_tiles = (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1;
+  const int ksteps = args.K / kTcK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_b[s], kTcProducers);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 4);
+    mbar_init(drain, 1);
+    *flag = 0;
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&amap) : "memory");
+  }
+  const uint32_t tmem = tc_alloc_all(tmem_slot, warp);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();
+      tc_tma_role<1, kTcStages, kStageBytes>(&amap, args, my_tiles, ksteps, stage_base, full_a,
+                                             empty, flag);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // descriptor of stage 0's A-hi tile; every other operand tile of every
+      // stage differs from it only in the start-address field (addr >> 4 < 2^14)
+      const uint64_t d0 = sw128_desc(stage_base);
+      const uint32_t d0_lo = (uint32_t)d0, d_hi = (uint32_t)(d0 >> 32);
+      constexpr uint32_t kA16 = kATile >> 4, kStage16 = kStageBytes >> 4;
+      const uint32_t dbig = tmem, dsmall = tmem + (uint32_t)kTcSmallCol;
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const uint32_t idesc = tc_idesc(kTcM, tc_tile<1>(args, blockIdx.x + i * gridDim.x).nr);
+        if (i > 0 && !mbar_wait(tempty, (i - 1) & 1)) {
+          tc_fail(flag, args.status);
+          ok = false;
+        }
+        // the epilogue's tensor-memory reads of the previous tile precede these MMAs
+        tc_fence_after();
         for (int kk = 0; kk < ksteps && ok; ++kk) {
           // the weight tile (producer warps) usually completes after the TMA copy;
           // the barriers order the producers' proxy-fenced stores and the TMA
           // bytes before the MMAs' shared-memory reads
           if (!mbar_wait(&full_b[s], phase) || !mbar_wait(&full_a[s], phase)) {
-            *flag = 1;
-            set_status(args.status, MOE_STATUS_TIMEOUT);
+            tc_fail(flag, args.status);
             ok = false;
             break;
           }
-          const uint32_t ahi = d0_lo + (uint32_t)s * kStage16, alo = ahi + kHalf16;
-          const uint32_t bhi = ahi + 2 * kHalf16, blo = ahi + 3 * kHalf16;
+          const uint32_t ahi = d0_lo + (uint32_t)s * kStage16, alo = ahi + kA16;
+          const uint32_t bhi = ahi + 2 * kA16, blo = bhi + (kBTile >> 4);
 #pragma unroll
           for (int k16 = 0; k16 < kTcK / 16; ++k16) {
             const uint32_t adv = (uint32_t)((k16 * 32) >> 4);   // +32 bytes per k16
@@ -533,168 +891,52 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
             phase ^= 1u;
           }
         }
-        tc_commit(&tfull[b]);     // buffer b complete (or abandoned: the flag is set)
+        tc_commit(tfull);         // accumulators complete (or abandoned: the flag is set)
       }
       // every MMA issued here completes before the tensor memory is released
       tc_commit(drain);
       mbar_wait(drain, 0);
     }
   } else if (warp < kTcEpi0) {
-    // weight producers: warps 2s + 2 and 2s + 3 dequantise the two halves of
-    // strip s (16 B-rows) of every stage.  The register cursor loads stage
-    // it + 3 as soon as stage it is stored; the L2 cursor (half 0 only) runs
-    // kTcL2Ahead stages ahead of it.
-    const int strip = (warp - kTcProd0) >> 1;         // 0..7 -> B rows 16*strip
-    const int half = (warp - kTcProd0) & 1;
-    auto strip_of = [&](int i) {
-      return tc_strip_tiles<QT, MODE>(args, tc_tile(args, blockIdx.x + i * gridDim.x), strip,
-                                      ksteps);
-    };
-    int li = 0, lk = 0;
-    const uint8_t* lp = strip_of(0);
-    int qn = 0, qi = 0, qk = 0;
-    const uint8_t* qp = lp;
-    constexpr int kLines = (Tr::kTileBytes + 127) / 128;
-    auto l2_step = [&]() {
-      const uint8_t* t = qp + (size_t)qk * Tr::kTileBytes;
-      if (lane < kLines) prefetch_l2(t + lane * 128);
-      else if (lane == kLines) prefetch_l2(t + Tr::kTileBytes - 1);
-      ++qn;
-      if (++qk == ksteps) {
-        qk = 0;
-        if (++qi < my_tiles) qp = strip_of(qi);
-      }
-    };
-    auto load_next = [&](PackedHalf<QT>& p) {
-      load_packed_half<QT>(p, lp + (size_t)lk * Tr::kTileBytes, lane, half);
-      if (++lk == ksteps) {
-        lk = 0;
-        if (++li < my_tiles) lp = strip_of(li);
-      }
-    };
-    PackedHalf<QT> p[3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-      if (i < total) load_next(p[i]);
-    if (half == 0)
-      while (qn < total && qn < 3 + kTcL2Ahead) l2_step();
-    bool ok = true;
-    for (int it0 = 0; it0 < total && ok; it0 += 3) {
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const int it = it0 + j;
-        if (it < total && ok) {
-          const int s = it % kTcStages, round = it / kTcStages;
-          if (round > 0 && !warp_mbar_wait(&empty[s], (round - 1) & 1, lane)) {
-            if (lane == 0) {
-              *flag = 1;
-              set_status(args.status, MOE_STATUS_TIMEOUT);
-            }
-            ok = false;
-          } else if ((it & 15) == 0 && __shfl_sync(0xffffffffu, *flag, 0)) {
-            ok = false;   // another role gave up
-          } else {
-            uint8_t* st = stage_base + s * kStageBytes;
-            store_packed_half<QT>(p[j], lane, half, st + 2 * kTileHalf, st + 3 * kTileHalf,
-                                  strip * 16);
-            fence_proxy_async_smem();   // generic stores -> visible to the tensor core
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full_b[s]);
-            // the next loads go out after the fence, which would otherwise wait for them
-            if (it + 3 < total) {
-              load_next(p[j]);
-              if (half == 0 && qn < total) l2_step();
-            }
-          }
-        }
-      }
-    }
-  } else if (warp >= kTcEpi0) {
+    tc_producer_role<QT, 1, kTcStages, kStageBytes, 2 * kATile, kBTile>(
+        args, warp - kTcProd0, lane, my_tiles, ksteps, stage_base, full_b, empty, flag);
+  } else {
     // epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (= tile rows)
     const int q = warp & 3;
     const int r = 32 * q + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
     for (int i = 0; i < my_tiles; ++i) {
-      const TcTile tt = tc_tile(args, blockIdx.x + i * gridDim.x);
+      const TcTile tt = tc_tile<1>(args, blockIdx.x + i * gridDim.x);
       const int row = tt.row0 + r;
       const bool valid = row < args.offsets[tt.e + 1];
-      float rs = 0.f;
-      int orow = 0;
-      if (MODE == 0) rs = valid ? args.row_scale[row] : 0.f;
-      else orow = valid ? (args.y_rows ? args.y_rows[row] : row) : 0;
-      const int b = i & 1, use = i >> 1;
-      const bool got = warp_mbar_wait(&tfull[b], use & 1, lane);
+      const int orow = valid ? (args.y_rows ? args.y_rows[row] : row) : 0;
+      const bool got = warp_mbar_wait(tfull, i & 1, lane);
       tc_fence_after();
       if (!got) {
-        if (lane == 0) {
-          *flag = 1;
-          set_status(args.status, MOE_STATUS_TIMEOUT);
-        }
+        if (lane == 0) tc_fail(flag, args.status);
         break;
       }
       if (__shfl_sync(0xffffffffu, *flag, 0)) break;
-      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kTcBufCols);
-      if (MODE == 0) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {           // gate columns [16c, 16c+16), up [64+16c, ..)
-          float g[16], u[16];
-          tmem_ld_pair(taddr + 16 * c, g);
-          tmem_ld_pair(taddr + 64 + 16 * c, u);
-          if (valid) {
-            __half* hi = args.h_planes + (size_t)row * args.F + tt.nt * 64 + 16 * c;
-            __half* lo = args.h_planes + ((size_t)args.P + row) * args.F + tt.nt * 64 + 16 * c;
-            uint32_t hw[8], lw[8];
+      for (int c = 0; c < tt.nr; c += 16) {
+        float v[16];
+        tmem_ld_pair(taddr + c, v);
+        if (valid) {
+          float4* dst = reinterpret_cast<float4*>(args.y + (size_t)orow * args.d + tt.n0 + c);
 #pragma unroll
-            for (int j = 0; j < 16; j += 2) {
-              float hv[2];
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                const float h = silu_f(g[j + k] * rs) * (u[j + k] * rs);
-                hv[k] = h * kTcHScale;
-                if (!(fabsf(hv[k]) <= 65504.f)) set_status(args.status, MOE_STATUS_ROW_OVERFLOW);
-              }
-              const __half2 hh = __floats2half2_rn(hv[0], hv[1]);
-              const float2 hf = __half22float2(hh);
-              const __half2 ll = __floats2half2_rn(hv[0] - hf.x, hv[1] - hf.y);
-              hw[j / 2] = *reinterpret_cast<const uint32_t*>(&hh);
-              lw[j / 2] = *reinterpret_cast<const uint32_t*>(&ll);
-            }
-            reinterpret_cast<uint4*>(hi)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            reinterpret_cast<uint4*>(hi)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-            reinterpret_cast<uint4*>(lo)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-            reinterpret_cast<uint4*>(lo)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
-          float v[16];
-          tmem_ld_pair(taddr + 16 * c, v);
-          if (valid) {
-            float4* dst = reinterpret_cast<float4*>(args.y + (size_t)orow * args.d +
-                                                    tt.nt * kTcN + 16 * c);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_float4(v[4 * j] * (1.f / kTcHScale), v[4 * j + 1] * (1.f / kTcHScale),
-                                   v[4 * j + 2] * (1.f / kTcHScale),
-                                   v[4 * j + 3] * (1.f / kTcHScale));
-          }
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_float4(v[4 * j] * (1.f / kTcHScale), v[4 * j + 1] * (1.f / kTcHScale),
+                                 v[4 * j + 2] * (1.f / kTcHScale),
+                                 v[4 * j + 3] * (1.f / kTcHScale));
         }
       }
-      // buffer b may take tile i + 2 once every epilogue warp has read it
+      // the next tile may overwrite the accumulators once every epilogue warp has read them
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
+      if (lane == 0) mbar_arrive(tempty);
     }
   }
-
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kTcCols)
-                 : "memory");
-  }
+  tc_dealloc_all(tmem, warp);
 }
 
 // ---------------------------------------------------------------------------
@@ -766,7 +1008,7 @@ static TcWs carve_tc(void* ws, int rows, int E, int d, int F) {
 size_t tc_workspace(int rows, int E, int d, int F) { return carve_tc(nullptr, rows, E, d, F).bytes; }
 
 bool tc_supported(int rows, int E, int d, int F) {
-  return rows > 0 && E <= 1024 && d % kTcN == 0 && F % 64 == 0 && d % kTcK == 0;
+  return rows > 0 && E <= 1024 && d % 128 == 0 && F % 64 == 0;
 }
 
 template <int QT>
@@ -780,9 +1022,9 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   int dev = 0;
   MOE_CUDA(cudaGetDevice(&dev));
   if (!((attr_set >> (dev & 63)) & 1ull)) {
-    MOE_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<QT, 0>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
-    MOE_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<QT, 1>,
+    MOE_CUDA(cudaFuncSetAttribute(tc_gateup_kernel<QT>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kGuSmem));
+    MOE_CUDA(cudaFuncSetAttribute(tc_down_kernel<QT>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem));
     attr_set |= 1ull << (dev & 63);
   }
@@ -812,7 +1054,7 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   a1.w1 = w_up;
   a1.mat_bytes = mat_bytes;
   a1.K = d;
-  a1.n_tiles_n = F / 64;
+  a1.n_tiles_n = F / kGuFRows;
   a1.P = rows;
   a1.F = F;
   a1.d = d;
@@ -827,20 +1069,20 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
     // persistent: one CTA per SM at most, each walking its share of the tiles
     const int grid = std::min(max_tiles * a1.n_tiles_n, sms);
-    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 0>, dim3(grid), dim3(kTcThreads), kTcSmem, s, xmap, a1));
+    MOE_CUDA(launch_pdl(tc_gateup_kernel<QT>, dim3(grid), dim3(kGuThreads), kGuSmem, s, xmap, a1));
   }
   MOE_CHECK(check_launch("tc_gemm gate/up"));
   TcArgs a2 = a1;
   a2.w0 = w_down;
   a2.w1 = nullptr;
   a2.K = F;
-  a2.n_tiles_n = d / kTcN;
+  a2.n_tiles_n = (d + kTcNMax - 1) / kTcNMax;
   a2.y = y;
   a2.y_rows = y_rows;
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
     const int grid = std::min(max_tiles * a2.n_tiles_n, sms);
-    MOE_CUDA(launch_pdl(tc_gemm_kernel<QT, 1>, dim3(grid), dim3(kTcThreads), kTcSmem, s, hmap, a2));
+    MOE_CUDA(launch_pdl(tc_down_kernel<QT>, dim3(grid), dim3(kTcThreads), kTcSmem, s, hmap, a2));
   }
   return check_launch("tc_gemm down");
 }
