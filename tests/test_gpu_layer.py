@@ -126,6 +126,19 @@ def test_prefill_layer_sampled_tokens():
                 tokens=sorted(toks))
 
 
+def test_long_reduction_layer_precision():
+    """d_model 4096 / ffn 1536 (the expert-parallel layer's shapes) with 256
+    rows per expert, so the tensor-core path runs with the longest reductions;
+    top-2 keeps each token's output close to a single expert's, where the
+    accumulation error would show."""
+    cfg = synth.MoEConfig("long_k", 4096, 8, 2, 1536, 1024, synth.QTYPE_Q8_0, 0.002)
+    data = synth.make_layer(cfg, 0)
+    out, ids, w = run(build_layer(data), data.x)
+    experts, shared = oracle_parts(data)
+    check_layer(data.x, data.gate_w, None, 2, 0, experts, shared, out, ids, w,
+                tokens=list(range(0, 1024, 32)))
+
+
 def test_shared_expert_layer_sampled_tokens():
     """Stacked-decode layer shape: routed Q4_0 + always-on Q8_0 shared expert."""
     data = synth.make_layer(synth.CONFIGS["stacked"], 0)
