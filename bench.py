@@ -416,7 +416,7 @@ def run_b200(args):
         dn_work = 2.0 * rows * F * d
         achieved = gu_work / (gu_launch_ms / 1e3) / 1e12 if gu_launch_ms else None
         roofline = {
-            "kernel": "tc_gemm gate/up (tcgen05 grouped GEMM + SiLU*up)",
+            "kernel": "tc_gateup_kernel (persistent tcgen05 grouped GEMM + SiLU*up)",
             "bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
             "frac": (achieved / tc_peak) if achieved else None,
             "traffic": ncu_traffic(args.workload, "gateup"),
