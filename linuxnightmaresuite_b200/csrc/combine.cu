@@ -85,6 +85,87 @@ rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ weight, f
     out[(size_t)t * d + i] = __fmul_rn(__fdiv_rn(xr[i], den), weight[i]);
 }
 
+// One CTA per row, for widths whose numpy pairwise tree is perfect: 2^levels
+// equal leaves of leaf_len terms (levels <= 5, leaf_len a multiple of 4).
+// Lane l of warp 0 sums the squares of leaf l in numpy's leaf order (eight
+// running sums, then ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7))); a shuffle tree
+// then adds (left + right) level by level -- the tree's own order -- so the
+// sum is bit-identical to numpy's.  All threads write the scaled row.
+__global__ void __launch_bounds__(256)
+rms_norm_leaf_kernel(const float* __restrict__ x, const float* __restrict__ weight, float eps,
+                     int d, int leaf_len, int levels, float* __restrict__ out) {
+  __shared__ float s_den;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* xr = x + (size_t)t * d;
+  if (warp == 0) {
+    const int L = 1 << levels;
+    float v = 0.f;
+    if (lane < L) {
+      const float4* e4 = reinterpret_cast<const float4*>(xr + lane * leaf_len);
+      if (leaf_len < 8) {
+        for (int i = 0; i < leaf_len; ++i) v = v + __fmul_rn(xr[lane * leaf_len + i], xr[lane * leaf_len + i]);
+      } else {
+        float r[8];
+        {
+          const float4 a = __ldg(e4), b = __ldg(e4 + 1);
+          r[0] = __fmul_rn(a.x, a.x); r[1] = __fmul_rn(a.y, a.y);
+          r[2] = __fmul_rn(a.z, a.z); r[3] = __fmul_rn(a.w, a.w);
+          r[4] = __fmul_rn(b.x, b.x); r[5] = __fmul_rn(b.y, b.y);
+          r[6] = __fmul_rn(b.z, b.z); r[7] = __fmul_rn(b.w, b.w);
+        }
+        const int full = leaf_len - leaf_len % 8;
+        for (int i = 8; i < full; i += 8) {
+          const float4 a = __ldg(e4 + i / 4), b = __ldg(e4 + i / 4 + 1);
+          r[0] = r[0] + __fmul_rn(a.x, a.x); r[1] = r[1] + __fmul_rn(a.y, a.y);
+          r[2] = r[2] + __fmul_rn(a.z, a.z); r[3] = r[3] + __fmul_rn(a.w, a.w);
+          r[4] = r[4] + __fmul_rn(b.x, b.x); r[5] = r[5] + __fmul_rn(b.y, b.y);
+          r[6] = r[6] + __fmul_rn(b.z, b.z); r[7] = r[7] + __fmul_rn(b.w, b.w);
+        }
+        v = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+        for (int i = full; i < leaf_len; ++i) {
+          const float e = xr[lane * leaf_len + i];
+          v = v + __fmul_rn(e, e);
+        }
+      }
+    }
+    for (int off = 1; off < L; off <<= 1) {
+      const float o = __shfl_down_sync(0xffffffffu, v, off);
+      if ((lane & (2 * off - 1)) == 0) v = v + o;
+    }
+    if (lane == 0) {
+      float ms = v / (float)d;
+      ms = ms + eps;
+      s_den = sqrtf(ms);
+    }
+  }
+  __syncthreads();
+  const float den = s_den;
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  const float4* w4 = reinterpret_cast<const float4*>(weight);
+  float4* o4 = reinterpret_cast<float4*>(out + (size_t)t * d);
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
+    const float4 a = __ldg(x4 + i), w = __ldg(w4 + i);
+    o4[i] = make_float4(__fmul_rn(__fdiv_rn(a.x, den), w.x), __fmul_rn(__fdiv_rn(a.y, den), w.y),
+                        __fmul_rn(__fdiv_rn(a.z, den), w.z), __fmul_rn(__fdiv_rn(a.w, den), w.w));
+  }
+}
+
+// leaf length of numpy's pairwise tree over n terms when that tree is perfect
+// with at most 32 leaves (levels set), else 0
+static int pairwise_perfect_leaf(int n, int& levels) {
+  levels = 0;
+  int len = n;
+  while (len > 128) {
+    int n2 = len / 2;
+    n2 -= n2 % 8;
+    if (2 * n2 != len) return 0;
+    len = n2;
+    ++levels;
+  }
+  return levels <= 5 ? len : 0;
+}
+
 int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
                    const float* residual, int T, int k, int d, float* out, cudaStream_t s) {
   if (T == 0) return MOE_OK;
@@ -117,6 +198,15 @@ int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, f
   MOE_REQUIRE(T >= 0 && d > 0, MOE_ERR_INVALID, "bad shape");
   if (T == 0) return MOE_OK;
   MOE_REQUIRE(x && weight && out, MOE_ERR_INVALID, "null pointer");
+  int levels = 0;
+  const int leaf = moe::pairwise_perfect_leaf(d, levels);
+  if (leaf > 0 && leaf % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)weight & 15) == 0 &&
+      ((uintptr_t)out & 15) == 0) {
+    ::moe::ProfScope _prof(MOE_K_RMS_NORM, reinterpret_cast<cudaStream_t>(stream));
+    moe::rms_norm_leaf_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        x, weight, eps, d, leaf, levels, out);
+    return moe::check_launch("rms_norm");
+  }
   // squares + one float per pairwise leaf (every leaf holds more than 32 terms)
   size_t smem = ((size_t)d + d / 32 + 2) * sizeof(float);
   MOE_REQUIRE(smem <= 200 * 1024, MOE_ERR_UNSUPPORTED, "d=%d too large", d);

@@ -217,6 +217,21 @@ def test_combine_and_rms_norm():
     np.testing.assert_allclose(got, exp, rtol=2e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("d", [100, 128, 1000, 2816, 4096, 8192])
+def test_rms_norm_widths(d):
+    """Warp-per-row path (perfect pairwise trees: 128, 2816, 4096) and the
+    CTA path (100, 1000, 8192), odd row counts."""
+    rng = np.random.default_rng(d)
+    T = 37
+    x = (rng.standard_normal((T, d)) * 3).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    got = K.rms_norm(cuda(x), cuda(nw)).cpu().numpy()
+    exp = np.stack([orc.rms_norm(x[t], nw) for t in range(T)])
+    np.testing.assert_allclose(got, exp, rtol=2e-6, atol=1e-6)
+    again = K.rms_norm(cuda(x), cuda(nw)).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+
+
 def test_gather_rows_and_ep_local_order():
     from linuxnightmaresuite_b200 import ep
     rng = np.random.default_rng(21)
