@@ -9,6 +9,10 @@
 // the router matrix straight from global memory (one 128-bit load per lane and
 // row, eight rows in flight per warp) and reduces the per-warp partial logits
 // in warp order.  It also records each token's max |x| over the slice.
+// For 128 tokens or more pass 1 is router_gemm_kernel instead: (d-slice, 64-token
+// tile, 128-expert tile) CTAs, both operands staged in shared memory (double
+// buffered), each thread holding a 4 x 8 register tile of logits; every logit
+// is still one fused multiply-add chain over its slice, in row order.
 // Pass 2 (router_select_kernel, a programmatic dependent launch of pass 1): one
 // warp per token sums the slice partials in slice order, adds the bias, and
 // selects with warp max-reductions on order-preserving integer keys.  Softmax
@@ -31,20 +35,38 @@ constexpr int kMaxK = 32;
 constexpr int kSelMaxThreads = 512;   // pass 2: up to 4 threads per expert
 
 // Grid of pass 1: token tiles of TT tokens and d-slices of `rows` rows (a
-// multiple of 4), about two CTAs per SM.
+// multiple of 4), about two CTAs per SM.  gemm: the tiled kernel (TT = 64,
+// 128-expert tiles, rows a multiple of 32).  max_parts caps nds * T * E.
+constexpr int kRgTT = 64, kRgTE = 128, kRgK = 16, kRgThreads = 256;
+constexpr int kRgMinT = 128;
+
 struct RouterPlan {
   int tt, tiles, nds, rows;
+  bool gemm;
 };
 
-static RouterPlan router_plan(int T, int d) {
+static RouterPlan router_plan(int T, int d, int E,
+                              size_t max_parts = ~(size_t)0) {
   RouterPlan p;
-  p.tt = T >= 16 ? 16 : (T >= 8 ? 8 : (T >= 4 ? 4 : 1));
-  p.tiles = (T + p.tt - 1) / p.tt;
-  const int want = std::max(1, (2 * sm_count() + p.tiles - 1) / p.tiles);
-  int rows = (d + want - 1) / want;
-  rows = std::max(32, (rows + 31) / 32 * 32);
-  p.rows = std::min(rows, (d + 3) / 4 * 4);
-  p.nds = (d + p.rows - 1) / p.rows;
+  p.gemm = T >= kRgMinT && d % 4 == 0;
+  int want;
+  if (p.gemm) {
+    p.tt = kRgTT;
+    p.tiles = (T + kRgTT - 1) / kRgTT;
+    const int ez = (E + kRgTE - 1) / kRgTE;
+    want = std::max(1, std::min(d / 128, (2 * sm_count() + p.tiles * ez - 1) / (p.tiles * ez)));
+  } else {
+    p.tt = T >= 16 ? 16 : (T >= 8 ? 8 : (T >= 4 ? 4 : 1));
+    p.tiles = (T + p.tt - 1) / p.tt;
+    want = std::max(1, (2 * sm_count() + p.tiles - 1) / p.tiles);
+  }
+  for (;; --want) {
+    int rows = (d + want - 1) / want;
+    rows = std::max(32, (rows + 31) / 32 * 32);
+    p.rows = std::min(rows, p.gemm ? (d + 31) / 32 * 32 : (d + 3) / 4 * 4);
+    p.nds = (d + p.rows - 1) / p.rows;
+    if (want <= 1 || (size_t)p.nds * T * E <= max_parts) break;
+  }
   return p;
 }
 
@@ -276,6 +298,112 @@ __device__ __forceinline__ void select_warp(float (&v)[NJ], int E, int k, int mo
 // loads in flight, and the Q range sums are added in range order (a fixed
 // order for a given plan).  Then the bias, the optional row max over the
 // slices' maxima, and the selection by warp 0.
+// Pass 1 for many tokens: logits of 64 tokens x 128 experts over one d-slice.
+// Thread (ty, tx) keeps tokens 4 ty .. 4 ty + 3 and experts 4 tx .. 4 tx + 3,
+// 64 + 4 tx .. 64 + 4 tx + 3 of the tile; chunks of 16 rows are staged
+// k-major in shared memory, the next chunk's loads in flight during the FMAs.
+__global__ void __launch_bounds__(kRgThreads)
+router_gemm_kernel(const float* __restrict__ x, const float* __restrict__ G, int T, int d, int E,
+                   int layout, int rows_per_slice, float* __restrict__ part,
+                   float* __restrict__ pmax) {
+  pdl_trigger();
+  __shared__ __align__(16) float xs[2][kRgK][kRgTT + 8];
+  __shared__ __align__(16) float gs[2][kRgK][kRgTE];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int slice = blockIdx.x, t0 = blockIdx.y * kRgTT, e0 = blockIdx.z * kRgTE;
+  const int r0 = slice * rows_per_slice, r1 = min(d, r0 + rows_per_slice);
+  // x loader: token tid >> 2, four rows at 4 (tid & 3)
+  const int xt = tid >> 2, xk = 4 * (tid & 3);
+  float xm = 0.f;
+  float4 xr, gr[2];
+  auto gload = [&](int i0) {
+    {
+      const int t = t0 + xt, i = i0 + xk;
+      xr = (t < T && i < r1) ? __ldg(reinterpret_cast<const float4*>(x + (size_t)t * d + i))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      xm = fmaxf(xm, fmaxf(fmaxf(fabsf(xr.x), fabsf(xr.y)), fmaxf(fabsf(xr.z), fabsf(xr.w))));
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int idx = tid + kRgThreads * j;
+      if (layout == MOE_ROUTER_D_E) {
+        const int k = idx >> 5, e = e0 + 4 * (idx & 31), i = i0 + k;
+        gr[j] = (i < r1 && e < E) ? __ldg(reinterpret_cast<const float4*>(G + (size_t)i * E + e))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+        const int e = e0 + (idx >> 2), i = i0 + 4 * (idx & 3);
+        gr[j] = (i < r1 && e < E) ? __ldg(reinterpret_cast<const float4*>(G + (size_t)e * d + i))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  auto sstore = [&](int b) {
+    xs[b][xk + 0][xt] = xr.x;
+    xs[b][xk + 1][xt] = xr.y;
+    xs[b][xk + 2][xt] = xr.z;
+    xs[b][xk + 3][xt] = xr.w;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int idx = tid + kRgThreads * j;
+      if (layout == MOE_ROUTER_D_E) {
+        *reinterpret_cast<float4*>(&gs[b][idx >> 5][4 * (idx & 31)]) = gr[j];
+      } else {
+        const int e = idx >> 2, k = 4 * (idx & 3);
+        gs[b][k + 0][e] = gr[j].x;
+        gs[b][k + 1][e] = gr[j].y;
+        gs[b][k + 2][e] = gr[j].z;
+        gs[b][k + 3][e] = gr[j].w;
+      }
+    }
+  };
+  float acc[4][8];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 8; ++v) acc[u][v] = 0.f;
+  gload(r0);
+  sstore(0);
+  __syncthreads();
+  int b = 0;
+  for (int i0 = r0; i0 < r1; i0 += kRgK) {
+    const bool more = i0 + kRgK < r1;
+    if (more) gload(i0 + kRgK);
+#pragma unroll
+    for (int k = 0; k < kRgK; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(&xs[b][k][4 * ty]);
+      const float4 g0 = *reinterpret_cast<const float4*>(&gs[b][k][4 * tx]);
+      const float4 g1 = *reinterpret_cast<const float4*>(&gs[b][k][64 + 4 * tx]);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) acc[u][v] = fmaf(av[u], gv[v], acc[u][v]);
+    }
+    if (more) sstore(b ^ 1);
+    __syncthreads();
+    b ^= 1;
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int t = t0 + 4 * ty + u;
+    if (t >= T) continue;
+    float* dst = part + ((size_t)slice * T + t) * E;
+    const int ea = e0 + 4 * tx, eb = e0 + 64 + 4 * tx;
+    if (ea < E)
+      *reinterpret_cast<float4*>(dst + ea) = make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+    if (eb < E)
+      *reinterpret_cast<float4*>(dst + eb) = make_float4(acc[u][4], acc[u][5], acc[u][6], acc[u][7]);
+  }
+  if (pmax && blockIdx.z == 0) {
+    float m = xm;
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int t = t0 + xt;
+    if ((tid & 3) == 0 && t < T) pmax[(size_t)slice * T + t] = m;
+  }
+}
+
 template <int NJ>
 __global__ void __launch_bounds__(kSelMaxThreads)
 router_select_kernel(const float* __restrict__ part, const float* __restrict__ pmax, int nds,
@@ -337,7 +465,7 @@ router_select_kernel(const float* __restrict__ part, const float* __restrict__ p
 // Workspace of moe_router: the status word, the partial logits and the
 // partial row maxima.
 static size_t router_ws(int T, int d, int E) {
-  const RouterPlan p = router_plan(T, d);
+  const RouterPlan p = router_plan(T, d, E);
   return 256 + align_up(router_part_floats(p, T, E) * sizeof(float), 256) +
          align_up((size_t)p.nds * T * sizeof(float), 256);
 }
@@ -346,8 +474,8 @@ static size_t router_ws(int T, int d, int E) {
 static int launch_router_passes(const float* x, const float* gate_w, const float* bias, int T,
                                 int d, int E, int k, int layout, int mode, int32_t* ids,
                                 float* weights, float* part, float* pmax, float* row_max,
-                                cudaStream_t s) {
-  const RouterPlan p = router_plan(T, d);
+                                cudaStream_t s, size_t max_parts = ~(size_t)0) {
+  const RouterPlan p = router_plan(T, d, E, max_parts);
   const size_t red = (size_t)kRouterWarps * p.tt * 128 * sizeof(float);
   {
     static std::mutex mu;
@@ -365,7 +493,11 @@ static int launch_router_passes(const float* x, const float* gate_w, const float
   }
   const dim3 grid(p.nds, p.tiles);
   float* pm = row_max ? pmax : nullptr;
-  {
+  if (p.gemm) {
+    ::moe::ProfScope _prof(MOE_K_ROUTER, s);
+    const dim3 g3(p.nds, p.tiles, (E + kRgTE - 1) / kRgTE);
+    router_gemm_kernel<<<g3, kRgThreads, 0, s>>>(x, gate_w, T, d, E, layout, p.rows, part, pm);
+  } else {
     ::moe::ProfScope _prof(MOE_K_ROUTER, s);
     switch (p.tt) {
       case 16:
@@ -435,7 +567,7 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
   MOE_REQUIRE(workspace, MOE_ERR_INVALID, "null workspace");
   MOE_REQUIRE(workspace_bytes >= router_ws(T, d, E), MOE_ERR_WORKSPACE,
               "router workspace %zu < %zu", workspace_bytes, router_ws(T, d, E));
-  const RouterPlan p = router_plan(T, d);
+  const RouterPlan p = router_plan(T, d, E);
   uint8_t* base = static_cast<uint8_t*>(workspace) + 256;
   float* part = reinterpret_cast<float*>(base);
   float* pmax = reinterpret_cast<float*>(
@@ -518,7 +650,7 @@ extern "C" int moe_router_noalloc(const float* x, const float* gate_w, const flo
   MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
   if (T == 0) return MOE_OK;
   MOE_CHECK(check_router_args(x, gate_w, T, d, E, k, layout, mode, ids, weights));
-  const RouterPlan p = router_plan(T, d);
+  const RouterPlan p = router_plan(T, d, E, kNoAllocScratchFloats);
   const size_t need = router_part_floats(p, T, E);
   MOE_REQUIRE(need <= kNoAllocScratchFloats, MOE_ERR_WORKSPACE,
               "moe_router_noalloc: T=%d E=%d needs %zu partial logits (%d slices), above the "
@@ -527,5 +659,6 @@ extern "C" int moe_router_noalloc(const float* x, const float* gate_w, const flo
   float* part = nullptr;
   MOE_CHECK(noalloc_scratch(&part));
   return launch_router_passes(x, gate_w, bias, T, d, E, k, layout, mode, ids, weights, part,
-                              nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
+                              nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream),
+                              kNoAllocScratchFloats);
 }

@@ -64,7 +64,8 @@ def test_router_matches_reference_goldens(case, mode):
 
 @pytest.mark.parametrize("layout", [_lib.MOE_ROUTER_D_E, _lib.MOE_ROUTER_E_D])
 @pytest.mark.parametrize("T,d,E,k", [(1, 2816, 128, 8), (64, 2816, 128, 8), (300, 1024, 8, 2),
-                                     (33, 4096, 128, 8), (5, 64, 4, 4), (17, 128, 256, 32)])
+                                     (33, 4096, 128, 8), (5, 64, 4, 4), (17, 128, 256, 32),
+                                     (512, 2816, 128, 8), (200, 4096, 256, 8), (130, 2816, 132, 4)])
 def test_router_shapes_and_layouts(layout, T, d, E, k):
     rng = np.random.default_rng(T * 7 + d)
     x = rng.standard_normal((T, d), dtype=np.float32)
