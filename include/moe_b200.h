@@ -131,8 +131,8 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
  * footprint is required).  Same inputs, outputs and results as moe_router; its
  * scratch is a fixed 4 MiB array inside the library (held on every GPU that
  * loads it), so it rejects with MOE_ERR_WORKSPACE any call needing more than
- * 1,048,576 partial logits (slices x T x E; e.g. T up to 128 tokens at d=2816,
- * E=128).  The first call on a device looks up the array's device address;
+ * 1,048,576 partial logits (slices x T x E; it uses as few slices as fit, so up
+ * to 8192 tokens at E=128).  The first call on a device looks up the array's device address;
  * make it before any stream capture.  Calls share the array: calls that overlap
  * on the GPU race and must be serialised by the caller.  Allocates nothing. */
 int moe_router_noalloc(const float* x, const float* gate_w, const float* bias, int T, int d,

@@ -42,7 +42,7 @@ def test_noalloc_router_matches_workspace_router_twice(mode):
     d, E, k = 2816, 128, 8
     G = torch.from_numpy(rng.standard_normal((d, E), dtype=np.float32) * np.float32(0.02)).cuda()
     bias = torch.from_numpy(rng.standard_normal(E).astype(np.float32) * np.float32(0.1)).cuda()
-    for T in (64, 7):            # second call smaller than the first
+    for T in (300, 64, 7):       # each call smaller than the one before; 300 takes the tiled pass
         x = torch.from_numpy(rng.standard_normal((T, d), dtype=np.float32)).cuda()
         ids_n, w_n = _noalloc(x, G, bias, k, mode)
         ids_r, w_r = K.router(x, G, k, mode, bias)
