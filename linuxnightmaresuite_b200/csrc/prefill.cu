@@ -18,9 +18,11 @@
 //   * the stage ring runs on across tiles; stage reuse is ordered by mbarriers
 //     (TMA transaction counts, producer arrivals, tcgen05.commit), and every
 //     wait is bounded;
-//   * tensor memory holds two accumulator buffers: four epilogue warps read
-//     tile i with tcgen05.ld while the MMAs of tile i + 1 run.  GEMM1 applies
-//     SiLU(gate) * up and writes the hidden hi/lo planes, GEMM2 writes f32 rows.
+//   * gate/up keeps two partial accumulators and two correction accumulators in
+//     tensor memory; eight promoter warps fold the partials into f32 registers
+//     and run the SiLU(gate) * up epilogue into the hidden hi/lo planes while
+//     the MMAs of the next period / tile run.  Down keeps one big and one small
+//     accumulator (all 512 columns) that four epilogue warps read into f32 rows.
 // Rows of a 128-row tile past the expert's range are computed and discarded.
 #include <cuda.h>
 #include <math.h>
@@ -42,7 +44,8 @@ constexpr int kTcStages = 2;
 constexpr int kTcProd0 = 2;
 constexpr int kTcProducers = kTcNMax / 16;
 constexpr int kTcEpi0 = kTcProd0 + kTcProducers;
-constexpr int kTcThreads = (kTcEpi0 + 4) * 32;
+constexpr int kTcEpiWarps = 4;
+constexpr int kTcThreads = (kTcEpi0 + kTcEpiWarps) * 32;
 constexpr int kATile = kTcM * kTcK * 2;               // one 128 x 64 fp16 plane tile: 16 KB
 constexpr int kBTile = kTcNMax * kTcK * 2;            // one 256 x 64 fp16 plane tile: 32 KB
 constexpr int kStageBytes = 2 * kATile + 2 * kBTile;  // A hi, A lo, B hi, B lo: 96 KB
@@ -833,7 +836,7 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
-    mbar_init(tempty, 4);
+    mbar_init(tempty, kTcEpiWarps);
     mbar_init(drain, 1);
     *flag = 0;
     fence_mbar_init();
