@@ -1,5 +1,5 @@
 """GPU parity of the whole MoE layer against the reference goldens and the
-oracle, at the BASELINE tolerance (max-abs <= 1e-2, rel-L2 <= 2e-3)."""
+oracle, at the parity tolerance (max-abs <= 1e-2, rel-L2 <= 2e-3)."""
 import os
 
 import numpy as np
