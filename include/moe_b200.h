@@ -46,7 +46,35 @@ enum {
   MOE_ERR_DEVICE = -5       /* moe_read_status found a device-side error bit */
 };
 
-enum { MOE_Q4_0 = 2, MOE_Q8_0 = 8 };  /* GGML type ids, dequant_fast.py:689-754 */
+/* GGML type ids, dequant_fast.py:689-754.  Q4_0 and Q8_0 run on the packed-tile
+ * GEMV / tensor-core kernels.  MOE_F32 (type 0: f32 matrices as the reference's
+ * ExpertFFN holds them, moe_forward.py:119-133) and the block formats Q5_1,
+ * Q4_K and Q6_K (dequant_fast.py:169-401; the formats gemma4 experts ship in)
+ * run on the raw-block path: the matrices are used as stored, each weight
+ * decoded in registers exactly as the reference decodes it. */
+enum { MOE_F32 = 0, MOE_Q4_0 = 2, MOE_Q5_1 = 7, MOE_Q8_0 = 8, MOE_Q4_K = 12, MOE_Q6_K = 14 };
+
+/* Gated activation of the experts: SwiGLU silu(g) * u (moe_forward.py:129-133)
+ * or gemma4's GeGLU-tanh (qwen35_gpu.py:933-939, nightmare_stream.py:3256-3271). */
+enum { MOE_ACT_SWIGLU = 0, MOE_ACT_GEGLU_TANH = 1 };
+
+/* Expert variant options (zero-initialised = the reference's MoELayer experts).
+ *   act             MOE_ACT_*
+ *   down_qtype      quant type of w_down; 0 with qtype != MOE_F32 means "same
+ *                   as qtype" (gemma4 ships Q4_K gate/up with a Q5_1 down)
+ *   gate_up_stride  bytes from one expert's gate (and up) matrix to the next;
+ *                   0 = one matrix.  For a fused ffn_gate_up_exps stack
+ *                   (E, 2F, d) pass w_gate = the stack, w_up = w_gate + one
+ *                   (F, d) matrix, stride = two matrices
+ *                   (nightmare_stream.py:3361-3441)
+ *   down_scale      (E_local,) f32 per-expert factor on the down projection
+ *                   (ffn_down_exps.scale, nightmare_stream.py:4307-4330), or NULL */
+typedef struct moe_expert_opts {
+  int act;
+  int down_qtype;
+  size_t gate_up_stride;
+  const float* down_scale;
+} moe_expert_opts;
 
 enum { MOE_ROUTE_TOPK_SOFTMAX = 0, MOE_ROUTE_SOFTMAX_TOPK_RENORM = 1 };
 
@@ -63,8 +91,9 @@ int moe_version(void);
 /* Copies the calling thread's last error message (NUL-terminated). */
 int moe_last_error(char* buf, size_t len);
 
-/* Weights per block and bytes per block of a GGML quant type.
- * Replaces dequant_fast.BLOCK_SIZES (dequant_fast.py:723-754) for types 2 and 8. */
+/* Weights per block and bytes per block of a GGML type (F32 is one weight of
+ * 4 bytes).  Replaces dequant_fast.BLOCK_SIZES (dequant_fast.py:723-754) for
+ * the types this library takes. */
 int moe_block_geometry(int qtype, int* elems_per_block, int* bytes_per_block);
 
 /* Reads (and clears) the device status word a workspace carries. Synchronises
@@ -79,16 +108,19 @@ int moe_read_status(const void* workspace, int* status_out, moe_stream_t stream)
 enum {
   MOE_K_ROUTER = 0, MOE_K_ROUTER_SELECT, MOE_K_DISPATCH, MOE_K_PLAN, MOE_K_XPREP,
   MOE_K_GATEUP, MOE_K_DOWN, MOE_K_COMBINE, MOE_K_RMS_NORM, MOE_K_PACK, MOE_K_DEQUANT,
-  MOE_K_AUX, MOE_K_COUNT
+  MOE_K_AUX, MOE_K_EP_SEND, MOE_K_EP_RECV, MOE_K_EP_RETURN, MOE_K_EP_WAIT, MOE_K_COUNT
 };
 int moe_profile_enable(int on);
 int moe_profile_collect(float* ms, int* launches, int n);
 
 /* ---- weights ---------------------------------------------------------------- */
 
-/* Decodes n_elements weights of raw GGUF blocks to f32.  GPU counterpart of
- * dequant_fast.dequantize_q4_0 / dequantize_q8_0 (dequant_fast.py:44-100) and of
- * the dequant_q4_0 / dequant_q8_34 kernels (qwen35_gpu.py:610-648). */
+/* Decodes n_elements weights of raw GGUF blocks (Q4_0, Q8_0, Q5_1, Q4_K, Q6_K)
+ * to f32, bit for bit as the reference.  GPU counterpart of
+ * dequant_fast.dequantize_q4_0 / dequantize_q8_0 / dequantize_q5_1 /
+ * dequantize_q4_k / dequantize_q6_k (dequant_fast.py:44-100, :169-201,
+ * :237-289, :343-378) and of the dequant_q4_0 / dequant_q8_34 kernels
+ * (qwen35_gpu.py:610-648). */
 int moe_dequantize(const uint8_t* raw, float* out, int qtype, int64_t n_elements,
                    moe_stream_t stream);
 
@@ -133,7 +165,8 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
  * loads it), so it rejects with MOE_ERR_WORKSPACE any call needing more than
  * 1,048,576 partial logits (slices x T x E; it uses as few slices as fit, so up
  * to 8192 tokens at E=128).  The first call on a device looks up the array's device address;
- * make it before any stream capture.  Calls share the array: calls that overlap
+ * make it before any stream capture.  That address is kept for the life of the
+ * process: do not call this again on a device after cudaDeviceReset.  Calls share the array: calls that overlap
  * on the GPU race and must be serialised by the caller.  Allocates nothing. */
 int moe_router_noalloc(const float* x, const float* gate_w, const float* bias, int T, int d,
                        int E, int k, int layout, int mode, int32_t* ids, float* weights,
@@ -176,6 +209,18 @@ int moe_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 const int32_t* y_rows, void* workspace, size_t workspace_bytes,
                 moe_stream_t stream);
 
+/* moe_experts with an expert variant (activation, fused gate/up stride,
+ * per-expert down scale, a down matrix of another type).  Q4_0 / Q8_0 on all
+ * three matrices run on packed weights; F32 and the other block formats (and
+ * mixed types) take the matrices as stored.  Replaces the gemma4 expert path
+ * of _moe_ffn_g4_gpu (nightmare_stream.py:4330-4459) and its CPU counterpart
+ * (_load_expert_fast + _expert_act, nightmare_stream.py:3256-3441). */
+int moe_experts_ex(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                   const moe_expert_opts* opts, const int32_t* expert_offsets, int E_local,
+                   int rows, const float* x, const int32_t* x_rows, int x_rows_div, int d, int F,
+                   float* y, const int32_t* y_rows, void* workspace, size_t workspace_bytes,
+                   moe_stream_t stream);
+
 /* ---- combine ----------------------------------------------------------------------- */
 
 /* out[t] = sum_slot weights[t,slot] * y[inv_perm[t*k+slot]]  (+ shared[t]) (+ residual[t]),
@@ -213,6 +258,11 @@ int moe_ep_local_order(const int32_t* recv_counts, int W, int E_local, int max_r
 int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, float* out,
                  moe_stream_t stream);
 
+/* moe_rms_norm with the reference's gemma_style switch (moe_forward.py:34-40):
+ * non-zero gemma_style scales by (1 + weight) instead of weight. */
+int moe_rms_norm_ex(const float* x, const float* weight, float eps, int gemma_style, int T, int d,
+                    float* out, moe_stream_t stream);
+
 /* ---- whole layer ----------------------------------------------------------------------- */
 
 typedef struct moe_layer_weights {
@@ -229,6 +279,9 @@ typedef struct moe_layer_weights {
   int shared_qtype;
   int E, k, d, F, Fs;
   int mode;
+  const moe_expert_opts* opts; /* expert variant, or NULL for the reference's SwiGLU experts;
+                                  the shared expert takes its activation only.  Under
+                                  expert parallelism down_scale holds the rank's experts */
 } moe_layer_weights;
 
 int moe_layer_workspace_bytes(const moe_layer_weights* w, int T, size_t* bytes);
@@ -245,6 +298,21 @@ int moe_layer_workspace_bytes(const moe_layer_weights* w, int T, size_t* bytes);
 int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* out,
                       const float* residual, int32_t* ids_out, float* weights_out,
                       void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* moe_layer_forward whose router reads router_x (T, d) instead of x: gemma4
+ * routes a scaled, unweighted RMS of the attention output while its experts
+ * read a differently normalised vector (nightmare_stream.py:4659-4674).
+ * router_x NULL = x. */
+int moe_layer_forward_ex(const moe_layer_weights* w, const float* x, const float* router_x, int T,
+                         float* out, const float* residual, int32_t* ids_out, float* weights_out,
+                         void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* gemma4's router input (nightmare_stream.py:4662-4667):
+ * out[t] = x[t] / sqrt(mean(x[t]^2) + eps) * f32(1 / sqrt(d)) * scale, each
+ * product rounded to f32 in that order; scale (d,) f32 (ffn_gate_inp.scale) or
+ * NULL. */
+int moe_router_input(const float* x, const float* scale, float eps, int T, int d, float* out,
+                     moe_stream_t stream);
 
 /* ---- expert parallelism over NVLink peer memory ----------------------------------
  * One process per GPU of a node.  Each rank allocates an exchange window
@@ -276,6 +344,25 @@ int moe_ep_workspace_bytes(const moe_layer_weights* w, int W, int T, size_t* byt
 int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* peers, void* window,
                    const float* x, int T, float* out, const float* residual, int epoch,
                    void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* The same step split into its three phases, for a caller that schedules them
+ * itself (no counterpart in the reference):
+ *   MOE_EP_PHASE_SEND     router, dispatch, rows and counts into the owners' windows
+ *   MOE_EP_PHASE_SERVE    wait for every source, experts on the received rows,
+ *                         outputs back into the sources' windows (+ shared expert)
+ *   MOE_EP_PHASE_COMBINE  wait for every owner, weighted combine into out
+ * moe_ep_forward is all three in order.  Phases of one step run in this order
+ * on each rank with the same epoch.  When all W ranks live on ONE device (one
+ * process driving W windows and workspaces), running a phase for every rank
+ * before any rank starts the next phase satisfies each wait from work that
+ * has already completed in stream order, so no kernel waits on another that
+ * is still to be scheduled. */
+enum { MOE_EP_PHASE_SEND = 1, MOE_EP_PHASE_SERVE = 2, MOE_EP_PHASE_COMBINE = 4,
+       MOE_EP_PHASE_ALL = 7 };
+int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* const* peers,
+                          void* window, const float* x, int T, float* out, const float* residual,
+                          int epoch, int phases, void* workspace, size_t workspace_bytes,
+                          moe_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -19,8 +19,14 @@ MOE_ERR_WORKSPACE = -3
 MOE_ERR_CUDA = -4
 MOE_ERR_DEVICE = -5
 
+MOE_F32 = 0
 MOE_Q4_0 = 2
+MOE_Q5_1 = 7
 MOE_Q8_0 = 8
+MOE_Q4_K = 12
+MOE_Q6_K = 14
+MOE_ACT_SWIGLU = 0
+MOE_ACT_GEGLU_TANH = 1
 MOE_ROUTE_TOPK_SOFTMAX = 0
 MOE_ROUTE_SOFTMAX_TOPK_RENORM = 1
 MOE_ROUTER_D_E = 0
@@ -37,6 +43,11 @@ ci64 = ctypes.c_int64
 cf = ctypes.c_float
 
 
+class MoEExpertOpts(ctypes.Structure):
+    """Mirror of ``moe_expert_opts``."""
+    _fields_ = [("act", ci), ("down_qtype", ci), ("gate_up_stride", csz), ("down_scale", vp)]
+
+
 class MoELayerWeights(ctypes.Structure):
     """Mirror of ``moe_layer_weights``."""
     _fields_ = [
@@ -44,6 +55,7 @@ class MoELayerWeights(ctypes.Structure):
         ("s_gate", vp), ("s_up", vp), ("s_down", vp),
         ("router_layout", ci), ("qtype", ci), ("shared_qtype", ci),
         ("E", ci), ("k", ci), ("d", ci), ("F", ci), ("Fs", ci), ("mode", ci),
+        ("opts", ctypes.POINTER(MoEExpertOpts)),
     ]
 
 
@@ -66,8 +78,14 @@ SIGNATURES = {
     "moe_dispatch": [vp, ci, ci, ci, vp, vp, vp, vp, csz, vp],
     "moe_experts_workspace_bytes": [ci, ci, ci, ci, ctypes.POINTER(csz)],
     "moe_experts": [vp, vp, vp, ci, vp, ci, ci, vp, vp, ci, ci, ci, vp, vp, vp, csz, vp],
+    "moe_experts_ex": [vp, vp, vp, ci, ctypes.POINTER(MoEExpertOpts), vp, ci, ci, vp, vp, ci, ci,
+                       ci, vp, vp, vp, csz, vp],
+    "moe_router_input": [vp, vp, cf, ci, ci, vp, vp],
+    "moe_layer_forward_ex": [ctypes.POINTER(MoELayerWeights), vp, vp, ci, vp, vp, vp, vp, vp, csz,
+                             vp],
     "moe_combine": [vp, vp, vp, vp, vp, ci, ci, ci, vp, vp],
     "moe_rms_norm": [vp, vp, cf, ci, ci, vp, vp],
+    "moe_rms_norm_ex": [vp, vp, cf, ci, ci, ci, vp, vp],
     "moe_gather_rows": [vp, vp, ci, ci, ci, vp, vp],
     "moe_ep_local_order": [vp, ci, ci, ci, vp, vp, vp, vp],
     "moe_ipc_alloc": [csz, ctypes.POINTER(ctypes.c_void_p)],
@@ -78,13 +96,20 @@ SIGNATURES = {
     "moe_ep_window_bytes": [ci, ci, ci, ci, ci, ctypes.POINTER(csz)],
     "moe_ep_workspace_bytes": [vp, ci, ci, ctypes.POINTER(csz)],
     "moe_ep_forward": [vp, ci, ci, vp, vp, vp, ci, vp, vp, ci, vp, csz, vp],
+    "moe_ep_forward_phases": [vp, ci, ci, vp, vp, vp, ci, vp, vp, ci, ci, vp, csz, vp],
     "moe_layer_workspace_bytes": [ctypes.POINTER(MoELayerWeights), ci, ctypes.POINTER(csz)],
     "moe_layer_forward": [ctypes.POINTER(MoELayerWeights), vp, ci, vp, vp, vp, vp, vp, csz, vp],
 }
 
 
 KERNEL_NAMES = ["router", "router_select", "dispatch", "plan", "xprep", "gateup", "down",
-                "combine", "rms_norm", "pack", "dequant", "aux"]
+                "combine", "rms_norm", "pack", "dequant", "aux", "ep_send", "ep_recv_plan",
+                "ep_return", "ep_wait"]
+
+MOE_EP_PHASE_SEND = 1
+MOE_EP_PHASE_SERVE = 2
+MOE_EP_PHASE_COMBINE = 4
+MOE_EP_PHASE_ALL = 7
 
 
 def profile_enable(on: bool) -> None:

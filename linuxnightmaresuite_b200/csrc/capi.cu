@@ -5,7 +5,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "moe_common.cuh"
+#include "blockfmt.cuh"
 
 namespace moe {
 
@@ -125,9 +125,9 @@ int moe_last_error(char* buf, size_t len) {
 
 int moe_block_geometry(int qtype, int* elems_per_block, int* bytes_per_block) {
   MOE_REQUIRE(elems_per_block && bytes_per_block, MOE_ERR_INVALID, "null output pointer");
-  MOE_REQUIRE(moe::qtype_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
-  *elems_per_block = 32;
-  *bytes_per_block = moe::block_bytes(qtype);
+  MOE_REQUIRE(moe::blockfmt_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
+  *elems_per_block = moe::blockfmt_elems(qtype);
+  *bytes_per_block = moe::blockfmt_bytes(qtype);
   return MOE_OK;
 }
 

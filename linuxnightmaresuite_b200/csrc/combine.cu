@@ -15,7 +15,10 @@ constexpr int kCombineThreads = 128;
 __global__ void __launch_bounds__(kCombineThreads)
 combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm,
                const float* __restrict__ w, const float* __restrict__ shared,
-               const float* __restrict__ residual, int k, int d, float* __restrict__ out) {
+               const float* residual, int k, int d, float* out) {
+  // out may alias residual (the stacked step keeps its residual stream in
+  // place): each element is read, then written, by the same thread, so those
+  // two pointers are neither restrict nor read through the read-only path
   pdl_wait();   // the expert outputs
   const int t = blockIdx.x;
   __shared__ int rows[32];
@@ -51,19 +54,30 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     if (residual) {
-      float4 v = __ldg(reinterpret_cast<const float4*>(residual + (size_t)t * d) + i);
+      float4 v = reinterpret_cast<const float4*>(residual + (size_t)t * d)[i];
       acc.x = v.x + acc.x; acc.y = v.y + acc.y; acc.z = v.z + acc.z; acc.w = v.w + acc.w;
     }
     reinterpret_cast<float4*>(out + (size_t)t * d)[i] = acc;
   }
 }
 
-// moe_forward.py:34-40: ms = mean(x*x) + eps; x / sqrt(ms) * weight.
-// The sum of squares follows numpy's pairwise order (one thread), the rest is
-// elementwise.
+// moe_forward.py:34-40: ms = mean(x*x) + eps; x / sqrt(ms) * weight, or
+// * (1 + weight) with gemma_style; or gemma4's router input, x / sqrt(ms) * c
+// * scale.  The sum of squares follows numpy's pairwise order, the rest is
+// elementwise, each operation rounded as numpy rounds it.
+enum { kNormWeight = 0, kNormGemma = 1, kNormRouterIn = 2 };
+
+__device__ __forceinline__ float norm_out(float xn, const float* __restrict__ w, int i, int mode,
+                                          float c) {
+  if (mode == kNormWeight) return __fmul_rn(xn, __ldg(w + i));
+  if (mode == kNormGemma) return __fmul_rn(xn, __fadd_rn(1.0f, __ldg(w + i)));
+  const float v = __fmul_rn(xn, c);
+  return w ? __fmul_rn(v, __ldg(w + i)) : v;
+}
+
 __global__ void __launch_bounds__(256)
 rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ weight, float eps, int d,
-                float* __restrict__ out) {
+                int mode, float c, float* __restrict__ out) {
   extern __shared__ float sq[];       // [d] squares, then the pairwise leaves
   __shared__ float s_den;
   const int t = blockIdx.x;
@@ -82,7 +96,7 @@ rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ weight, f
   __syncthreads();
   const float den = s_den;
   for (int i = threadIdx.x; i < d; i += blockDim.x)
-    out[(size_t)t * d + i] = __fmul_rn(__fdiv_rn(xr[i], den), weight[i]);
+    out[(size_t)t * d + i] = norm_out(__fdiv_rn(xr[i], den), weight, i, mode, c);
 }
 
 // One CTA per row, for widths whose numpy pairwise tree is perfect: 2^levels
@@ -93,7 +107,8 @@ rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ weight, f
 // sum is bit-identical to numpy's.  All threads write the scaled row.
 __global__ void __launch_bounds__(256)
 rms_norm_leaf_kernel(const float* __restrict__ x, const float* __restrict__ weight, float eps,
-                     int d, int leaf_len, int levels, float* __restrict__ out) {
+                     int d, int leaf_len, int levels, int mode, float c,
+                     float* __restrict__ out) {
   __shared__ float s_den;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -142,12 +157,13 @@ rms_norm_leaf_kernel(const float* __restrict__ x, const float* __restrict__ weig
   __syncthreads();
   const float den = s_den;
   const float4* x4 = reinterpret_cast<const float4*>(xr);
-  const float4* w4 = reinterpret_cast<const float4*>(weight);
   float4* o4 = reinterpret_cast<float4*>(out + (size_t)t * d);
   for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
-    const float4 a = __ldg(x4 + i), w = __ldg(w4 + i);
-    o4[i] = make_float4(__fmul_rn(__fdiv_rn(a.x, den), w.x), __fmul_rn(__fdiv_rn(a.y, den), w.y),
-                        __fmul_rn(__fdiv_rn(a.z, den), w.z), __fmul_rn(__fdiv_rn(a.w, den), w.w));
+    const float4 a = __ldg(x4 + i);
+    o4[i] = make_float4(norm_out(__fdiv_rn(a.x, den), weight, 4 * i, mode, c),
+                        norm_out(__fdiv_rn(a.y, den), weight, 4 * i + 1, mode, c),
+                        norm_out(__fdiv_rn(a.z, den), weight, 4 * i + 2, mode, c),
+                        norm_out(__fdiv_rn(a.w, den), weight, 4 * i + 3, mode, c));
   }
 }
 
@@ -178,6 +194,9 @@ int launch_combine(const float* y, const int32_t* inv_perm, const float* w, cons
   return check_launch("combine");
 }
 
+int launch_norm(const float* x, const float* weight, float eps, int mode, float c, int T, int d,
+                float* out, cudaStream_t stream);
+
 }  // namespace moe
 
 extern "C" {
@@ -195,16 +214,39 @@ int moe_combine(const float* y, const int32_t* inv_perm, const float* weights,
 
 int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, float* out,
                  moe_stream_t stream) {
+  return moe_rms_norm_ex(x, weight, eps, 0, T, d, out, stream);
+}
+
+int moe_rms_norm_ex(const float* x, const float* weight, float eps, int gemma_style, int T, int d,
+                    float* out, moe_stream_t stream) {
+  MOE_REQUIRE(weight, MOE_ERR_INVALID, "null weight");
+  return moe::launch_norm(x, weight, eps, gemma_style ? moe::kNormGemma : moe::kNormWeight, 0.f,
+                          T, d, out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moe_router_input(const float* x, const float* scale, float eps, int T, int d, float* out,
+                     moe_stream_t stream) {
+  // nightmare_stream.py:4666: rtmp * np.float32(1.0 / np.sqrt(float(dim)))
+  const float c = (float)(1.0 / sqrt((double)d));
+  return moe::launch_norm(x, scale, eps, moe::kNormRouterIn, c, T, d, out,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace moe {
+
+int launch_norm(const float* x, const float* weight, float eps, int mode, float c, int T, int d,
+                float* out, cudaStream_t stream) {
   MOE_REQUIRE(T >= 0 && d > 0, MOE_ERR_INVALID, "bad shape");
   if (T == 0) return MOE_OK;
-  MOE_REQUIRE(x && weight && out, MOE_ERR_INVALID, "null pointer");
+  MOE_REQUIRE(x && out, MOE_ERR_INVALID, "null pointer");
   int levels = 0;
   const int leaf = moe::pairwise_perfect_leaf(d, levels);
-  if (leaf > 0 && leaf % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)weight & 15) == 0 &&
-      ((uintptr_t)out & 15) == 0) {
-    ::moe::ProfScope _prof(MOE_K_RMS_NORM, reinterpret_cast<cudaStream_t>(stream));
-    moe::rms_norm_leaf_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        x, weight, eps, d, leaf, levels, out);
+  if (leaf > 0 && leaf % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0) {
+    ::moe::ProfScope _prof(MOE_K_RMS_NORM, stream);
+    moe::rms_norm_leaf_kernel<<<T, 256, 0, stream>>>(
+        x, weight, eps, d, leaf, levels, mode, c, out);
     return moe::check_launch("rms_norm");
   }
   // squares + one float per pairwise leaf (every leaf holds more than 32 terms)
@@ -214,11 +256,13 @@ int moe_rms_norm(const float* x, const float* weight, float eps, int T, int d, f
     MOE_CUDA(cudaFuncSetAttribute(moe::rms_norm_kernel,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   {
-    ::moe::ProfScope _prof(MOE_K_RMS_NORM, reinterpret_cast<cudaStream_t>(stream));
-    moe::rms_norm_kernel<<<T, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(x, weight, eps,
-                                                                                   d, out);
+    ::moe::ProfScope _prof(MOE_K_RMS_NORM, stream);
+    moe::rms_norm_kernel<<<T, 256, smem, stream>>>(x, weight, eps,
+                                                                                   d, mode, c,
+                                                                                   out);
   }
   return moe::check_launch("rms_norm");
 }
 
-}  // extern "C"
+}  // namespace moe
+

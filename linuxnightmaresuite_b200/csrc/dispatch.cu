@@ -122,8 +122,10 @@ dispatch_kernel(const int32_t* __restrict__ ids, int P, int E, int32_t* __restri
 
 // ---------------------------------------------------------------------------
 // Chunked dispatch for many pairs (prefill): the same stable order from three
-// launches.  Chunk c holds pairs [c * chunk, (c + 1) * chunk).
-//   count:   per-chunk expert counts (shared-memory integer adds; order-free)
+// launches, still without atomics.  Chunk c holds pairs [c * chunk,
+// (c + 1) * chunk); warp w of its CTA owns the w-th of kChunkWarps equal parts.
+//   count:   per-chunk expert counts: warp-private counters updated by the
+//            leader lane of each __match_any_sync group, summed over the warps
 //   scan:    expert offsets, each chunk's first slot per expert, the plan
 //   scatter: per chunk, warp counts + in-warp ranks as in dispatch_kernel,
 //            placed after the chunk's first slot
@@ -138,21 +140,34 @@ dispatch_count_kernel(const int32_t* __restrict__ ids, int P, int E, int chunk,
                       int* __restrict__ status) {
   pdl_wait();   // the router's ids
   pdl_trigger();
-  extern __shared__ int cnt[];   // [E]
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  extern __shared__ int wcnt[];   // [warps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int i = threadIdx.x; i < kChunkWarps * E; i += blockDim.x) wcnt[i] = 0;
   __syncthreads();
-  const int p0 = blockIdx.x * chunk, p1 = min(P, p0 + chunk);
-  for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
-    const int e = ids[p];
-    if (e < 0 || e >= E) {
-      set_status(status, MOE_STATUS_BAD_EXPERT_ID);
-      inv_perm[p] = -1;
-    } else {
-      atomicAdd(&cnt[e], 1);
+  const int wchunk = chunk / kChunkWarps;   // chunk is a multiple of 32 * warps
+  const int p0 = min(P, blockIdx.x * chunk + warp * wchunk), p1 = min(P, p0 + wchunk);
+  for (int base = p0; base < p1; base += 32) {
+    const int p = base + lane;
+    int e = -1;
+    if (p < p1) {
+      e = ids[p];
+      if (e < 0 || e >= E) {
+        set_status(status, MOE_STATUS_BAD_EXPERT_ID);
+        inv_perm[p] = -1;
+        e = -1;
+      }
     }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (peers & lt_mask) == 0) wcnt[warp * E + e] += __popc(peers);
+    __syncwarp();
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cta_counts[(size_t)blockIdx.x * E + e] = cnt[e];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int n = 0;
+    for (int w = 0; w < kChunkWarps; ++w) n += wcnt[w * E + e];
+    cta_counts[(size_t)blockIdx.x * E + e] = n;
+  }
 }
 
 __global__ void __launch_bounds__(kDispThreads)
@@ -263,8 +278,11 @@ static int launch_dispatch_chunked(const int32_t* ids, int P, int E, int32_t* of
     MOE_CUDA(cudaFuncSetAttribute(dispatch_scatter_kernel,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_w));
   ::moe::ProfScope _prof(MOE_K_DISPATCH, s);
-  MOE_CUDA(launch_pdl(dispatch_count_kernel, dim3(C), dim3(kChunkThreads), sizeof(int) * E, s, ids,
-                      P, E, chunk, cta_counts, inv_perm, status));
+  if (smem_w > 48 * 1024)
+    MOE_CUDA(cudaFuncSetAttribute(dispatch_count_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_w));
+  MOE_CUDA(launch_pdl(dispatch_count_kernel, dim3(C), dim3(kChunkThreads), smem_w, s, ids, P, E,
+                      chunk, cta_counts, inv_perm, status));
   MOE_CUDA(launch_pdl(dispatch_scan_kernel, dim3(1), dim3(kDispThreads), 0, s,
                       (const int32_t*)cta_counts, C, E, offsets, cta_base, status, n_active, active,
                       goff, coff, done, max_groups, rpc));

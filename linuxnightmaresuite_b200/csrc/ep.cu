@@ -2,7 +2,7 @@
 // expert order of received rows.
 #include <string.h>
 
-#include "moe_common.cuh"
+#include "internal.cuh"
 
 namespace moe {
 
@@ -316,26 +316,6 @@ __global__ void ep_wait_kernel(EpArgs a, int* __restrict__ status) {
     set_status(status, MOE_STATUS_TIMEOUT);
 }
 
-int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
-                  int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
-                  size_t workspace_bytes, cudaStream_t stream, float* row_max);
-int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
-                            int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
-                            int* active, int* goff, int* coff, int* done, int max_groups,
-                            int rpc, int32_t* scratch, cudaStream_t s);
-int experts_rows_per_chunk(int qtype, int rows, int E, int d, int F);
-size_t dispatch_scratch_bytes(int P, int E);
-int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes);
-void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
-                         int** goff, int** coff, int** done, int* mg);
-int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
-                const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
-                int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
-                size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
-                bool planned, int rows_hint);
-int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
-                   const float* residual, int T, int k, int d, float* out, cudaStream_t s);
-
 __global__ void ep_fill_two(int32_t* off, int n) {
   if (threadIdx.x == 0) {
     off[0] = 0;
@@ -449,14 +429,17 @@ int moe_ep_workspace_bytes(const moe_layer_weights* w, int W, int T, size_t* byt
   return MOE_OK;
 }
 
-int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* peers, void* window,
-                   const float* x, int T, float* out, const float* residual, int epoch,
-                   void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* const* peers,
+                          void* window, const float* x, int T, float* out, const float* residual,
+                          int epoch, int phases, void* workspace, size_t workspace_bytes,
+                          moe_stream_t stream) {
   using namespace moe;
   MOE_REQUIRE(w && peers && window && x && out && workspace, MOE_ERR_INVALID, "null pointer");
   MOE_REQUIRE(W > 0 && W <= kEpMaxW && rank >= 0 && rank < W && w->E % W == 0,
               MOE_ERR_INVALID, "bad expert-parallel shape (W=%d rank=%d E=%d)", W, rank, w->E);
   MOE_REQUIRE(T > 0 && epoch > 0, MOE_ERR_INVALID, "T and epoch must be positive");
+  MOE_REQUIRE(phases > 0 && (phases & ~MOE_EP_PHASE_ALL) == 0, MOE_ERR_INVALID,
+              "phases must be a non-empty mask of MOE_EP_PHASE_* bits");
   MOE_REQUIRE(!w->s_gate || (w->s_up && w->s_down && w->Fs > 0), MOE_ERR_INVALID,
               "incomplete shared expert");
   const int El = w->E / W;
@@ -477,54 +460,71 @@ int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* pee
   a.cap = P;
   a.d = w->d;
   a.epoch = epoch;
-  MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
-                          L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr));
-  MOE_CHECK(launch_dispatch_planned(L.ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
-                                    nullptr, nullptr, nullptr, nullptr, nullptr, 0, 1,
-                                    L.disp_scratch, s));
-  {
-    ::moe::ProfScope _prof(MOE_K_AUX, s);
-    ep_send_kernel<<<(P + 7) / 8, 256, 0, s>>>(x, L.perm, w->k, L.offsets, P, a);
-  }
-  MOE_CHECK(check_launch("ep_send"));
-  const int R = P * W;
-  int *n_active, *active, *goff, *coff, *done, mg;
-  experts_plan_arrays(L.exp_ws, R, El, w->d, w->F, &n_active, &active, &goff, &coff, &done, &mg);
-  const int rpc = experts_rows_per_chunk(w->qtype, R, El, w->d, w->F);
-  {
-    ::moe::ProfScope _prof(MOE_K_AUX, s);
-    ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, coff,
-                                           done, mg, rpc, L.status);
-  }
-  MOE_CHECK(check_launch("ep_recv_plan"));
-  float* recv = reinterpret_cast<float*>(a.win + a.off.recv_x);
-  MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.loff, El, R, recv, L.row_map,
-                        1, w->d, w->F, recv, L.row_map, L.exp_ws, L.exp_bytes, s, L.status,
-                        nullptr, true, P));
-  {
-    ::moe::ProfScope _prof(MOE_K_AUX, s);
-    ep_return_kernel<<<dim3((P + 7) / 8, W), 256, 0, s>>>(a);
-  }
-  MOE_CHECK(check_launch("ep_return"));
-  if (w->s_gate) {
-    // the shared expert runs on this rank's own tokens (replicated weights)
-    // while the other ranks finish their experts and returns
+  if (phases & MOE_EP_PHASE_SEND) {
+    MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout,
+                            w->mode, L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr));
+    MOE_CHECK(launch_dispatch_planned(L.ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, 0, 1,
+                                      L.disp_scratch, s));
     {
-      ::moe::ProfScope _prof(MOE_K_AUX, s);
-      ep_fill_two<<<1, 32, 0, s>>>(L.s_off, T);
+      ::moe::ProfScope _prof(MOE_K_EP_SEND, s);
+      ep_send_kernel<<<(P + 7) / 8, 256, 0, s>>>(x, L.perm, w->k, L.offsets, P, a);
     }
-    MOE_CHECK(check_launch("ep_fill_two"));
-    MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
-                          nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.s_ws, L.s_bytes, s, L.status,
-                          nullptr, false, T));
+    MOE_CHECK(check_launch("ep_send"));
   }
-  {
-    ::moe::ProfScope _prof(MOE_K_AUX, s);
-    ep_wait_kernel<<<1, 32, 0, s>>>(a, L.status);
+  if (phases & MOE_EP_PHASE_SERVE) {
+    const int R = P * W;
+    int *n_active, *active, *goff, *coff, *done, mg;
+    experts_plan_arrays(L.exp_ws, R, El, w->d, w->F, &n_active, &active, &goff, &coff, &done,
+                        &mg);
+    const int rpc = experts_rows_per_chunk(w->qtype, experts_down_qtype(w->qtype, w->opts), R,
+                                           El, w->d, w->F);
+    {
+      ::moe::ProfScope _prof(MOE_K_EP_RECV, s);
+      ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, coff,
+                                             done, mg, rpc, L.status);
+    }
+    MOE_CHECK(check_launch("ep_recv_plan"));
+    float* recv = reinterpret_cast<float*>(a.win + a.off.recv_x);
+    MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.loff, El, R, recv,
+                          L.row_map, 1, w->d, w->F, recv, L.row_map, L.exp_ws, L.exp_bytes, s,
+                          L.status, nullptr, true, P, w->opts));
+    {
+      ::moe::ProfScope _prof(MOE_K_EP_RETURN, s);
+      ep_return_kernel<<<dim3((P + 7) / 8, W), 256, 0, s>>>(a);
+    }
+    MOE_CHECK(check_launch("ep_return"));
+    if (w->s_gate) {
+      // the shared expert runs on this rank's own tokens (replicated weights)
+      // while the other ranks finish their experts and returns
+      {
+        ::moe::ProfScope _prof(MOE_K_AUX, s);
+        ep_fill_two<<<1, 32, 0, s>>>(L.s_off, T);
+      }
+      MOE_CHECK(check_launch("ep_fill_two"));
+      const moe_expert_opts so = shared_expert_opts(w->opts);
+      MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
+                            nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.s_ws, L.s_bytes, s,
+                            L.status, nullptr, false, T, &so));
+    }
   }
-  MOE_CHECK(check_launch("ep_wait"));
-  return launch_combine(reinterpret_cast<const float*>(a.win + a.off.ret_y), L.inv, L.wts,
-                        L.s_y, residual, T, w->k, w->d, out, s);
+  if (phases & MOE_EP_PHASE_COMBINE) {
+    {
+      ::moe::ProfScope _prof(MOE_K_EP_WAIT, s);
+      ep_wait_kernel<<<1, 32, 0, s>>>(a, L.status);
+    }
+    MOE_CHECK(check_launch("ep_wait"));
+    MOE_CHECK(launch_combine(reinterpret_cast<const float*>(a.win + a.off.ret_y), L.inv, L.wts,
+                             L.s_y, residual, T, w->k, w->d, out, s));
+  }
+  return MOE_OK;
+}
+
+int moe_ep_forward(const moe_layer_weights* w, int W, int rank, void* const* peers, void* window,
+                   const float* x, int T, float* out, const float* residual, int epoch,
+                   void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  return moe_ep_forward_phases(w, W, rank, peers, window, x, T, out, residual, epoch,
+                               MOE_EP_PHASE_ALL, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

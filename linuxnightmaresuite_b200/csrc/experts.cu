@@ -32,6 +32,9 @@
 
 namespace moe {
 
+int raw_rows_per_chunk(int d, int F);   // experts_raw.cu
+bool experts_packed(int qtype, int dn_qtype);
+
 constexpr int kMaxCG = 4;                 // column groups (4 rows each) per pass
 constexpr float kHScale = 1.0f / 256.0f;  // hidden activations are stored / 256
 constexpr float kSubUnit = 16777216.0f;   // 2^24: one fp16 subnormal step
@@ -239,17 +242,6 @@ __device__ __forceinline__ bool wait_count(const int* p, int target) {
   return false;
 }
 
-// Work item `item` (a chunk of rpc rows of one expert) -> expert e and the
-// chunk's first row c0 inside the expert; false past the last item.
-__device__ __forceinline__ bool chunk_of(int item, const int* __restrict__ citem, int rpc,
-                                         int& e, int& c0) {
-  const int v = citem[item];
-  if (v < 0) return false;
-  e = v >> 16;
-  c0 = (v & 0xFFFF) * rpc;
-  return true;
-}
-
 // Per-CTA state of a gate/up work item.
 struct GuCtx {
   const uint8_t* gbase;   // this warp's strip of W_gate (tile 0)
@@ -261,7 +253,7 @@ struct GuCtx {
   uint8_t* hfrag;
   int* status;
   uint64_t pol;
-  int nst, jb, ntile, nbx, nbF, ks, kp, s, row0, n, G0, lane;
+  int nst, jb, ntile, nbx, nbF, ks, kp, s, row0, n, G0, lane, act;
   bool strip_ok;
 };
 
@@ -427,7 +419,7 @@ __device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, int c
           for (int rr = 0; rr < 2; ++rr) {
             const float gacc = ci ? accg[cg][rr].y : accg[cg][rr].x;
             const float uacc = ci ? accu[cg][rr].y : accu[cg][rr].x;
-            const float h = silu_f(gacc * rs) * (uacc * rs);
+            const float h = expert_act(c.act, gacc * rs) * (uacc * rs);
             const float hsc = h * kHScale;
             if (!(fabsf(hsc) <= 65504.f)) set_status(c.status, MOE_STATUS_ROW_OVERFLOW);
             const __half hh = __float2half_rn(hsc);
@@ -564,8 +556,8 @@ __device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rma
 // ---------------------------------------------------------------------------
 template <int QT>
 __global__ void __launch_bounds__(kGuWarps * 32, 1)
-gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t mat_bytes,
-              int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
+gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t gu_stride,
+              int act, int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
               const int* __restrict__ active, const int* __restrict__ goff,
               const int* __restrict__ citem, const float* __restrict__ x,
               const int32_t* __restrict__ x_rows, int x_div, const float* __restrict__ x_row_max,
@@ -613,8 +605,9 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   c.lane = lane;
   c.hfrag = hfrag;
   c.status = status;
-  c.gbase = wg + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
-  c.ubase = wu + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
+  c.gbase = wg + (size_t)e * gu_stride + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
+  c.ubase = wu + (size_t)e * gu_stride + (size_t)(c.strip_ok ? c.s : 0) * JT * TB;
+  c.act = act;
   c.pol = evict_first_policy();
   if (lane == 0) {
     for (int i = 0; i < nst; ++i) mbar_init(&c.bars[i], 1);
@@ -648,6 +641,7 @@ struct DnCtx {
   const int32_t* y_rows;
   int* status;
   uint64_t pol;
+  float scale;   // per-expert factor on the down projection (1 if none)
   int nst, JT, nbF, s, d, row0, n, lane;
   bool strip_ok;
 };
@@ -752,8 +746,8 @@ __device__ __forceinline__ bool dn_chunk(const DnCtx& c, uint32_t& parity, int c
         const int r = c.row0 + tok;
         const int orow = c.y_rows ? c.y_rows[r] : r;
         float* yr = c.y + (size_t)orow * c.d + c.s * 16 + g;
-        yr[0] = (ci ? acc[cg][0].y : acc[cg][0].x) * (1.0f / kHScale);
-        yr[8] = (ci ? acc[cg][1].y : acc[cg][1].x) * (1.0f / kHScale);
+        yr[0] = (ci ? acc[cg][0].y : acc[cg][0].x) * (1.0f / kHScale) * c.scale;
+        yr[8] = (ci ? acc[cg][1].y : acc[cg][1].x) * (1.0f / kHScale) * c.scale;
       }
     }
   }
@@ -766,8 +760,8 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
             const int* __restrict__ active, const int* __restrict__ goff,
             const int* __restrict__ citem, const uint8_t* __restrict__ hfrag, float* __restrict__ y,
-            const int32_t* __restrict__ y_rows, int cgp, int nst, const int* __restrict__ done,
-            int gu_cpe, int* __restrict__ status) {
+            const int32_t* __restrict__ y_rows, const float* __restrict__ down_scale, int cgp,
+            int nst, const int* __restrict__ done, int gu_cpe, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SMAX = Ring<QT>::kDnStages;
@@ -799,6 +793,7 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   c.y_rows = y_rows;
   c.status = status;
   c.base = wd + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * c.JT * TB;
+  c.scale = down_scale ? down_scale[e] : 1.0f;
   c.pol = evict_first_policy();
   if (lane == 0) {
     for (int i = 0; i < nst; ++i) mbar_init(&c.bars[i], 1);
@@ -864,7 +859,7 @@ int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_
                    const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                    int x_div, const float* x_row_max, int d, int F, float* y,
                    const int32_t* y_rows, void* ws, size_t ws_bytes, int* status,
-                   cudaStream_t s);
+                   const moe_expert_opts* opts, cudaStream_t s);
 
 // Rows per active expert from which the tcgen05 GEMM path is used.
 #ifndef MOE_TC_MIN_MEAN_ROWS
@@ -955,7 +950,7 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
                           const int32_t* offsets, int E, int rows, const float* x,
                           const int32_t* x_rows, int x_div, const float* x_row_max, bool planned,
                           int d, int F, float* y, const int32_t* y_rows, const ExpertsWs& w,
-                          cudaStream_t s) {
+                          const moe_expert_opts* opts, cudaStream_t s) {
   using Tr = QTraits<QT>;
   ExpertsPlan p;
   MOE_REQUIRE(plan_experts<QT>(rows, E, d, F, p), MOE_ERR_UNSUPPORTED,
@@ -978,10 +973,13 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   }
   MOE_CHECK(check_launch("plan"));
   const size_t mat_bytes = (size_t)F * (d / 32) * Tr::kBlockBytes;
+  const size_t gu_stride = (opts && opts->gate_up_stride) ? opts->gate_up_stride : mat_bytes;
+  const int act = opts ? opts->act : MOE_ACT_SWIGLU;
+  const float* down_scale = opts ? opts->down_scale : nullptr;
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
     MOE_CUDA(launch_pdl(gateup_kernel<QT>, dim3(p.grid_gu), dim3(kGuWarps * 32), p.smem_gu, s,
-                        w_gate, w_up, mat_bytes, d, F, offsets, (const int*)w.n_active,
+                        w_gate, w_up, gu_stride, act, d, F, offsets, (const int*)w.n_active,
                         (const int*)w.active, (const int*)w.goff, (const int*)w.coff, x, x_rows,
                         x_div, x_row_max, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.done, w.status));
   }
@@ -991,7 +989,7 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
     MOE_CUDA(launch_pdl(down_kernel<QT>, dim3(p.grid_dn), dim3(kDnWarps * 32), p.smem_dn, s,
                         w_down, mat_bytes, d, F, offsets, (const int*)w.n_active,
                         (const int*)w.active, (const int*)w.goff, (const int*)w.coff,
-                        (const uint8_t*)w.hfrag, y, y_rows, p.cgp_dn, p.nst_dn,
+                        (const uint8_t*)w.hfrag, y, y_rows, down_scale, p.cgp_dn, p.nst_dn,
                         (const int*)w.done, p.cpe_gu, w.status));
   }
   return check_launch("down");
@@ -999,7 +997,8 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
 
 // Plan arrays inside an experts workspace, for a dispatch that writes them.
 // Rows per work item (chunk) of the GEMV kernels for a call's shape.
-int experts_rows_per_chunk(int qtype, int rows, int E, int d, int F) {
+int experts_rows_per_chunk(int qtype, int dn_qtype, int rows, int E, int d, int F) {
+  if (!experts_packed(qtype, dn_qtype)) return raw_rows_per_chunk(d, F);
   ExpertsPlan p;
   const bool ok = qtype == MOE_Q4_0 ? plan_experts<MOE_Q4_0>(rows, E, d, F, p)
                                     : plan_experts<MOE_Q8_0>(rows, E, d, F, p);
@@ -1017,12 +1016,60 @@ void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active
   *mg = max_groups(rows, E);
 }
 
+void experts_hidden(void* ws, int rows, int E, int d, int F, uint8_t** hidden, int** status) {
+  ExpertsWs w = carve_experts(ws, rows, E, d, F);
+  *hidden = w.hfrag;
+  *status = w.status;
+}
+
+// The expert plan (work items of rpc rows) from expert_offsets, in ws.
+int launch_expert_plan(const int32_t* offsets, int E, int rows, int rpc, void* ws, int d, int F,
+                       cudaStream_t s) {
+  ExpertsWs w = carve_experts(ws, rows, E, d, F);
+  {
+    ::moe::ProfScope _prof(MOE_K_PLAN, s);
+    plan_kernel<<<1, kPlanThreads, 0, s>>>(offsets, E, rows, max_groups(rows, E), rpc, w.n_active,
+                                           w.active, w.goff, w.coff, w.done, w.status);
+  }
+  return check_launch("plan");
+}
+
+int raw_rows_per_chunk(int d, int F);
+int run_experts_raw(const uint8_t* wg, const uint8_t* wu, const uint8_t* wd, int gu_fmt,
+                    int dn_fmt, const moe_expert_opts* opts, const int32_t* offsets, int E,
+                    int rows, const float* x, const int32_t* x_rows, int x_div, int d, int F,
+                    float* y, const int32_t* y_rows, void* ws, bool planned, cudaStream_t s);
+
+// quant type of the down matrices under opts
+int experts_down_qtype(int qtype, const moe_expert_opts* opts) {
+  return (opts && opts->down_qtype != 0) ? opts->down_qtype : qtype;
+}
+
+// Whether a layer's weights run on the packed-tile kernels (Q4_0 / Q8_0 for
+// all three matrices) rather than the raw-block path.
+bool experts_packed(int qtype, int dn_qtype) {
+  return qtype_ok(qtype) && dn_qtype == qtype;
+}
+
 int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
                 const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
                 size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
-                bool planned, int rows_hint) {
-  MOE_REQUIRE(qtype_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
+                bool planned, int rows_hint, const moe_expert_opts* opts) {
+  const int dn_qtype = experts_down_qtype(qtype, opts);
+  if (!experts_packed(qtype, dn_qtype)) {
+    MOE_REQUIRE(E > 0 && E <= kPlanThreads, MOE_ERR_UNSUPPORTED, "local expert count %d", E);
+    MOE_REQUIRE(rows >= 0, MOE_ERR_INVALID, "rows must be >= 0");
+    if (rows == 0) return MOE_OK;
+    MOE_REQUIRE(w_gate && w_up && w_down && offsets && x && y && ws, MOE_ERR_INVALID,
+                "null pointer");
+    MOE_REQUIRE(x_div > 0, MOE_ERR_INVALID, "x_rows_div must be positive");
+    const size_t need = carve_experts(nullptr, rows, E, d, F).bytes;
+    MOE_REQUIRE(ws_bytes >= need, MOE_ERR_WORKSPACE, "experts workspace %zu < %zu", ws_bytes,
+                need);
+    return run_experts_raw(w_gate, w_up, w_down, qtype, dn_qtype, opts, offsets, E, rows, x,
+                           x_rows, x_div, d, F, y, y_rows, ws, planned, s);
+  }
   MOE_REQUIRE(E > 0 && E <= kPlanThreads, MOE_ERR_UNSUPPORTED, "local expert count %d", E);
   MOE_REQUIRE(d > 0 && F > 0 && d % 64 == 0 && F % 64 == 0, MOE_ERR_UNSUPPORTED,
               "d=%d and F=%d must be multiples of 64", d, F);
@@ -1035,16 +1082,16 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
               MOE_ERR_INVALID, "weights and activations must be 16-byte aligned");
   if (use_tc(rows_hint > 0 ? rows_hint : rows, E, d, F))
     return run_experts_tc(w_gate, w_up, w_down, qtype, offsets, E, rows, x, x_rows, x_div,
-                          x_row_max, d, F, y, y_rows, ws, ws_bytes, status, s);
+                          x_row_max, d, F, y, y_rows, ws, ws_bytes, status, opts, s);
   ExpertsWs w = carve_experts(ws, rows, E, d, F);
   if (status) w.status = status;
   MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "experts workspace %zu < %zu", ws_bytes,
               w.bytes);
   if (qtype == MOE_Q4_0)
     return launch_experts<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
-                                    x_row_max, planned, d, F, y, y_rows, w, s);
+                                    x_row_max, planned, d, F, y, y_rows, w, opts, s);
   return launch_experts<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
-                                  x_row_max, planned, d, F, y, y_rows, w, s);
+                                  x_row_max, planned, d, F, y, y_rows, w, opts, s);
 }
 
 }  // namespace moe
@@ -1062,9 +1109,21 @@ int moe_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 const int32_t* x_rows, int x_rows_div, int d, int F, float* y,
                 const int32_t* y_rows, void* workspace, size_t workspace_bytes,
                 moe_stream_t stream) {
+  return moe_experts_ex(w_gate, w_up, w_down, qtype, nullptr, expert_offsets, E_local, rows, x,
+                        x_rows, x_rows_div, d, F, y, y_rows, workspace, workspace_bytes, stream);
+}
+
+int moe_experts_ex(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                   const moe_expert_opts* opts, const int32_t* expert_offsets, int E_local,
+                   int rows, const float* x, const int32_t* x_rows, int x_rows_div, int d, int F,
+                   float* y, const int32_t* y_rows, void* workspace, size_t workspace_bytes,
+                   moe_stream_t stream) {
+  MOE_REQUIRE(!opts || opts->act == MOE_ACT_SWIGLU || opts->act == MOE_ACT_GEGLU_TANH,
+              MOE_ERR_INVALID, "unknown activation %d", opts ? opts->act : 0);
   return moe::run_experts(w_gate, w_up, w_down, qtype, expert_offsets, E_local, rows, x, x_rows,
                           x_rows_div, d, F, y, y_rows, workspace, workspace_bytes,
-                          reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, false, 0);
+                          reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, false, 0,
+                          opts);
 }
 
 }  // extern "C"

@@ -1,28 +1,8 @@
 // Whole MoE layer: router -> dispatch -> grouped experts -> combine.
 // MoELayer.forward (moe_forward.py:154-174) for a batch of tokens.
-#include "moe_common.cuh"
+#include "internal.cuh"
 
 namespace moe {
-
-int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
-                const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
-                int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
-                size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
-                bool planned, int rows_hint);
-void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active, int** active,
-                         int** goff, int** coff, int** done, int* mg);
-int experts_rows_per_chunk(int qtype, int rows, int E, int d, int F);
-int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
-                  int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
-                  size_t workspace_bytes, cudaStream_t stream, float* row_max);
-int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,
-                            int32_t* perm_rows, int32_t* inv_perm, int* status, int* n_active,
-                            int* active, int* goff, int* coff, int* done, int max_groups,
-                            int rpc, int32_t* scratch, cudaStream_t s);
-size_t dispatch_scratch_bytes(int P, int E);
-int experts_workspace(int rows, int E, int d, int F, size_t* bytes);
-int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
-                   const float* residual, int T, int k, int d, float* out, cudaStream_t s);
 
 __global__ void fill_two_offsets(int32_t* off, int n) {
   if (threadIdx.x == 0) {
@@ -91,13 +71,22 @@ int moe_layer_workspace_bytes(const moe_layer_weights* w, int T, size_t* bytes) 
 int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* out,
                       const float* residual, int32_t* ids_out, float* weights_out,
                       void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  return moe_layer_forward_ex(w, x, nullptr, T, out, residual, ids_out, weights_out, workspace,
+                              workspace_bytes, stream);
+}
+
+int moe_layer_forward_ex(const moe_layer_weights* w, const float* x, const float* router_x, int T,
+                         float* out, const float* residual, int32_t* ids_out, float* weights_out,
+                         void* workspace, size_t workspace_bytes, moe_stream_t stream) {
   using namespace moe;
   MOE_REQUIRE(w, MOE_ERR_INVALID, "null weights");
   MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
   if (T == 0) return MOE_OK;
   MOE_REQUIRE(x && out && workspace && w->gate_w && w->w_gate && w->w_up && w->w_down,
               MOE_ERR_INVALID, "null pointer");
-  MOE_REQUIRE(x != out, MOE_ERR_INVALID, "out must not alias x");
+  MOE_REQUIRE(x != out && router_x != out, MOE_ERR_INVALID, "out must not alias the inputs");
+  MOE_REQUIRE(!w->opts || w->opts->act == MOE_ACT_SWIGLU || w->opts->act == MOE_ACT_GEGLU_TANH,
+              MOE_ERR_INVALID, "unknown activation %d", w->opts ? w->opts->act : 0);
   MOE_REQUIRE(w->k > 0 && w->k <= w->E, MOE_ERR_INVALID, "top_k %d vs %d experts", w->k, w->E);
   MOE_REQUIRE(!w->s_gate || (w->s_up && w->s_down && w->Fs > 0), MOE_ERR_INVALID,
               "incomplete shared expert");
@@ -108,27 +97,33 @@ int moe_layer_forward(const moe_layer_weights* w, const float* x, int T, float* 
   int32_t* ids = ids_out ? ids_out : L.ids;
   float* wts = weights_out ? weights_out : L.wts;
   const int P = T * w->k;
-  MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout, w->mode,
-                          ids, wts, L.router_ws, L.router_bytes, s, L.row_max));
+  // the router's per-row maxima double as the experts' activation scaling,
+  // so they are only taken from the router when it reads the experts' input
+  MOE_CHECK(launch_router(router_x ? router_x : x, w->gate_w, w->bias, T, w->d, w->E, w->k,
+                          w->router_layout, w->mode, ids, wts, L.router_ws, L.router_bytes, s,
+                          router_x ? nullptr : L.row_max));
+  const float* row_max = router_x ? nullptr : L.row_max;
   int *n_active, *active, *goff, *coff, *done, mg;
   experts_plan_arrays(L.exp_ws, P, w->E, w->d, w->F, &n_active, &active, &goff, &coff, &done,
                       &mg);
-  const int rpc = experts_rows_per_chunk(w->qtype, P, w->E, w->d, w->F);
+  const int rpc = experts_rows_per_chunk(w->qtype, experts_down_qtype(w->qtype, w->opts), P,
+                                         w->E, w->d, w->F);
   MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
                                     n_active, active, goff, coff, done, mg, rpc, L.disp_scratch,
                                     s));
   MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
                         w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
-                        L.row_max, true, 0));
+                        row_max, true, 0, w->opts));
   if (w->s_gate) {
     {
       ::moe::ProfScope _prof(MOE_K_AUX, s);
       fill_two_offsets<<<1, 32, 0, s>>>(L.s_off, T);
     }
     MOE_CHECK(check_launch("fill_offsets"));
+    const moe_expert_opts so = shared_expert_opts(w->opts);
     MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
                           nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.exp_ws, L.exp_bytes, s,
-                          L.status, L.row_max, false, 0));
+                          L.status, row_max, false, 0, &so));
   }
   return launch_combine(L.y, L.inv, wts, L.s_y, residual, T, w->k, w->d, out, s);
 }

@@ -206,6 +206,19 @@ __device__ __forceinline__ float silu_f(float g) {
   return g / (1.0f + expf(-c));
 }
 
+// GeGLU with the tanh approximation, the gemma4 expert activation
+// (qwen35_gpu.py:933-939, nightmare_stream.py:3256-3271):
+// 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))).
+__device__ __forceinline__ float gelu_tanh_f(float g) {
+  const float a = 0.7978845608028654f * (g + 0.044715f * g * g * g);
+  return 0.5f * g * (1.0f + tanhf(a));
+}
+
+// Gated activation of an expert: act(gate) (times up, by the caller).
+__device__ __forceinline__ float expert_act(int act, float g) {
+  return act == MOE_ACT_GEGLU_TANH ? gelu_tanh_f(g) : silu_f(g);
+}
+
 // numpy's float32 add.reduce order over n contiguous values (its pairwise
 // summation): sequential below 8 terms, eight running sums up to 128 terms,
 // and above that a split at n/2 rounded down to a multiple of 8.
@@ -465,6 +478,17 @@ static __device__ void write_expert_plan(int n, int e, int E, int rpc, int max_g
   }
 }
 
+
+// Work item `item` (a chunk of rpc rows of one expert) -> expert e and the
+// chunk's first row c0 inside the expert; false past the last item.
+__device__ __forceinline__ bool chunk_of(int item, const int* __restrict__ citem, int rpc,
+                                         int& e, int& c0) {
+  const int v = citem[item];
+  if (v < 0) return false;
+  e = v >> 16;
+  c0 = (v & 0xFFFF) * rpc;
+  return true;
+}
 
 // Programmatic dependent launch: wait for the previous kernel's completion
 // (no-op when launched normally) / allow the next kernel to start.

@@ -1,5 +1,5 @@
-// GGUF block decode (Q4_0 / Q8_0) and the load-time repack into MMA tiles.
-#include "moe_common.cuh"
+// GGUF block decode and the load-time repack into MMA tiles.
+#include "blockfmt.cuh"
 
 namespace moe {
 
@@ -94,6 +94,22 @@ static int repack(const uint8_t* src, uint8_t* dst, int qtype, int n_mats, int r
   return check_launch("repack");
 }
 
+// Q5_1 / Q4_K / Q6_K (dequant_fast.py:169-201, :237-289, :343-378): one thread
+// per eight weights, decoded by the expert kernels' own register decoder.
+template <int FMT>
+__global__ void dequantize8_kernel(const uint8_t* __restrict__ raw, float* __restrict__ out,
+                                   int64_t n_groups) {
+  constexpr int BE = BlockFmt<FMT>::kElems, BB = BlockFmt<FMT>::kBytes;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n_groups) return;
+  const int64_t c = 8 * g;
+  float w[8];
+  dq8<FMT>(raw + (c / BE) * BB, (int)(c % BE), w);
+  float4* o = reinterpret_cast<float4*>(out + c);
+  o[0] = make_float4(w[0], w[1], w[2], w[3]);
+  o[1] = make_float4(w[4], w[5], w[6], w[7]);
+}
+
 }  // namespace moe
 
 extern "C" {
@@ -101,6 +117,26 @@ extern "C" {
 int moe_dequantize(const uint8_t* raw, float* out, int qtype, int64_t n_elements,
                    moe_stream_t stream) {
   MOE_REQUIRE(raw && out, MOE_ERR_INVALID, "null pointer");
+  if (qtype == MOE_Q5_1 || qtype == MOE_Q4_K || qtype == MOE_Q6_K) {
+    const int be = moe::blockfmt_elems(qtype);
+    MOE_REQUIRE(n_elements >= 0 && n_elements % be == 0, MOE_ERR_INVALID,
+                "element count %lld is not a multiple of %d", (long long)n_elements, be);
+    if (n_elements == 0) return MOE_OK;
+    MOE_REQUIRE(((uintptr_t)out & 15) == 0, MOE_ERR_INVALID, "out must be 16-byte aligned");
+    const int64_t ng = n_elements / 8;
+    const unsigned grid = (unsigned)((ng + 255) / 256);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    {
+      ::moe::ProfScope _prof(MOE_K_DEQUANT, s);
+      if (qtype == MOE_Q5_1)
+        moe::dequantize8_kernel<MOE_Q5_1><<<grid, 256, 0, s>>>(raw, out, ng);
+      else if (qtype == MOE_Q4_K)
+        moe::dequantize8_kernel<MOE_Q4_K><<<grid, 256, 0, s>>>(raw, out, ng);
+      else
+        moe::dequantize8_kernel<MOE_Q6_K><<<grid, 256, 0, s>>>(raw, out, ng);
+    }
+    return moe::check_launch("dequantize");
+  }
   MOE_REQUIRE(moe::qtype_ok(qtype), MOE_ERR_UNSUPPORTED, "quant type %d not supported", qtype);
   MOE_REQUIRE(n_elements >= 0 && n_elements % 32 == 0, MOE_ERR_INVALID,
               "element count %lld is not a multiple of 32", (long long)n_elements);

@@ -330,7 +330,9 @@ tc_tile_plan_kernel(const int32_t* __restrict__ offsets, int E, int max_tiles,
 struct TcArgs {
   const uint8_t* w0;       // MODE 0: W_gate stack; MODE 1: W_down stack
   const uint8_t* w1;       // MODE 0: W_up stack
-  size_t mat_bytes;
+  size_t mat_bytes;        // bytes per expert of the MODE's stacks
+  int act;                 // MODE 0: MOE_ACT_*
+  const float* down_scale; // MODE 1: per-expert factor, or null
   int K;                   // reduction length (d or F)
   int n_tiles_n;           // output column tiles
   int P;                   // sorted rows (plane height)
@@ -777,7 +779,7 @@ tc_gateup_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
 #pragma unroll
             for (int k = 0; k < 2; ++k) {
               const int col = 8 * c8 + j + k;
-              const float h = silu_f(acc[col] * rs) * (acc[32 + col] * rs);
+              const float h = expert_act(args.act, acc[col] * rs) * (acc[32 + col] * rs);
               hv[k] = h * kTcHScale;
               if (!(fabsf(hv[k]) <= 65504.f)) set_status(args.status, MOE_STATUS_ROW_OVERFLOW);
             }
@@ -920,6 +922,7 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
         break;
       }
       if (__shfl_sync(0xffffffffu, *flag, 0)) break;
+      const float osc = (1.f / kTcHScale) * (args.down_scale ? args.down_scale[tt.e] : 1.f);
 #pragma unroll 1
       for (int c = 0; c < tt.nr; c += 16) {
         float v[16];
@@ -928,9 +931,8 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
           float4* dst = reinterpret_cast<float4*>(args.y + (size_t)orow * args.d + tt.n0 + c);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            dst[j] = make_float4(v[4 * j] * (1.f / kTcHScale), v[4 * j + 1] * (1.f / kTcHScale),
-                                 v[4 * j + 2] * (1.f / kTcHScale),
-                                 v[4 * j + 3] * (1.f / kTcHScale));
+            dst[j] = make_float4(v[4 * j] * osc, v[4 * j + 1] * osc, v[4 * j + 2] * osc,
+                                 v[4 * j + 3] * osc);
         }
       }
       // the next tile may overwrite the accumulators once every epilogue warp has read them
@@ -1019,7 +1021,7 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
                      const int32_t* offsets, int E, int rows, const float* x,
                      const int32_t* x_rows, int x_div, const float* x_row_max, int d, int F,
                      float* y, const int32_t* y_rows, const TcWs& w, int* status,
-                     cudaStream_t s) {
+                     const moe_expert_opts* opts, cudaStream_t s) {
   using Tr = QTraits<QT>;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -1055,7 +1057,8 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   TcArgs a1 = {};
   a1.w0 = w_gate;
   a1.w1 = w_up;
-  a1.mat_bytes = mat_bytes;
+  a1.mat_bytes = (opts && opts->gate_up_stride) ? opts->gate_up_stride : mat_bytes;
+  a1.act = opts ? opts->act : MOE_ACT_SWIGLU;
   a1.K = d;
   a1.n_tiles_n = F / kGuFRows;
   a1.P = rows;
@@ -1078,6 +1081,8 @@ static int launch_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* 
   TcArgs a2 = a1;
   a2.w0 = w_down;
   a2.w1 = nullptr;
+  a2.mat_bytes = mat_bytes;
+  a2.down_scale = opts ? opts->down_scale : nullptr;
   a2.K = F;
   a2.n_tiles_n = (d + kTcNMax - 1) / kTcNMax;
   a2.y = y;
@@ -1094,7 +1099,7 @@ int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_
                    const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
                    int x_div, const float* x_row_max, int d, int F, float* y,
                    const int32_t* y_rows, void* ws, size_t ws_bytes, int* status,
-                   cudaStream_t s) {
+                   const moe_expert_opts* opts, cudaStream_t s) {
   MOE_REQUIRE(tc_supported(rows, E, d, F), MOE_ERR_UNSUPPORTED, "tensor-core path shape");
   TcWs w = carve_tc(ws, rows, E, d, F);
   MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "tensor-core workspace %zu < %zu",
@@ -1102,9 +1107,9 @@ int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_
   if (!status) status = static_cast<int*>(ws);
   if (qtype == MOE_Q4_0)
     return launch_tc<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
-                               x_row_max, d, F, y, y_rows, w, status, s);
+                               x_row_max, d, F, y, y_rows, w, status, opts, s);
   return launch_tc<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div, x_row_max,
-                             d, F, y, y_rows, w, status, s);
+                             d, F, y, y_rows, w, status, opts, s);
 }
 
 }  // namespace moe

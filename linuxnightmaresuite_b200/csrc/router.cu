@@ -613,6 +613,9 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
 // names a host-side stand-in), so the address is looked up with
 // cudaGetSymbolAddress once per device, with that device current, on the first
 // call made on that device; make that first call before any stream capture.
+// The looked-up address is kept for the rest of the process: after a
+// cudaDeviceReset the device's module is loaded again and may sit elsewhere,
+// so a process that resets a device must not call this entry point again.
 // All calls share the array and it keeps the last call's contents.  Nothing
 // needs clearing: a call writes every partial logit it later reads.  Calls
 // whose kernels overlap on the GPU (different streams, or different host

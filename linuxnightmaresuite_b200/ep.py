@@ -28,6 +28,13 @@ import torch
 import torch.distributed as dist
 
 
+def _rows(a, sl=slice(None)):
+    """Contiguous expert rows of a raw block stack (numpy array or tensor)."""
+    if isinstance(a, torch.Tensor):
+        return a[sl].contiguous()
+    return np.ascontiguousarray(a[sl])
+
+
 def expert_range(rank: int, world: int, n_experts: int) -> Tuple[int, int]:
     if n_experts % world:
         raise ValueError(f"{n_experts} experts do not split over {world} ranks")
@@ -204,19 +211,16 @@ class EPMoELayer:
         sl = slice(0, El) if local else slice(self.e0, self.e1)
         if local and int(w_gate.shape[0]) != El:
             raise ValueError(f"local weights hold {w_gate.shape[0]} experts, rank owns {El}")
-        self.w_gate = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_gate[sl]), dev),
-                                     qtype, El, self.F, d)
-        self.w_up = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_up[sl]), dev),
-                                   qtype, El, self.F, d)
-        self.w_down = K.pack_weights(_to_dev_u8(np.ascontiguousarray(w_down[sl]), dev),
-                                     qtype, El, d, self.F)
+        self.w_gate = K.pack_weights(_to_dev_u8(_rows(w_gate, sl), dev), qtype, El, self.F, d)
+        self.w_up = K.pack_weights(_to_dev_u8(_rows(w_up, sl), dev), qtype, El, self.F, d)
+        self.w_down = K.pack_weights(_to_dev_u8(_rows(w_down, sl), dev), qtype, El, d, self.F)
         sh, Fs = None, 0
         if shared is not None:
             sg, su, sd = shared
-            Fs = int(np.asarray(sg).shape[-2])
-            sh = (K.pack_weights(_to_dev_u8(np.ascontiguousarray(sg), dev), shared_qtype, 1, Fs, d),
-                  K.pack_weights(_to_dev_u8(np.ascontiguousarray(su), dev), shared_qtype, 1, Fs, d),
-                  K.pack_weights(_to_dev_u8(np.ascontiguousarray(sd), dev), shared_qtype, 1, d, Fs))
+            Fs = int(sg.shape[-2])
+            sh = (K.pack_weights(_to_dev_u8(_rows(sg), dev), shared_qtype, 1, Fs, d),
+                  K.pack_weights(_to_dev_u8(_rows(su), dev), shared_qtype, 1, Fs, d),
+                  K.pack_weights(_to_dev_u8(_rows(sd), dev), shared_qtype, 1, d, Fs))
         self.lw = K.LayerWeights(self.gate_w, self.w_gate, self.w_up, self.w_down, qtype, E,
                                  top_k, d, self.F, mode, self.bias, shared=sh,
                                  shared_qtype=shared_qtype, Fs=Fs)
@@ -257,3 +261,104 @@ class EPMoELayer:
         dist.all_reduce(cnt, group=self.group)
         local = cnt[self.e0:self.e1].cpu().numpy()
         return int(np.count_nonzero(local)), int(local.sum())
+
+
+class EPLocalRanks:
+    """All W ranks of an expert-parallel layer driven by one process on one
+    device: W windows, W workspaces and W expert shards in the same HBM, the
+    same device code as one process per GPU (``moe_ep_forward_phases``).
+
+    A step runs the send phase of every rank, then the serve phase of every
+    rank, then the combine phase of every rank, all on one stream.  Each wait
+    in a phase is then satisfied by work that has already completed in stream
+    order, so no kernel depends on another one being scheduled at the same
+    time.  This exercises the exchange windows, the counts and positions, the
+    owner-side expert order and the return path on a single GPU.
+
+    Arguments as ``EPMoELayer`` (all E experts' raw blocks), plus ``world``."""
+
+    def __init__(self, gate_weight, w_gate, w_up, w_down, qtype: int, top_k: int, world: int,
+                 mode: int = 0, bias=None, device=None, shared=None, shared_qtype: int = 8):
+        from . import kernels as K
+        from . import _lib
+        from .moe_forward import _to_dev_u8, _device
+        self.K, self._lib = K, _lib
+        self.world = int(world)
+        self.device = _device(device)
+        dev = self.device
+        d, E = int(gate_weight.shape[0]), int(gate_weight.shape[1])
+        self.d, self.E, self.k, self.qtype, self.mode = d, E, top_k, qtype, mode
+        self.F = int(w_gate.shape[1])
+        self.gate_w = torch.as_tensor(np.ascontiguousarray(gate_weight, dtype=np.float32)).to(dev)
+        self.bias = None if bias is None else torch.as_tensor(
+            np.ascontiguousarray(bias, dtype=np.float32)).to(dev)
+        sh, Fs = None, 0
+        if shared is not None:
+            sg, su, sd = shared
+            Fs = int(sg.shape[-2])
+            sh = (K.pack_weights(_to_dev_u8(_rows(sg), dev), shared_qtype, 1, Fs, d),
+                  K.pack_weights(_to_dev_u8(_rows(su), dev), shared_qtype, 1, Fs, d),
+                  K.pack_weights(_to_dev_u8(_rows(sd), dev), shared_qtype, 1, d, Fs))
+        self.lws = []
+        for r in range(self.world):
+            e0, e1 = expert_range(r, self.world, E)
+            El = e1 - e0
+            sl = slice(e0, e1)
+            wg = K.pack_weights(_to_dev_u8(_rows(w_gate, sl), dev), qtype, El, self.F, d)
+            wu = K.pack_weights(_to_dev_u8(_rows(w_up, sl), dev), qtype, El, self.F, d)
+            wd = K.pack_weights(_to_dev_u8(_rows(w_down, sl), dev), qtype, El, d, self.F)
+            self.lws.append(K.LayerWeights(self.gate_w, wg, wu, wd, qtype, E, top_k, d, self.F,
+                                           mode, self.bias, shared=sh, shared_qtype=shared_qtype,
+                                           Fs=Fs))
+        self.T = None
+        self.epoch = 0
+
+    def _ensure(self, T: int) -> None:
+        if self.T == T:
+            return
+        _lib, K = self._lib, self.K
+        W = self.world
+        nbytes = ctypes.c_size_t(0)
+        _lib.call("moe_ep_window_bytes", W, self.E, T, self.k, self.d, ctypes.byref(nbytes))
+        self.windows = [torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
+                        for _ in range(W)]
+        self.peers = torch.tensor([w.data_ptr() for w in self.windows], dtype=torch.int64,
+                                  device=self.device)
+        wsb = ctypes.c_size_t(0)
+        _lib.call("moe_ep_workspace_bytes", ctypes.byref(self.lws[0].c), W, T, ctypes.byref(wsb))
+        self.wss = [torch.zeros(max(wsb.value, 256), dtype=torch.uint8, device=self.device)
+                    for _ in range(W)]
+        self.T = T
+        self.epoch = 0
+
+    def forward(self, xs, residuals=None, outs=None):
+        """xs: W tensors (T, d) f32, rank r's tokens in xs[r].  Returns the W
+        outputs.  Device work only."""
+        K, _lib = self.K, self._lib
+        W = self.world
+        if len(xs) != W:
+            raise ValueError(f"{len(xs)} token blocks for {W} ranks")
+        T = int(xs[0].shape[0])
+        for x in xs:
+            K._need(x, torch.float32, "x")
+            if int(x.shape[0]) != T:
+                raise ValueError("every rank must bring the same number of tokens")
+        self._ensure(T)
+        if outs is None:
+            outs = [torch.empty_like(x) for x in xs]
+        res = residuals if residuals is not None else [None] * W
+        self.epoch += 1
+        for phase in (_lib.MOE_EP_PHASE_SEND, _lib.MOE_EP_PHASE_SERVE, _lib.MOE_EP_PHASE_COMBINE):
+            for r in range(W):
+                _lib.call("moe_ep_forward_phases", ctypes.byref(self.lws[r].c), W, r,
+                          ctypes.c_void_p(self.peers.data_ptr()),
+                          ctypes.c_void_p(self.windows[r].data_ptr()), K._ptr(xs[r]), T,
+                          K._ptr(outs[r]), K._ptr(res[r]), self.epoch, phase,
+                          K._ptr(self.wss[r]), self.wss[r].numel(), K._stream())
+        return outs
+
+    def device_status(self):
+        """Per-rank device status words (reads and clears them; synchronises)."""
+        if self.T is None:
+            return [0] * self.world
+        return [self.K.read_status(ws) for ws in self.wss]

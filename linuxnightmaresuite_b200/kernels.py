@@ -14,9 +14,49 @@ import torch
 from . import _lib
 from ._lib import call
 
+QTYPE_F32 = _lib.MOE_F32
 QTYPE_Q4_0 = _lib.MOE_Q4_0
+QTYPE_Q5_1 = _lib.MOE_Q5_1
 QTYPE_Q8_0 = _lib.MOE_Q8_0
+QTYPE_Q4_K = _lib.MOE_Q4_K
+QTYPE_Q6_K = _lib.MOE_Q6_K
+ACT_SWIGLU = _lib.MOE_ACT_SWIGLU
+ACT_GEGLU_TANH = _lib.MOE_ACT_GEGLU_TANH
+# GGML type -> (weights per block, bytes per block), dequant_fast.py:723-754
+BLOCK_GEOMETRY = {QTYPE_F32: (1, 4), QTYPE_Q4_0: (32, 18), QTYPE_Q5_1: (32, 24),
+                  QTYPE_Q8_0: (32, 34), QTYPE_Q4_K: (256, 144), QTYPE_Q6_K: (256, 210)}
 BLOCK_BYTES = {QTYPE_Q4_0: 18, QTYPE_Q8_0: 34}
+PACKED_QTYPES = (QTYPE_Q4_0, QTYPE_Q8_0)
+
+
+def row_bytes(qtype: int, cols: int) -> int:
+    e, b = BLOCK_GEOMETRY[qtype]
+    if cols % e:
+        raise ValueError(f"row of {cols} weights is not whole blocks of type {qtype}")
+    return cols // e * b
+
+
+def packed_path(qtype: int, down_qtype: int) -> bool:
+    """Whether a layer's expert matrices are repacked into MMA tiles (Q4_0 /
+    Q8_0 on all three) or used as stored (every other combination)."""
+    return qtype in PACKED_QTYPES and down_qtype == qtype
+
+
+class ExpertOpts:
+    """Expert variant (``moe_expert_opts``): activation, down matrix type,
+    gate/up stride of a fused stack, per-expert down scale (device f32)."""
+
+    def __init__(self, act: int = ACT_SWIGLU, down_qtype: int = 0, gate_up_stride: int = 0,
+                 down_scale: Optional[torch.Tensor] = None):
+        if down_scale is not None:
+            _need(down_scale, torch.float32, "down_scale")
+        self.down_scale = down_scale
+        self.c = _lib.MoEExpertOpts(act, down_qtype, gate_up_stride,
+                                    0 if down_scale is None else down_scale.data_ptr())
+
+    @property
+    def ref(self):
+        return ctypes.byref(self.c)
 
 
 def _stream() -> ctypes.c_void_p:
@@ -54,6 +94,21 @@ def block_geometry(qtype: int) -> Tuple[int, int]:
 
 
 # --------------------------------------------------------------------------- weights
+
+def router_input(x: torch.Tensor, scale: Optional[torch.Tensor], eps: float = 1e-6,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """gemma4's router input, x / sqrt(mean(x^2) + eps) * f32(1/sqrt(d)) * scale
+    (nightmare_stream.py:4662-4667)."""
+    _need(x, torch.float32, "x")
+    if scale is not None:
+        _need(scale, torch.float32, "scale")
+    T, d = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    call("moe_router_input", _ptr(x), _ptr(scale), ctypes.c_float(eps), T, d, _ptr(out),
+         _stream())
+    return out
+
 
 def dequantize(raw: torch.Tensor, qtype: int, n_elements: int) -> torch.Tensor:
     _need(raw, torch.uint8, "raw")
@@ -126,10 +181,13 @@ def experts(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, qtyp
             offsets: torch.Tensor, x: torch.Tensor, d: int, F: int,
             x_rows: Optional[torch.Tensor] = None, x_rows_div: int = 1,
             y: Optional[torch.Tensor] = None, y_rows: Optional[torch.Tensor] = None,
-            rows: Optional[int] = None, ws: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Grouped SwiGLU experts on packed weights; returns y (rows, d) f32."""
+            rows: Optional[int] = None, ws: Optional[torch.Tensor] = None,
+            opts: Optional[ExpertOpts] = None) -> torch.Tensor:
+    """Grouped experts on packed weights (Q4_0 / Q8_0) or raw matrices (other
+    types, or a down matrix of another type); returns y (rows, d) f32."""
     for t, n in ((w_gate, "w_gate"), (w_up, "w_up"), (w_down, "w_down")):
-        _need(t, torch.uint8, n)
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or not t.is_contiguous():
+            raise TypeError(f"{n} must be a contiguous CUDA tensor")
     _need(offsets, torch.int32, "offsets")
     _need(x, torch.float32, "x")
     E = offsets.numel() - 1
@@ -140,9 +198,9 @@ def experts(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, qtyp
     if ws is None:
         ws = workspace(_size_out("moe_experts_workspace_bytes", rows, E, d, F), x.device)
         ws[:256].zero_()
-    call("moe_experts", _ptr(w_gate), _ptr(w_up), _ptr(w_down), qtype, _ptr(offsets), E, rows,
-         _ptr(x), _ptr(x_rows), x_rows_div, d, F, _ptr(y), _ptr(y_rows), _ptr(ws), ws.numel(),
-         _stream())
+    call("moe_experts_ex", _ptr(w_gate), _ptr(w_up), _ptr(w_down), qtype,
+         None if opts is None else opts.ref, _ptr(offsets), E, rows, _ptr(x), _ptr(x_rows),
+         x_rows_div, d, F, _ptr(y), _ptr(y_rows), _ptr(ws), ws.numel(), _stream())
     return y
 
 
@@ -181,13 +239,14 @@ def ep_local_order(recv_counts: torch.Tensor, max_rows: int, ws: torch.Tensor):
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
-             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+             out: Optional[torch.Tensor] = None, gemma_style: bool = False) -> torch.Tensor:
     _need(x, torch.float32, "x")
     _need(weight, torch.float32, "weight")
     T, d = x.shape
     if out is None:
         out = torch.empty_like(x)
-    call("moe_rms_norm", _ptr(x), _ptr(weight), ctypes.c_float(eps), T, d, _ptr(out), _stream())
+    call("moe_rms_norm_ex", _ptr(x), _ptr(weight), ctypes.c_float(eps), 1 if gemma_style else 0,
+         T, d, _ptr(out), _stream())
     return out
 
 
@@ -201,8 +260,10 @@ class LayerWeights:
                  mode: int = 0, bias: Optional[torch.Tensor] = None,
                  router_layout: int = _lib.MOE_ROUTER_D_E,
                  shared: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
-                 shared_qtype: int = QTYPE_Q8_0, Fs: int = 0):
+                 shared_qtype: int = QTYPE_Q8_0, Fs: int = 0,
+                 opts: Optional[ExpertOpts] = None):
         self.gate_w, self.bias = gate_w, bias
+        self.opts = opts
         self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
         self.shared = shared
         self.qtype, self.E, self.k, self.d, self.F, self.mode = qtype, E, k, d, F, mode
@@ -213,7 +274,8 @@ class LayerWeights:
             w_gate.data_ptr(), w_up.data_ptr(), w_down.data_ptr(),
             0 if s[0] is None else s[0].data_ptr(), 0 if s[1] is None else s[1].data_ptr(),
             0 if s[2] is None else s[2].data_ptr(),
-            router_layout, qtype, shared_qtype, E, k, d, F, Fs, mode)
+            router_layout, qtype, shared_qtype, E, k, d, F, Fs, mode,
+            ctypes.pointer(opts.c) if opts is not None else None)
 
     def workspace_bytes(self, T: int) -> int:
         out = ctypes.c_size_t(0)
@@ -224,14 +286,19 @@ class LayerWeights:
 def layer_forward(lw: LayerWeights, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                   residual: Optional[torch.Tensor] = None, ws: Optional[torch.Tensor] = None,
                   ids: Optional[torch.Tensor] = None,
-                  weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  weights: Optional[torch.Tensor] = None,
+                  router_x: Optional[torch.Tensor] = None) -> torch.Tensor:
     _need(x, torch.float32, "x")
+    if router_x is not None:
+        _need(router_x, torch.float32, "router_x")
+        if router_x.shape != x.shape:
+            raise ValueError("router_x must have the shape of x")
     T = x.shape[0]
     if out is None:
         out = torch.empty_like(x)
     if ws is None:
         ws = workspace(lw.workspace_bytes(T), x.device)
         ws[:256].zero_()
-    call("moe_layer_forward", ctypes.byref(lw.c), _ptr(x), T, _ptr(out), _ptr(residual),
-         _ptr(ids), _ptr(weights), _ptr(ws), ws.numel(), _stream())
+    call("moe_layer_forward_ex", ctypes.byref(lw.c), _ptr(x), _ptr(router_x), T, _ptr(out),
+         _ptr(residual), _ptr(ids), _ptr(weights), _ptr(ws), ws.numel(), _stream())
     return out

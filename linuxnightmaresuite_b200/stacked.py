@@ -37,17 +37,20 @@ class StackedMoE:
         return cls(layers, norms, eps)
 
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """x (T, d) f32 on the device -> (T, d)."""
-        cur = x
+        """x (T, d) f32 on the device -> (T, d).  The residual stream lives in
+        ``out`` (allocated once if not given): the first layer adds x into it,
+        later layers update it in place (the combine may write over its own
+        residual input), so a step allocates nothing after the first."""
         if self._buf is None or self._buf.shape != x.shape:
             self._buf = torch.empty_like(x)
         xn = self._buf
-        for i, (layer, nw) in enumerate(zip(self.layers, self.norms)):
+        res = out if out is not None else torch.empty_like(x)
+        cur = x
+        for layer, nw in zip(self.layers, self.norms):
             K.rms_norm(cur, nw, self.eps, out=xn)
-            dst = out if (out is not None and i == len(self.layers) - 1) else torch.empty_like(x)
-            layer.forward_batch(xn, residual=cur, out=dst)
-            cur = dst
-        return cur
+            layer.forward_batch(xn, residual=cur, out=res)
+            cur = res
+        return res
 
 
 class StackedEP:
@@ -83,18 +86,38 @@ class StackedEP:
             ns.append(torch.from_numpy(data.norm_w).to(layer.device))
         return cls(ls, ns, eps)
 
+    @classmethod
+    def from_layers(cls, datas, group=None, device=None, eps: float = 1e-6) -> "StackedEP":
+        """From per-layer data whose expert stacks hold this rank's experts
+        only (``synth.make_layer_device`` / ``make_layer_slice`` for the rank's
+        expert range); the layers share one exchange window."""
+        from .ep import EPExchange, EPMoELayer
+        ex = EPExchange(group, device)
+        ls, ns = [], []
+        for data in datas:
+            cfg = data.cfg
+            shared = (data.s_gate, data.s_up, data.s_down) if cfg.shared_ffn else None
+            layer = EPMoELayer(data.gate_w, data.w_gate, data.w_up, data.w_down, cfg.qtype,
+                               cfg.top_k, cfg.route_mode, data.bias, group=group, device=device,
+                               shared=shared, shared_qtype=cfg.shared_qtype, local=True,
+                               exchange=ex)
+            ls.append(layer)
+            ns.append(torch.from_numpy(data.norm_w).to(layer.device))
+        return cls(ls, ns, eps)
+
     def close(self) -> None:
         if self.layers:
             self.layers[0].exchange.close()
 
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        cur = x
+        """As ``StackedMoE.forward``, every layer expert-parallel."""
         if self._buf is None or self._buf.shape != x.shape:
             self._buf = torch.empty_like(x)
         xn = self._buf
-        for i, (layer, nw) in enumerate(zip(self.layers, self.norms)):
+        res = out if out is not None else torch.empty_like(x)
+        cur = x
+        for layer, nw in zip(self.layers, self.norms):
             K.rms_norm(cur, nw, self.eps, out=xn)
-            dst = out if (out is not None and i == len(self.layers) - 1) else torch.empty_like(x)
-            layer.forward(xn, out=dst, residual=cur)
-            cur = dst
-        return cur
+            layer.forward(xn, out=res, residual=cur)
+            cur = res
+        return res

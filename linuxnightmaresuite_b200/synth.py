@@ -118,6 +118,106 @@ CONFIGS: Dict[str, MoEConfig] = {
 }
 
 
+def q5_1_blocks(rng: np.random.Generator, n_blocks: int, scale: float) -> np.ndarray:
+    """Q5_1 blocks ``[fp16 d][fp16 m][u32 qh][16 B]``: uniform quants, d =
+    fp16(|N(0,1)| * scale), m = fp16(-16 * d * U[0.5, 1.5])."""
+    out = np.empty((n_blocks, 24), dtype=np.uint8)
+    d = _fp16_scales(rng, n_blocks, scale)
+    m = (-16.0 * d.astype(np.float32) * rng.uniform(0.5, 1.5, n_blocks).astype(np.float32))
+    out[:, :2] = d.view(np.uint8).reshape(n_blocks, 2)
+    out[:, 2:4] = m.astype(np.float16).view(np.uint8).reshape(n_blocks, 2)
+    out[:, 4:] = np.frombuffer(rng.bytes(n_blocks * 20), dtype=np.uint8).reshape(n_blocks, 20)
+    return out
+
+
+def q4_k_blocks(rng: np.random.Generator, n_blocks: int, scale: float) -> np.ndarray:
+    """Q4_K super-blocks ``[fp16 d][fp16 dmin][12 scale bytes][128 quant bytes]``:
+    uniform 6-bit scales / mins and nibbles, d = fp16(|N| * scale / 32), dmin =
+    fp16(|N| * scale / 64), so weights span about +-scale * 15."""
+    out = np.empty((n_blocks, 144), dtype=np.uint8)
+    out[:, :2] = _fp16_scales(rng, n_blocks, scale / 32).view(np.uint8).reshape(n_blocks, 2)
+    out[:, 2:4] = _fp16_scales(rng, n_blocks, scale / 64).view(np.uint8).reshape(n_blocks, 2)
+    out[:, 4:] = np.frombuffer(rng.bytes(n_blocks * 140), dtype=np.uint8).reshape(n_blocks, 140)
+    return out
+
+
+def q6_k_blocks(rng: np.random.Generator, n_blocks: int, scale: float) -> np.ndarray:
+    """Q6_K super-blocks ``[ql x 128][qh x 64][int8 scales x 16][fp16 d]``:
+    uniform quants, int8 scales in [-64, 63], d = fp16(|N| * scale / 64)."""
+    out = np.empty((n_blocks, 210), dtype=np.uint8)
+    out[:, :192] = np.frombuffer(rng.bytes(n_blocks * 192), dtype=np.uint8).reshape(n_blocks, 192)
+    out[:, 192:208] = rng.integers(-64, 64, size=(n_blocks, 16), dtype=np.int8).view(np.uint8)
+    out[:, 208:] = _fp16_scales(rng, n_blocks, scale / 64).view(np.uint8).reshape(n_blocks, 2)
+    return out
+
+
+# GGML type -> (weights per block, bytes per block) of every type the layer takes
+ALL_GEOMETRY = {0: (1, 4), QTYPE_Q4_0: (32, 18), 7: (32, 24), QTYPE_Q8_0: (32, 34),
+                12: (256, 144), 14: (256, 210)}
+
+
+def blocks_of(rng: np.random.Generator, qtype: int, n_mats: int, rows: int, cols: int,
+              scale: float) -> np.ndarray:
+    """Raw blocks of ``n_mats`` stacked (rows, cols) matrices in any type the
+    layer takes, shape (n_mats, rows, row bytes)."""
+    be, bb = ALL_GEOMETRY[qtype]
+    if cols % be:
+        raise ValueError(f"{cols} columns are not whole blocks of type {qtype}")
+    nb = n_mats * rows * (cols // be)
+    if qtype in (QTYPE_Q4_0, QTYPE_Q8_0):
+        return quant_matrix(rng, qtype, n_mats, rows, cols, scale)
+    if qtype == 0:
+        w = rng.standard_normal(nb, dtype=np.float32) * np.float32(scale * 40)
+        return w.view(np.uint8).reshape(n_mats, rows, cols * 4)
+    gen = {7: q5_1_blocks, 12: q4_k_blocks, 14: q6_k_blocks}[qtype]
+    return gen(rng, nb, scale).reshape(n_mats, rows, cols // be * bb)
+
+
+@dataclasses.dataclass
+class Gemma4LayerData:
+    """Inputs of a gemma4 MoE feed-forward block (host numpy arrays)."""
+    x: np.ndarray              # (T, d) attention output
+    router: np.ndarray         # (E, d) f32 moe_router
+    gate_inp_scale: np.ndarray  # (d,) ffn_gate_inp.scale
+    gate_up: np.ndarray        # (E, 2F, row bytes) fused Q4_K ffn_gate_up_exps
+    down: np.ndarray           # (E, d, row bytes) Q5_1 ffn_down_exps
+    down_scale: np.ndarray     # (E,) ffn_down_exps.scale
+    s_gate: np.ndarray         # (Fs, row bytes) Q8_0 dense shared MLP
+    s_up: np.ndarray
+    s_down: np.ndarray
+    ffn_norm: np.ndarray
+    post_norm_1: np.ndarray
+    pre_norm_2: np.ndarray
+    post_norm_2: np.ndarray
+
+    def digest(self) -> str:
+        h = hashlib.sha256()
+        for a in dataclasses.astuple(self):
+            h.update(np.ascontiguousarray(a).tobytes())
+        return h.hexdigest()
+
+
+def make_gemma4_layer(d: int, E: int, F: int, Fs: int, T: int, seed: int = 0,
+                      gu_qtype: int = 12, down_qtype: int = 7) -> Gemma4LayerData:
+    """A gemma4-style MoE block in the layout gemma4 GGUFs ship
+    (nightmare_stream.py:3366-3370): fused gate_up Q4_K, down Q5_1 with a
+    per-expert scale, a Q8_0 dense shared MLP."""
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((T, d), dtype=np.float32) * np.float32(4.0))
+    router = rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.5)
+    gis = (1.0 + 0.2 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+    gate_up = blocks_of(rng, gu_qtype, E, 2 * F, d, 0.01)
+    down = blocks_of(rng, down_qtype, E, d, F, 0.01)
+    down_scale = (0.5 + rng.uniform(0, 1, E)).astype(np.float32)
+    s_gate = quant_matrix(rng, QTYPE_Q8_0, 1, Fs, d, 0.002)[0]
+    s_up = quant_matrix(rng, QTYPE_Q8_0, 1, Fs, d, 0.002)[0]
+    s_down = quant_matrix(rng, QTYPE_Q8_0, 1, d, Fs, 0.002)[0]
+    norms = [(1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+             for _ in range(4)]
+    return Gemma4LayerData(x, router, gis, gate_up, down, down_scale, s_gate, s_up, s_down,
+                           *norms)
+
+
 def zipf_bias(rng: np.random.Generator, n_experts: int, s: float, c: float) -> np.ndarray:
     """Per-expert logit bias ``c * log(rank^-s)`` over a seeded permutation of
     experts: adding the log of Zipf(s) probabilities to the logits skews the
@@ -193,12 +293,7 @@ def make_layer_slice(cfg: MoEConfig, seed: int, tokens: int, e0: int, e1: int) -
     rng = np.random.default_rng([seed, E])
     gate_w = (rng.standard_normal((d, E), dtype=np.float32) * np.float32(cfg.router_std))
     x = rng.standard_normal((tokens, d), dtype=np.float32)
-    mats = []
-    for e in range(e0, e1):
-        re = np.random.default_rng([seed, e, 7])
-        mats.append((quant_matrix(re, cfg.qtype, 1, F, d, cfg.qscale),
-                     quant_matrix(re, cfg.qtype, 1, F, d, cfg.qscale),
-                     quant_matrix(re, cfg.qtype, 1, d, F, cfg.qscale)))
+    mats = [slice_expert(cfg, seed, e) for e in range(e0, e1)]
     def stack(j, rows, cols):
         if not mats:
             return np.zeros((0, rows, row_bytes(cfg.qtype, cols)), np.uint8)
@@ -212,6 +307,17 @@ def make_layer_slice(cfg: MoEConfig, seed: int, tokens: int, e0: int, e1: int) -
         data.s_down = quant_matrix(rng, cfg.shared_qtype, 1, d, Fs, cfg.shared_qscale)
     data.norm_w = (1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
     return data
+
+
+def slice_expert(cfg: MoEConfig, seed: int, e: int):
+    """Raw (gate, up, down) blocks of expert ``e`` of a ``make_layer_slice``
+    layer, each shaped (1, rows, row bytes); drawn from its own generator
+    (seed, e), so any expert can be rebuilt alone."""
+    d, F = cfg.d_model, cfg.ffn
+    re = np.random.default_rng([seed, e, 7])
+    return (quant_matrix(re, cfg.qtype, 1, F, d, cfg.qscale),
+            quant_matrix(re, cfg.qtype, 1, F, d, cfg.qscale),
+            quant_matrix(re, cfg.qtype, 1, d, F, cfg.qscale))
 
 
 def tune_zipf_scale(x: np.ndarray, gate_w: np.ndarray, unit_bias: np.ndarray, k: int,
@@ -238,3 +344,99 @@ def tune_zipf_scale(x: np.ndarray, gate_w: np.ndarray, unit_bias: np.ndarray, k:
         else:
             hi = mid
     return float(hi)
+
+
+# ----------------------------------------------------------------------------
+# device-side generation (benchmark workloads)
+#
+# The benchmark's large workloads (gigabytes of expert blocks) are drawn on the
+# GPU with torch's seeded generator: same block layout and value distribution
+# as above, a different random stream.  Every expert comes from its own
+# generator (seed, layer, expert), so a rank builds only its experts and any
+# expert can be rebuilt alone (``device_expert``) to check results on the host.
+# ----------------------------------------------------------------------------
+
+def _mix(*vals: int) -> int:
+    h = 0x9E3779B97F4A7C15
+    for v in vals:
+        h = (h ^ (int(v) & 0xFFFFFFFFFFFFFFFF)) * 0x100000001B3 & 0xFFFFFFFFFFFFFFFF
+    return h & 0x7FFFFFFFFFFFFFFF
+
+
+def _device_quant(gen, qtype: int, rows: int, cols: int, scale: float, out):
+    import torch
+    nb = rows * (cols // 32)
+    dev = out.device
+    sc = (torch.randn(nb, generator=gen, device=dev).abs_() * scale).to(torch.float16)
+    blk = out.view(nb, block_bytes(qtype))
+    blk[:, :2] = sc.view(torch.uint8).view(nb, 2)
+    if qtype == QTYPE_Q8_0:
+        blk[:, 2:] = torch.randint(-127, 128, (nb, 32), generator=gen, device=dev,
+                                   dtype=torch.int8).view(torch.uint8)
+    elif qtype == QTYPE_Q4_0:
+        blk[:, 2:] = torch.randint(0, 256, (nb, 16), generator=gen, device=dev,
+                                   dtype=torch.uint8)
+    else:
+        raise ValueError(f"unsupported qtype {qtype}")
+
+
+def _device_expert_into(cfg: MoEConfig, seed: int, layer: int, e: int, g_out, u_out, d_out):
+    import torch
+    gen = torch.Generator(device=g_out.device)
+    gen.manual_seed(_mix(seed, layer, e))
+    d, F = cfg.d_model, cfg.ffn
+    _device_quant(gen, cfg.qtype, F, d, cfg.qscale, g_out)
+    _device_quant(gen, cfg.qtype, F, d, cfg.qscale, u_out)
+    _device_quant(gen, cfg.qtype, d, F, cfg.qscale, d_out)
+
+
+def device_expert(cfg: MoEConfig, seed: int, layer: int, e: int, device):
+    """Raw (gate, up, down) blocks of expert e of a device-generated layer,
+    each (rows, row bytes) uint8 on ``device``."""
+    import torch
+    d, F = cfg.d_model, cfg.ffn
+    g = torch.empty((F, row_bytes(cfg.qtype, d)), dtype=torch.uint8, device=device)
+    u = torch.empty_like(g)
+    dn = torch.empty((d, row_bytes(cfg.qtype, F)), dtype=torch.uint8, device=device)
+    _device_expert_into(cfg, seed, layer, e, g, u, dn)
+    return g, u, dn
+
+
+def make_layer_device(cfg: MoEConfig, seed: int, tokens: int, e0: int, e1: int, device,
+                      layer: int = 0) -> MoELayerData:
+    """One layer whose experts e0..e1-1 are drawn on ``device`` (torch uint8
+    tensors in w_gate / w_up / w_down / s_*); the tokens, router weights, Zipf
+    bias and RMSNorm weight are host numpy arrays from (seed, layer) and are the
+    same on every rank."""
+    import torch
+    d, E, F = cfg.d_model, cfg.n_experts, cfg.ffn
+    rng = np.random.default_rng([seed, layer, E, 11])
+    gate_w = (rng.standard_normal((d, E), dtype=np.float32) * np.float32(cfg.router_std))
+    x = rng.standard_normal((tokens, d), dtype=np.float32)
+    bias = None
+    if cfg.zipf_s > 0:
+        unit = zipf_bias(rng, E, cfg.zipf_s, 1.0)
+        c = tune_zipf_scale(x, gate_w, unit, cfg.top_k, cfg.zipf_max_rows)
+        bias = (unit * np.float32(c)).astype(np.float32)
+    norm_w = (1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+    El = e1 - e0
+    wg = torch.empty((El, F, row_bytes(cfg.qtype, d)), dtype=torch.uint8, device=device)
+    wu = torch.empty_like(wg)
+    wd = torch.empty((El, d, row_bytes(cfg.qtype, F)), dtype=torch.uint8, device=device)
+    for i, e in enumerate(range(e0, e1)):
+        _device_expert_into(cfg, seed, layer, e, wg[i], wu[i], wd[i])
+    data = MoELayerData(cfg, x, gate_w, bias, wg, wu, wd, norm_w=norm_w)
+    if cfg.shared_ffn:
+        Fs = cfg.shared_ffn
+        gen = torch.Generator(device=device)
+        gen.manual_seed(_mix(seed, layer, 1 << 20))
+        sg = torch.empty((1, Fs, row_bytes(cfg.shared_qtype, d)), dtype=torch.uint8,
+                         device=device)
+        su = torch.empty_like(sg)
+        sd = torch.empty((1, d, row_bytes(cfg.shared_qtype, Fs)), dtype=torch.uint8,
+                         device=device)
+        _device_quant(gen, cfg.shared_qtype, Fs, d, cfg.shared_qscale, sg[0])
+        _device_quant(gen, cfg.shared_qtype, Fs, d, cfg.shared_qscale, su[0])
+        _device_quant(gen, cfg.shared_qtype, d, Fs, cfg.shared_qscale, sd[0])
+        data.s_gate, data.s_up, data.s_down = sg, su, sd
+    return data

@@ -70,7 +70,106 @@ def dequantize_q4_0(data, n_elements: int) -> np.ndarray:
     return (scales * quants).reshape(-1)
 
 
-DEQUANT = {QTYPE_Q4_0: dequantize_q4_0, QTYPE_Q8_0: dequantize_q8_0}
+QTYPE_F32 = 0
+QTYPE_Q5_1 = 7
+QTYPE_Q4_K = 12
+QTYPE_Q6_K = 14
+# dequant_fast.py:723-754 rows of the other types the layer takes
+BLOCK_SIZES.update({QTYPE_F32: (1, 4), QTYPE_Q5_1: (32, 24), QTYPE_Q4_K: (256, 144),
+                    QTYPE_Q6_K: (256, 210)})
+
+
+def _raw_blocks(data, n_blocks, block_bytes):
+    buf = data.tobytes() if isinstance(data, np.ndarray) else bytes(data)
+    return np.frombuffer(buf, dtype=np.uint8).reshape(n_blocks, block_bytes)
+
+
+def dequantize_f32(data, n_elements: int) -> np.ndarray:
+    buf = data.tobytes() if isinstance(data, np.ndarray) else bytes(data)
+    return np.frombuffer(buf, dtype=np.float32)[:n_elements].copy()
+
+
+def dequantize_q5_1(data, n_elements: int) -> np.ndarray:
+    """dequant_fast.py:169-201: 24-byte blocks [fp16 d][fp16 m][u32 qh][16 B];
+    q = nibble (low: weights 0-15, high: 16-31) | qh bit of the weight << 4;
+    value d * q + m."""
+    nb = n_elements // 32
+    raw = _raw_blocks(data, nb, 24)
+    scales = raw[:, :2].copy().view(np.float16).astype(np.float32).reshape(nb, 1)
+    mins = raw[:, 2:4].copy().view(np.float16).astype(np.float32).reshape(nb, 1)
+    qh = raw[:, 4:8].copy().view(np.uint32).reshape(nb)
+    packed = raw[:, 8:]
+    quants = np.empty((nb, 32), dtype=np.uint32)
+    quants[:, 0:16] = (packed & 0x0F).astype(np.uint32)
+    quants[:, 16:32] = ((packed >> 4) & 0x0F).astype(np.uint32)
+    bits = (qh[:, None] >> np.arange(32, dtype=np.uint32)[None, :]) & 1
+    quants |= (bits.astype(np.uint32) << 4)
+    return (scales * quants.astype(np.float32) + mins).reshape(-1)
+
+
+def _k4_scales(raw_scales, d, dmin):
+    """6-bit sub-block scales / mins of a Q4_K super-block (dequant_fast.py:256-266,
+    llama.cpp's get_scale_min_k4 packing), times d / dmin."""
+    n = raw_scales.shape[0]
+    scales = np.zeros((n, 8), dtype=np.float32)
+    mins = np.zeros((n, 8), dtype=np.float32)
+    for j in range(4):
+        scales[:, j] = d * (raw_scales[:, j] & 0x3F).astype(np.float32)
+        mins[:, j] = dmin * (raw_scales[:, j + 4] & 0x3F).astype(np.float32)
+    for j in range(4):
+        scales[:, 4 + j] = d * (((raw_scales[:, j + 8] & 0x0F)
+                                 | ((raw_scales[:, j] >> 6) << 4)).astype(np.float32))
+        mins[:, 4 + j] = dmin * (((raw_scales[:, j + 8] >> 4)
+                                  | ((raw_scales[:, j + 4] >> 6) << 4)).astype(np.float32))
+    return scales, mins
+
+
+def dequantize_q4_k(data, n_elements: int) -> np.ndarray:
+    """dequant_fast.py:237-289: 144-byte super-blocks of 256 [fp16 d][fp16 dmin]
+    [12 scale bytes][128 quant bytes]; sub-block s: low (s even) / high (s
+    odd) nibbles of quant bytes 32 (s // 2) ..; value scale_s * q - min_s."""
+    nb = n_elements // 256
+    raw = _raw_blocks(data, nb, 144)
+    d = raw[:, 0:2].copy().view(np.float16).astype(np.float32).reshape(nb)
+    dmin = raw[:, 2:4].copy().view(np.float16).astype(np.float32).reshape(nb)
+    scales, mins = _k4_scales(raw[:, 4:16], d, dmin)
+    qs = raw[:, 16:]
+    out = np.zeros((nb, 256), dtype=np.float32)
+    for g in range(4):
+        sl = qs[:, g * 32:(g + 1) * 32]
+        low = (sl & 0x0F).astype(np.float32)
+        high = ((sl >> 4) & 0x0F).astype(np.float32)
+        out[:, 64 * g:64 * g + 32] = scales[:, 2 * g, None] * low - mins[:, 2 * g, None]
+        out[:, 64 * g + 32:64 * g + 64] = scales[:, 2 * g + 1, None] * high - mins[:, 2 * g + 1, None]
+    return out.reshape(-1)
+
+
+def dequantize_q6_k(data, n_elements: int) -> np.ndarray:
+    """dequant_fast.py:343-378: 210-byte super-blocks [ql x 128][qh x 64]
+    [int8 scales x 16][fp16 d]; per half of 128 weights four streams of 32
+    from ql bytes l / l + 32 (low then high nibbles) and two qh bits each;
+    value d * scale[p // 16] * (q - 32)."""
+    nb = n_elements // 256
+    raw = _raw_blocks(data, nb, 210)
+    ql, qh = raw[:, :128], raw[:, 128:192]
+    scales = raw[:, 192:208].view(np.int8).astype(np.float32)
+    d = raw[:, 208:210].copy().view(np.float16).astype(np.float32).reshape(nb, 1)
+    out = np.zeros((nb, 256), dtype=np.float32)
+    for half in range(2):
+        qlh, qhh = ql[:, half * 64:(half + 1) * 64], qh[:, half * 32:(half + 1) * 32]
+        sch = scales[:, half * 8:(half + 1) * 8]
+        l = np.arange(32)
+        q1 = ((qlh[:, l] & 0x0F) | ((qhh[:, l] >> 0) & 0x03) << 4).astype(np.float32) - 32
+        q2 = ((qlh[:, l + 32] & 0x0F) | ((qhh[:, l] >> 2) & 0x03) << 4).astype(np.float32) - 32
+        q3 = ((qlh[:, l] >> 4) | ((qhh[:, l] >> 4) & 0x03) << 4).astype(np.float32) - 32
+        q4 = ((qlh[:, l + 32] >> 4) | ((qhh[:, l] >> 6) & 0x03) << 4).astype(np.float32) - 32
+        q_all = np.concatenate([q1, q2, q3, q4], axis=1)
+        out[:, half * 128:(half + 1) * 128] = d * np.repeat(sch, 16, axis=1) * q_all
+    return out.reshape(-1)
+
+
+DEQUANT = {QTYPE_Q4_0: dequantize_q4_0, QTYPE_Q8_0: dequantize_q8_0, QTYPE_F32: dequantize_f32,
+           QTYPE_Q5_1: dequantize_q5_1, QTYPE_Q4_K: dequantize_q4_k, QTYPE_Q6_K: dequantize_q6_k}
 
 
 def dequantize_matrix(raw: np.ndarray, qtype: int, rows: int, cols: int) -> np.ndarray:
@@ -83,9 +182,13 @@ def dequantize_matrix(raw: np.ndarray, qtype: int, rows: int, cols: int) -> np.n
 # math primitives, moe_forward.py:34-52
 # --------------------------------------------------------------------------
 
-def rms_norm(x, weight, eps=1e-6):
+def rms_norm(x, weight, eps=1e-6, gemma_style=False):
+    """moe_forward.py:34-40; gemma_style scales by (1 + weight)."""
     ms = np.mean(x * x) + eps
-    return (x / np.sqrt(ms)) * weight
+    normed = x / np.sqrt(ms)
+    if gemma_style:
+        return normed * (1.0 + weight)
+    return normed * weight
 
 
 def silu(x):
@@ -96,6 +199,25 @@ def softmax(x):
     m = np.max(x)
     e = np.exp(x - m)
     return e / np.sum(e)
+
+
+def geglu_tanh(g, u):
+    """gemma4's expert activation, nightmare_stream.py:3256-3271 (the
+    GPUStreamEngine._expert_act GeGLU branch): 0.5 g (1 + tanh(sqrt(2/pi)
+    (g + 0.044715 g^3))) u."""
+    a = np.sqrt(2.0 / np.pi) * (g + 0.044715 * g ** 3)
+    return 0.5 * g * (1.0 + np.tanh(a)) * u
+
+
+def gemma4_router_input(x, scale, dim, eps):
+    """nightmare_stream.py:4662-4667: rms of x without weight, times
+    f32(1/sqrt(dim)), times ffn_gate_inp.scale."""
+    r = x.astype(np.float32)
+    r = r / np.sqrt(np.mean(r * r) + eps)
+    r = r * np.float32(1.0 / np.sqrt(float(dim)))
+    if scale is not None:
+        r = r * np.asarray(scale, dtype=np.float32)
+    return r
 
 
 # --------------------------------------------------------------------------
@@ -171,10 +293,72 @@ class DenseExpert:
         return (silu(gate) * up) @ self.w_down.T
 
 
-def expert_from_blocks(raw_gate, raw_up, raw_down, qtype, d, F) -> DenseExpert:
+def expert_from_blocks(raw_gate, raw_up, raw_down, qtype, d, F, down_qtype=None) -> DenseExpert:
     return DenseExpert(dequantize_matrix(raw_gate, qtype, F, d),
                        dequantize_matrix(raw_up, qtype, F, d),
-                       dequantize_matrix(raw_down, qtype, d, F))
+                       dequantize_matrix(raw_down, qtype if down_qtype is None else down_qtype,
+                                         d, F))
+
+
+class GeGLUExpert:
+    """A gemma4 expert on dequantised f32 weights: down @ geglu(gate @ x, up @ x)
+    (nightmare_stream.py:4686-4690), with the down matrix already multiplied
+    by the expert's ffn_down_exps.scale as _load_expert_fast does
+    (nightmare_stream.py:3430-3438)."""
+
+    def __init__(self, w_gate, w_up, w_down):
+        self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
+
+    def forward(self, x):
+        return self.w_down @ geglu_tanh(self.w_gate @ x, self.w_up @ x)
+
+
+def gemma4_expert_from_blocks(raw_gate_up, gu_qtype, raw_down, down_qtype, d, F, down_scale=None):
+    """nightmare_stream.py:3361-3441 (_load_expert_fast): the fused gate_up
+    slice (2F, d) splits into gate = rows [0, F), up = rows [F, 2F); the down
+    slice (d, F) is multiplied by the expert's scale."""
+    gu = dequantize_matrix(raw_gate_up, gu_qtype, 2 * F, d)
+    down = dequantize_matrix(raw_down, down_qtype, d, F)
+    if down_scale is not None:
+        down = down * float(down_scale)
+    return GeGLUExpert(np.ascontiguousarray(gu[:F]), np.ascontiguousarray(gu[F:]), down)
+
+
+def gemma4_moe_block(attn_out, w, experts, n_used, eps):
+    """The MoE feed-forward of a gemma4 layer, nightmare_stream.py:4655-4693
+    (CPU branch): shared GeGLU MLP on rms(attn_out, ffn_norm) with its post
+    norm, plus the routed experts on rms(attn_out, pre_ffw_norm_2) with
+    softmax -> top-k -> renormalised weights from the router input, and their
+    post norm.  ``w``: dict with moe_router (E, d), moe_gate_inp_scale,
+    ffn_norm, wg / wu (Fs, d), wd (d, Fs), post_ffw_norm_1, pre_ffw_norm_2,
+    post_ffw_norm_2 (f32).  ``experts[e]`` has forward(x)."""
+    dim = attn_out.shape[0]
+
+    def rms(v, weight):
+        return v / np.sqrt(np.mean(v * v) + eps) * weight
+
+    mlp_in = rms(attn_out, w["ffn_norm"])
+    g_ = (mlp_in.reshape(1, -1) @ w["wg"].T)[0]
+    u_ = (mlp_in.reshape(1, -1) @ w["wu"].T)[0]
+    cur_mlp = ((geglu_tanh(g_, 1.0) * u_).reshape(1, -1) @ w["wd"].T)[0]
+    if w.get("post_ffw_norm_1") is not None:
+        cur_mlp = rms(cur_mlp, w["post_ffw_norm_1"])
+    moe_in = rms(attn_out, w["pre_ffw_norm_2"])
+    r = gemma4_router_input(attn_out, w.get("moe_gate_inp_scale"), dim, eps)
+    logits = np.asarray(w["moe_router"], dtype=np.float32) @ r
+    probs = np.exp(logits - logits.max())
+    probs /= probs.sum()
+    E = probs.shape[0]
+    k = min(int(n_used), E)
+    top = np.argsort(probs, kind="stable")[-k:]
+    tw = probs[top]
+    tw = tw / tw.sum()
+    cur_moe = np.zeros(dim, dtype=np.float32)
+    for e, wt in zip(top, tw):
+        cur_moe += float(wt) * experts[int(e)].forward(moe_in.astype(np.float32))
+    if w.get("post_ffw_norm_2") is not None:
+        cur_moe = rms(cur_moe, w["post_ffw_norm_2"])
+    return cur_mlp + cur_moe, top, tw
 
 
 class LazyExperts:

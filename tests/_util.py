@@ -74,3 +74,46 @@ def check_layer(x, gate_w, bias, k, mode, experts, shared, out_dev, ids_dev, w_d
 
 def make(cfg_name, seed=0, tokens=None, **kw):
     return synth.make_layer(synth.CONFIGS[cfg_name], seed, tokens=tokens, **kw)
+
+
+class SliceExperts:
+    """Experts of a ``synth.make_layer_slice`` layer for the oracle: each is
+    generated from its own seed and dequantised the first time it is used."""
+
+    def __init__(self, cfg, seed):
+        self.cfg, self.seed = cfg, seed
+        self.cache = {}
+
+    def __getitem__(self, e):
+        e = int(e)
+        if e not in self.cache:
+            g, u, d = synth.slice_expert(self.cfg, self.seed, e)
+            self.cache[e] = orc.expert_from_blocks(g[0], u[0], d[0], self.cfg.qtype,
+                                                   self.cfg.d_model, self.cfg.ffn)
+        return self.cache[e]
+
+
+def slice_layers(cfg, seed, tokens, n_layers):
+    """Oracle layers (gate_w, experts, shared, norm_w, bias) of a stack built
+    from ``make_layer_slice(cfg, seed + l, tokens, ...)``, yielded one at a
+    time so that a layer's dequantised experts are freed once it is done."""
+    for li in range(n_layers):
+        base = synth.make_layer_slice(cfg, seed + li, tokens, 0, 0)
+        shared = None
+        if cfg.shared_ffn:
+            shared = orc.expert_from_blocks(base.s_gate[0], base.s_up[0], base.s_down[0],
+                                            cfg.shared_qtype, cfg.d_model, cfg.shared_ffn)
+        yield base.gate_w, SliceExperts(cfg, seed + li), shared, base.norm_w, None
+
+
+def sample_tokens(ids: np.ndarray, extra=(), per_expert: int = 1):
+    """Token rows to check: ``extra`` plus, for the busiest and the rarest
+    routed expert, the first ``per_expert`` tokens that route there."""
+    E = int(ids.max()) + 1
+    counts = np.bincount(ids.reshape(-1), minlength=E)
+    busiest = int(np.argmax(counts))
+    rare = int(np.argmin(np.where(counts > 0, counts, 1 << 30)))
+    toks = set(int(t) for t in extra)
+    for e in (busiest, rare):
+        toks |= set(np.nonzero((ids == e).any(1))[0][:per_expert].tolist())
+    return sorted(toks), busiest, rare, counts

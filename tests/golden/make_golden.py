@@ -1,9 +1,10 @@
 """Generate the golden fixtures by running the reference implementation.
 
-Run from the repository root, in a container where the reference checkout is
-available (default ``/root/reference``, override with ``MOE_REFERENCE_DIR``):
+Run from the repository root, with the directory of a reference checkout as
+the argument (or in ``MOE_REFERENCE_DIR``); ``--only NAME`` regenerates just
+the named fixture groups:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py REFERENCE_DIR [--only rms_norm ...]
 
 It imports the reference's own modules -- ``moe_forward`` (router, expert
 FFN, layer), ``dequant_fast`` (Q8_0 / Q4_0 decoders, through the reference's
@@ -25,7 +26,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("MOE_REFERENCE_DIR", "/root/reference")
+REF = None   # set by main() from the command line or MOE_REFERENCE_DIR
 sys.path.insert(0, ROOT)
 
 from linuxnightmaresuite_b200 import synth  # noqa: E402
@@ -347,14 +348,183 @@ def stacked_case(mf, dqn, name, cfg, seed, n_layers, tokens):
     print("stacked", name, x.shape)
 
 
-def main():
+def rms_norm_cases(mf):
+    """The reference's rms_norm (moe_forward.py:34-40) over seeded rows of
+    several widths, both scalings."""
+    rng = np.random.default_rng(21)
+    out = {}
+    for d in (7, 100, 1024, 2816, 4096, 5000):
+        x = (rng.standard_normal((3, d), dtype=np.float32) * np.float32(3.0))
+        w = (1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+        for g in (0, 1):
+            out[f"x_{d}"] = x
+            out[f"w_{d}"] = w
+            out[f"out_{d}_{g}"] = np.stack([mf.rms_norm(x[t], w, 1e-6, gemma_style=bool(g))
+                                           for t in range(3)])
+    np.savez(os.path.join(HERE, "rms_norm.npz"), **out, **_meta())
+    print("rms_norm", len(out))
+
+
+def _special_halves(rng, n):
+    """fp16 scales with +-0, subnormals, 1.0, 65504 and random magnitudes."""
+    v = (np.abs(rng.standard_normal(n, dtype=np.float32)) * np.float32(0.01)).astype(np.float16)
+    special = np.array([0.0, -0.0, 6e-8, 1.0, 65504.0, -2.0], dtype=np.float16)
+    v[:special.size] = special
+    return v
+
+
+def kquant_blocks(dq_real, dqn):
+    """Q5_1 / Q4_K / Q6_K known answers: seeded raw blocks with special fp16
+    scales, decoded by the reference's dequant_fast on its own nightmare_np
+    substrate and on numpy (the two must agree)."""
+    rng = np.random.default_rng(31)
+    out = {}
+    cases = {7: (32, 24, 48), 12: (256, 144, 12), 14: (256, 210, 12)}
+    names = {7: "dequantize_q5_1", 12: "dequantize_q4_k", 14: "dequantize_q6_k"}
+    for qt, (be, bb, nb) in cases.items():
+        raw = np.frombuffer(rng.bytes(nb * bb), dtype=np.uint8).reshape(nb, bb).copy()
+        if qt == 7:
+            raw[:, 0:2] = _special_halves(rng, nb).view(np.uint8).reshape(nb, 2)
+            raw[:, 2:4] = _special_halves(rng, nb)[::-1].copy().view(np.uint8).reshape(nb, 2)
+        elif qt == 12:
+            raw[:, 0:2] = _special_halves(rng, nb).view(np.uint8).reshape(nb, 2)
+            raw[:, 2:4] = _special_halves(rng, nb)[::-1].copy().view(np.uint8).reshape(nb, 2)
+        else:
+            raw[:, 208:210] = _special_halves(rng, nb).view(np.uint8).reshape(nb, 2)
+        n = nb * be
+        exp_np = np.asarray(getattr(dqn, names[qt])(raw.tobytes(), n), dtype=np.float32)
+        try:   # the reference's own nightmare_np substrate, when it runs these
+            exp_real = np.asarray(getattr(dq_real, names[qt])(raw.tobytes(), n),
+                                  dtype=np.float32)
+            assert np.array_equal(exp_np.view(np.uint32), exp_real.view(np.uint32)), qt
+            out[f"substrate_{qt}"] = np.array("nightmare_np+numpy")
+        except AssertionError:
+            raise
+        except Exception as exc:   # noqa: BLE001
+            print("nightmare_np substrate failed on", names[qt], repr(exc)[:120])
+            out[f"substrate_{qt}"] = np.array("numpy")
+        out[f"raw_{qt}"] = raw
+        out[f"expected_{qt}"] = exp_np
+    np.savez(os.path.join(HERE, "kquant_blocks.npz"), **out, **_meta())
+    print("kquant_blocks", sorted(out))
+
+
+class _G4Stub:
+    """The engine state the gemma4 FFN block reads, around the reference's own
+    GPUStreamEngine methods (_mm, _rms_norm, _expert_act)."""
+
+    def __init__(self, ns, dim, n_exp, k, experts):
+        cls = ns.GPUStreamEngine
+        self._n_experts, self._n_experts_used, self.dim = n_exp, k, dim
+        self._architecture = "gemma4"
+        self.use_gpu = False
+        self._experts = experts
+        for name in ("_mm", "_rms_norm", "_expert_act", "_uses_geglu_expert"):
+            setattr(self, name, getattr(cls, name).__get__(self))
+
+    def _g4_moe_gpu_enabled(self):
+        return False
+
+    def _load_expert(self, layer_idx, ei):
+        return self._experts[ei]
+
+
+def _g4_block_source(ns):
+    """The FFN part of GPUStreamEngine._layer_forward_gemma4, from the MoE
+    test up to the sum of the shared and routed outputs."""
+    import inspect
+    import textwrap
+    src = inspect.getsource(ns.GPUStreamEngine._layer_forward_gemma4)
+    a = src.index("_is_moe = (self._n_experts")
+    b = src.index("pfn = weights.get('post_ffw_norm')")
+    body = src[a:b]
+    lines = body.split("\n")
+    indent = len(lines[1]) - len(lines[1].lstrip()) if len(lines) > 1 else 0
+    return textwrap.dedent("\n".join(" " * indent + lines[0].lstrip() if i == 0 else ln
+                                     for i, ln in enumerate(lines)))
+
+
+def gemma4_cases(dq_real, dqn, ns_np):
+    """Reference outputs of the gemma4 MoE FFN (nightmare_stream.py:4655-4693)
+    and of its GeGLU activation (GPUStreamEngine._expert_act) on seeded
+    inputs: fused Q4_K gate_up, Q5_1 down with a per-expert scale, Q8_0 shared
+    MLP, router input scale, the four sandwich norms."""
+    rng = np.random.default_rng(41)
+    stub0 = _G4Stub(ns_np, 4, 1, 1, {})
+    g = (rng.standard_normal(257, dtype=np.float32) * np.float32(3.0))
+    u = rng.standard_normal(257, dtype=np.float32)
+    act = np.asarray(stub0._expert_act(g, u))
+    from linuxnightmaresuite_b200 import synth as sy
+    d, E, k, F, Fs, T, eps = 256, 16, 4, 256, 192, 5, 1e-6
+    data = sy.make_gemma4_layer(d, E, F, Fs, T, seed=43)
+    experts = {}
+    for e in range(E):
+        gu = np.asarray(dqn.dequantize_q4_k(data.gate_up[e].tobytes(), 2 * F * d),
+                        dtype=np.float32).reshape(2 * F, d)
+        dn = np.asarray(dqn.dequantize_q5_1(data.down[e].tobytes(), d * F),
+                        dtype=np.float32).reshape(d, F)
+        # nightmare_stream.py:3422-3438: split the fused slice, scale the down
+        dn = dn * float(data.down_scale[e])
+        experts[e] = (np.ascontiguousarray(gu[:F]), np.ascontiguousarray(gu[F:]), dn)
+    shared = [np.asarray(dqn.dequantize_q8_0(m.tobytes(), m.shape[0] * (m.shape[1] // 34) * 32),
+                         dtype=np.float32).reshape(m.shape[0], -1) for m in
+              (data.s_gate, data.s_up, data.s_down)]
+    weights = {"moe_router": data.router, "moe_gate_inp_scale": data.gate_inp_scale,
+               "ffn_norm": data.ffn_norm, "wg": shared[0], "wu": shared[1], "wd": shared[2],
+               "post_ffw_norm_1": data.post_norm_1, "pre_ffw_norm_2": data.pre_norm_2,
+               "post_ffw_norm_2": data.post_norm_2}
+    code = compile(_g4_block_source(ns_np), "nightmare_stream.py:_layer_forward_gemma4", "exec")
+    outs = []
+    for t in range(T):
+        env = {"self": _G4Stub(ns_np, d, E, k, experts), "np": np, "weights": weights,
+               "x": data.x[t], "eps": eps, "layer": 0}
+        exec(code, env)
+        outs.append(np.asarray(env["f"], dtype=np.float32))
+    np.savez(os.path.join(HERE, "gemma4.npz"), act_g=g, act_u=u, act_out=act,
+             out=np.stack(outs), seed=np.int32(43), tokens=np.int32(T), digest=data.digest(),
+             eps=np.float32(eps), **_meta())
+    print("gemma4", np.stack(outs).shape)
+
+
+def main(argv=None):
+    import argparse
+    global REF
+    ap = argparse.ArgumentParser(description="generate the golden fixtures from the reference")
+    ap.add_argument("reference_dir", nargs="?", default=os.environ.get("MOE_REFERENCE_DIR"))
+    ap.add_argument("--only", action="append", default=None,
+                    help="fixture groups: kat, router, layers, stacked, rms_norm, kquant, "
+                         "gemma4")
+    args = ap.parse_args(argv)
+    if not args.reference_dir:
+        ap.error("give the reference checkout directory (argument or MOE_REFERENCE_DIR)")
+    REF = os.path.abspath(args.reference_dir)
+    only = set(args.only) if args.only else None
+
+    def want(name):
+        return only is None or name in only
+
     mf, dq_real, ns = _import_reference()
     dqn = _dequant_fast_on_numpy()
-    kat_blocks(dq_real)
+    if want("rms_norm"):
+        rms_norm_cases(mf)
+    if want("kquant"):
+        kquant_blocks(dq_real, dqn)
+    if want("gemma4"):
+        gemma4_cases(dq_real, dqn, _nightmare_stream_on_numpy())
+    if want("kat"):
+        kat_blocks(dq_real)
     ns_np = _nightmare_stream_on_numpy()
-    router_cases(mf, ns, ns_np)
+    if want("router"):
+        router_cases(mf, ns, ns_np)
     ns = ns_np
     C = synth.CONFIGS
+    if not (want("layers") or want("stacked")):
+        return
+    if not want("layers"):
+        small_stack = synth.MoEConfig("small_stack", 256, 16, 4, 128, 5, synth.QTYPE_Q4_0, 0.01,
+                                      shared_ffn=192, n_layers=2)
+        stacked_case(mf, dqn, "small_stack", small_stack, 11, 2, 5)
+        return
     layer_case(mf, ns, dqn, "cpu_layer_mode0", C["cpu_layer"], 0, None, 0)
     layer_case(mf, ns, dqn, "cpu_layer_mode1", C["cpu_layer"], 0, None, 1)
     layer_case(mf, ns, dqn, "decode_t2", C["decode_t8"], 0, 2, 0)
@@ -366,7 +536,8 @@ def main():
     layer_case(mf, ns, dqn, "small_zipf", small_zipf, 3, None, 0)
     small_stack = synth.MoEConfig("small_stack", 256, 16, 4, 128, 5, synth.QTYPE_Q4_0, 0.01,
                                   shared_ffn=192, n_layers=2)
-    stacked_case(mf, dqn, "small_stack", small_stack, 11, 2, 5)
+    if want("stacked"):
+        stacked_case(mf, dqn, "small_stack", small_stack, 11, 2, 5)
 
 
 if __name__ == "__main__":

@@ -45,7 +45,11 @@ def test_version_and_geometry(lib):
     assert (e.value, b.value) == (32, 18)
     assert lib.moe_block_geometry(8, ctypes.byref(e), ctypes.byref(b)) == 0
     assert (e.value, b.value) == (32, 34)
-    assert lib.moe_block_geometry(12, ctypes.byref(e), ctypes.byref(b)) == _lib.MOE_ERR_UNSUPPORTED
+    # dequant_fast.py:723-754 rows of the other types the layer takes
+    for qt, geo in ((0, (1, 4)), (7, (32, 24)), (12, (256, 144)), (14, (256, 210))):
+        assert lib.moe_block_geometry(qt, ctypes.byref(e), ctypes.byref(b)) == 0
+        assert (e.value, b.value) == geo
+    assert lib.moe_block_geometry(13, ctypes.byref(e), ctypes.byref(b)) == _lib.MOE_ERR_UNSUPPORTED
     assert "not supported" in _lib.last_error()
 
 

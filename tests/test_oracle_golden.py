@@ -30,8 +30,11 @@ def test_block_decode_known_answers():
 
 
 def test_block_geometry_matches_reference_table():
-    assert orc.BLOCK_SIZES == {2: (32, 18), 8: (32, 34)}
-    assert synth.BLOCK_GEOMETRY == orc.BLOCK_SIZES
+    # dequant_fast.py:723-754 rows of the types this library takes
+    ref = {0: (1, 4), 2: (32, 18), 7: (32, 24), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
+    assert orc.BLOCK_SIZES == ref
+    assert synth.ALL_GEOMETRY == ref
+    assert all(synth.BLOCK_GEOMETRY[q] == ref[q] for q in synth.BLOCK_GEOMETRY)
 
 
 @pytest.mark.parametrize("case", [0, 1, 2])
@@ -135,3 +138,57 @@ def test_dispatch_is_stable_counting_sort():
         rows = perm[off[e]:off[e + 1]]
         assert np.all(flat[rows] == e)
         assert np.all(np.diff(rows) > 0)
+
+
+@pytest.mark.parametrize("d", [7, 100, 1024, 2816, 4096, 5000])
+@pytest.mark.parametrize("gemma", [0, 1])
+def test_rms_norm_matches_reference(d, gemma):
+    """rms_norm of moe_forward.py:34-40, both weight scalings, bit for bit."""
+    z = _load("rms_norm.npz")
+    x, w = z[f"x_{d}"], z[f"w_{d}"]
+    got = np.stack([orc.rms_norm(x[t], w, 1e-6, gemma_style=bool(gemma)) for t in range(3)])
+    assert np.array_equal(got.view(np.uint32), z[f"out_{d}_{gemma}"].view(np.uint32))
+
+
+@pytest.mark.parametrize("qt", [7, 12, 14])
+def test_kquant_decoders_match_reference(qt):
+    """Q5_1 / Q4_K / Q6_K (dequant_fast.py:169-201, :237-289, :343-378) bit for bit."""
+    z = _load("kquant_blocks.npz")
+    raw, exp = z[f"raw_{qt}"], z[f"expected_{qt}"]
+    got = orc.DEQUANT[qt](raw, exp.size)
+    assert np.array_equal(got.view(np.uint32), exp.view(np.uint32))
+
+
+def test_geglu_matches_reference_expert_act():
+    z = _load("gemma4.npz")
+    got = orc.geglu_tanh(z["act_g"], z["act_u"])
+    assert got.dtype == z["act_out"].dtype
+    np.testing.assert_array_equal(got, z["act_out"])
+
+
+def gemma4_oracle_parts(data, F):
+    E = data.router.shape[0]
+    d = data.x.shape[1]
+    experts = [orc.gemma4_expert_from_blocks(data.gate_up[e], 12, data.down[e], 7, d, F,
+                                             data.down_scale[e]) for e in range(E)]
+    Fs = data.s_gate.shape[0]
+    w = {"moe_router": data.router, "moe_gate_inp_scale": data.gate_inp_scale,
+         "ffn_norm": data.ffn_norm,
+         "wg": orc.dequantize_matrix(data.s_gate, 8, Fs, d),
+         "wu": orc.dequantize_matrix(data.s_up, 8, Fs, d),
+         "wd": orc.dequantize_matrix(data.s_down, 8, d, Fs),
+         "post_ffw_norm_1": data.post_norm_1, "pre_ffw_norm_2": data.pre_norm_2,
+         "post_ffw_norm_2": data.post_norm_2}
+    return experts, w
+
+
+def test_gemma4_block_matches_reference():
+    """The oracle's gemma4 MoE block against the reference's own block code
+    (nightmare_stream.py:4655-4693) run on the same inputs."""
+    z = _load("gemma4.npz")
+    data = synth.make_gemma4_layer(256, 16, 256, 192, int(z["tokens"]), seed=int(z["seed"]))
+    assert data.digest() == str(z["digest"])
+    experts, w = gemma4_oracle_parts(data, 256)
+    for t in range(data.x.shape[0]):
+        out, _, _ = orc.gemma4_moe_block(data.x[t], w, experts, 4, float(z["eps"]))
+        np.testing.assert_allclose(out, z["out"][t], rtol=1e-6, atol=1e-5)
