@@ -100,5 +100,14 @@ class Gemma4MoEBlock:
         out = f if isinstance(attn_out, torch.Tensor) else f.cpu().numpy()
         return (out, res[1], res[2]) if return_routing else out
 
+    def routed(self, attn_out: torch.Tensor, moe_in: torch.Tensor,
+               eps: Optional[float] = None) -> torch.Tensor:
+        """The routed experts' sum alone, before post_ffw_norm_2, for a caller
+        that has normalised the experts' input itself -- what
+        _moe_ffn_g4_gpu returns (nightmare_stream.py:4330-4459)."""
+        e = self.eps if eps is None else float(eps)
+        r_in = K.router_input(attn_out, self.gis, e)
+        return self.layer.forward_batch(moe_in, router_x=r_in)
+
     def device_status(self) -> int:
         return self.layer.device_status()

@@ -302,3 +302,12 @@ def layer_forward(lw: LayerWeights, x: torch.Tensor, out: Optional[torch.Tensor]
     call("moe_layer_forward_ex", ctypes.byref(lw.c), _ptr(x), _ptr(router_x), T, _ptr(out),
          _ptr(residual), _ptr(ids), _ptr(weights), _ptr(ws), ws.numel(), _stream())
     return out
+
+
+def layer_forward_ptr(lw: LayerWeights, x_ptr: int, T: int, out_ptr: int, ws: torch.Tensor,
+                      router_x_ptr: int = 0, residual_ptr: int = 0) -> None:
+    """moe_layer_forward_ex on raw device pointers (f32 (T, d) rows on the
+    current device), for callers that hold their own device buffers."""
+    call("moe_layer_forward_ex", ctypes.byref(lw.c), ctypes.c_void_p(int(x_ptr)),
+         ctypes.c_void_p(int(router_x_ptr)), T, ctypes.c_void_p(int(out_ptr)),
+         ctypes.c_void_p(int(residual_ptr)), None, None, _ptr(ws), ws.numel(), _stream())

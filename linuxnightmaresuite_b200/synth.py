@@ -440,3 +440,58 @@ def make_layer_device(cfg: MoEConfig, seed: int, tokens: int, e0: int, e1: int, 
         _device_quant(gen, cfg.shared_qtype, d, Fs, cfg.shared_qscale, sd[0])
         data.s_gate, data.s_up, data.s_down = sg, su, sd
     return data
+
+
+# ----------------------------------------------------------------------------
+# synthetic GGUF models (one MoE block)
+# ----------------------------------------------------------------------------
+
+def moe_gguf_tensors(kind: str = "swiglu", seed: int = 0, d: int = 512, E: int = 16, F: int = 256,
+                     Fs: int = 192, k: int = 4, block: int = 0):
+    """(metadata, tensors) of a one-block MoE model in llama.cpp's tensor
+    naming, for ``gguf.write_gguf``.  Shapes are ggml order (contiguous first):
+    a logical (out, in) matrix is ``[in, out]``, an expert stack ``[in, out, E]``.
+
+    kind "swiglu": ffn_gate_inp (F32), ffn_gate_exps / ffn_up_exps (Q4_0),
+    ffn_down_exps (Q8_0), shared expert ffn_*_shexp (Q8_0).
+    kind "gemma4": fused ffn_gate_up_exps (Q4_K), ffn_down_exps (Q5_1) with
+    ffn_down_exps.scale, ffn_gate_inp.scale, dense ffn_gate/up/down (Q8_0) and
+    the four norms -- the layout nightmare_stream.py:3366-3370 describes."""
+    rng = np.random.default_rng([seed, 101])
+    p = f"blk.{block}."
+    arch = "gemma4" if kind == "gemma4" else "qwen3moe"
+    meta = {"general.architecture": arch, "general.name": f"synthetic-{kind}",
+            f"{arch}.embedding_length": d, f"{arch}.expert_count": E,
+            f"{arch}.expert_used_count": k, f"{arch}.expert_feed_forward_length": F,
+            f"{arch}.block_count": 1, f"{arch}.attention.layer_norm_rms_epsilon": 1e-6,
+            "general.tags": ["synthetic", "moe"], "general.flag": True,
+            "general.scale_hint": 0.5}
+    router = (rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.05))
+    t = [(p + "ffn_gate_inp.weight", (d, E), 0, router.tobytes())]
+    if kind == "gemma4":
+        gu = blocks_of(rng, 12, E, 2 * F, d, 0.01)
+        dn = blocks_of(rng, 7, E, d, F, 0.01)
+        ds = (0.5 + rng.uniform(0, 1, E)).astype(np.float32)
+        gis = (1.0 + 0.2 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+        t += [(p + "ffn_gate_up_exps.weight", (d, 2 * F, E), 12, gu.tobytes()),
+              (p + "ffn_down_exps.weight", (F, d, E), 7, dn.tobytes()),
+              (p + "ffn_down_exps.scale", (E,), 0, ds.tobytes()),
+              (p + "ffn_gate_inp.scale", (d,), 0, gis.tobytes())]
+        for m, (r, c) in (("gate", (Fs, d)), ("up", (Fs, d)), ("down", (d, Fs))):
+            t.append((p + f"ffn_{m}.weight", (c, r), 8,
+                      quant_matrix(rng, QTYPE_Q8_0, 1, r, c, 0.002).tobytes()))
+        for n in ("ffn_norm", "post_ffw_norm_1", "pre_ffw_norm_2", "post_ffw_norm_2"):
+            w = (1.0 + 0.1 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
+            t.append((p + f"{n}.weight", (d,), 0, w.tobytes()))
+    else:
+        for m in ("gate", "up"):
+            t.append((p + f"ffn_{m}_exps.weight", (d, F, E), 2,
+                      quant_matrix(rng, QTYPE_Q4_0, E, F, d, 0.01).tobytes()))
+        t.append((p + "ffn_down_exps.weight", (F, d, E), 8,
+                  quant_matrix(rng, QTYPE_Q8_0, E, d, F, 0.002).tobytes()))
+        for m, (r, c) in (("gate", (Fs, d)), ("up", (Fs, d)), ("down", (d, Fs))):
+            t.append((p + f"ffn_{m}_shexp.weight", (c, r), 8,
+                      quant_matrix(rng, QTYPE_Q8_0, 1, r, c, 0.002).tobytes()))
+    t.append(("token_embd.weight", (d, 8), 0,
+              rng.standard_normal((8, d), dtype=np.float32).tobytes()))
+    return meta, t

@@ -324,6 +324,43 @@ def gemma4_expert_from_blocks(raw_gate_up, gu_qtype, raw_down, down_qtype, d, F,
     return GeGLUExpert(np.ascontiguousarray(gu[:F]), np.ascontiguousarray(gu[F:]), down)
 
 
+def gemma4_routed(attn_out, moe_in, router, gate_inp_scale, experts, n_used, eps):
+    """gemma4's routed experts for one token (nightmare_stream.py:4343-4370 and
+    the expert loop of :4681-4690): router input from attn_out, softmax over
+    all experts, top-k, renormalised, sum of w * expert(moe_in).  Returns
+    (cur_moe, ids ascending, weights)."""
+    dim = attn_out.shape[0]
+    r = gemma4_router_input(attn_out, gate_inp_scale, dim, eps)
+    logits = np.asarray(router, dtype=np.float32) @ r
+    probs = np.exp(logits - logits.max())
+    probs /= probs.sum()
+    k = min(int(n_used), probs.shape[0])
+    top = np.argsort(probs, kind="stable")[-k:]
+    tw = probs[top]
+    tw = tw / tw.sum()
+    cur_moe = np.zeros(dim, dtype=np.float32)
+    for e, wt in zip(top, tw):
+        cur_moe += float(wt) * experts[int(e)].forward(np.asarray(moe_in, dtype=np.float32))
+    return cur_moe, top, tw
+
+
+def engine_moe_ffn(xn, router, experts, n_used):
+    """GPUStreamEngine._moe_ffn, nightmare_stream.py:3220-3253: logits =
+    router (E, d) @ xn, softmax over all experts, top-k ascending,
+    renormalised, sum of w * SwiGLU expert; returns (1, dim)."""
+    x = np.asarray(xn, dtype=np.float32).reshape(-1)
+    logits = np.asarray(router, dtype=np.float32) @ x
+    probs = np.exp(logits - np.max(logits))
+    probs = probs / np.sum(probs)
+    k = min(int(n_used), probs.shape[0])
+    top = np.argsort(probs, kind="stable")[-k:]
+    tw = probs[top] / np.sum(probs[top])
+    out = np.zeros(x.shape[0], dtype=np.float32)
+    for e, wt in zip(top, tw):
+        out += float(wt) * experts[int(e)].forward(x)
+    return out.reshape(1, -1), top, tw
+
+
 def gemma4_moe_block(attn_out, w, experts, n_used, eps):
     """The MoE feed-forward of a gemma4 layer, nightmare_stream.py:4655-4693
     (CPU branch): shared GeGLU MLP on rms(attn_out, ffn_norm) with its post
@@ -344,18 +381,8 @@ def gemma4_moe_block(attn_out, w, experts, n_used, eps):
     if w.get("post_ffw_norm_1") is not None:
         cur_mlp = rms(cur_mlp, w["post_ffw_norm_1"])
     moe_in = rms(attn_out, w["pre_ffw_norm_2"])
-    r = gemma4_router_input(attn_out, w.get("moe_gate_inp_scale"), dim, eps)
-    logits = np.asarray(w["moe_router"], dtype=np.float32) @ r
-    probs = np.exp(logits - logits.max())
-    probs /= probs.sum()
-    E = probs.shape[0]
-    k = min(int(n_used), E)
-    top = np.argsort(probs, kind="stable")[-k:]
-    tw = probs[top]
-    tw = tw / tw.sum()
-    cur_moe = np.zeros(dim, dtype=np.float32)
-    for e, wt in zip(top, tw):
-        cur_moe += float(wt) * experts[int(e)].forward(moe_in.astype(np.float32))
+    cur_moe, top, tw = gemma4_routed(attn_out, moe_in, w["moe_router"],
+                                     w.get("moe_gate_inp_scale"), experts, n_used, eps)
     if w.get("post_ffw_norm_2") is not None:
         cur_moe = rms(cur_moe, w["post_ffw_norm_2"])
     return cur_mlp + cur_moe, top, tw

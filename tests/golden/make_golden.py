@@ -486,6 +486,52 @@ def gemma4_cases(dq_real, dqn, ns_np):
     print("gemma4", np.stack(outs).shape)
 
 
+def gguf_cases():
+    """The reference's own GGUF parser (gguf_parser.py:325-555) on the two
+    synthetic one-block MoE files this library writes: header, metadata,
+    tensor infos, data offset and the raw bytes load_tensor_raw returns."""
+    import hashlib
+    import json
+    import tempfile
+    sys.path.insert(0, REF)
+    import gguf_parser
+    from linuxnightmaresuite_b200 import gguf
+    out = {}
+    for kind in ("swiglu", "gemma4"):
+        meta, tensors = synth.moe_gguf_tensors(kind, 3)
+        with tempfile.TemporaryDirectory() as tmp:
+            path = os.path.join(tmp, f"{kind}.gguf")
+            gguf.write_gguf(path, meta, tensors)
+            with open(path, "rb") as f:
+                file_sha = hashlib.sha256(f.read()).hexdigest()
+            parser = gguf_parser.GGUFParser(path)
+            model = parser.parse()
+            infos = {n: [list(i.shape), int(i.dtype), int(i.offset)]
+                     for n, i in model.tensors.items()}
+            raw_sha = {}
+            # the parser's arrays are its nightmare_np substrate's: convert by value
+            for n in model.tensors:
+                raw, dt, shape, ne = parser.load_tensor_raw(model, n)
+                b = np.asarray(raw.reshape(-1).tolist(), dtype=np.uint8).tobytes()
+                raw_sha[n] = [hashlib.sha256(b).hexdigest(), int(ne)]
+            f32 = {}
+            for n, i in model.tensors.items():
+                if int(i.dtype) == 0:
+                    a = parser.load_tensor(model, n)
+                    f32[n] = np.asarray(a.reshape(-1).tolist(),
+                                        dtype=np.float32).reshape(tuple(a.shape))
+            parser.close()
+        rec = {"file_sha": file_sha, "version": int(model.version),
+               "tensor_data_offset": int(model.tensor_data_offset), "infos": infos,
+               "raw_sha": raw_sha,
+               "metadata": {k: v for k, v in model.metadata.items()}}
+        out[f"{kind}_json"] = np.array(json.dumps(rec, sort_keys=True))
+        for n, a in f32.items():
+            out[f"{kind}_f32_{n}"] = a
+    np.savez(os.path.join(HERE, "gguf.npz"), **out, **_meta())
+    print("gguf", sorted(k for k in out if k.endswith("_json")))
+
+
 def main(argv=None):
     import argparse
     global REF
@@ -493,7 +539,7 @@ def main(argv=None):
     ap.add_argument("reference_dir", nargs="?", default=os.environ.get("MOE_REFERENCE_DIR"))
     ap.add_argument("--only", action="append", default=None,
                     help="fixture groups: kat, router, layers, stacked, rms_norm, kquant, "
-                         "gemma4")
+                         "gemma4, gguf")
     args = ap.parse_args(argv)
     if not args.reference_dir:
         ap.error("give the reference checkout directory (argument or MOE_REFERENCE_DIR)")
@@ -507,6 +553,8 @@ def main(argv=None):
     dqn = _dequant_fast_on_numpy()
     if want("rms_norm"):
         rms_norm_cases(mf)
+    if want("gguf"):
+        gguf_cases()
     if want("kquant"):
         kquant_blocks(dq_real, dqn)
     if want("gemma4"):

@@ -192,3 +192,19 @@ def test_gemma4_block_matches_reference():
     for t in range(data.x.shape[0]):
         out, _, _ = orc.gemma4_moe_block(data.x[t], w, experts, 4, float(z["eps"]))
         np.testing.assert_allclose(out, z["out"][t], rtol=1e-6, atol=1e-5)
+
+
+def test_engine_moe_ffn_matches_reference_engine():
+    """oracle.engine_moe_ffn against the reference's GPUStreamEngine._moe_ffn
+    outputs (the production-routing layer golden, nightmare_stream.py:3220-3253)."""
+    z = _load("layer_cpu_layer_mode1.npz")
+    data = _layer_inputs(z, LAYER_CASES["cpu_layer_mode1"])
+    cfg = data.cfg
+    experts = orc.LazyExperts(data.w_gate, data.w_up, data.w_down, cfg.qtype, cfg.d_model, cfg.ffn)
+    router = np.ascontiguousarray(data.gate_w.T)
+    for t in range(data.x.shape[0]):
+        out, ids, w = orc.engine_moe_ffn(data.x[t], router, experts, cfg.top_k)
+        assert out.shape == (1, cfg.d_model)
+        assert np.array_equal(ids, z["ids"][t])
+        mx, rel = orc.compare(out[0], z["out"][t])
+        assert rel <= 1e-6, (mx, rel)
