@@ -208,7 +208,7 @@ template <> struct Ring<MOE_Q8_0> {
 };
 
 constexpr int kGuWarps = 16;            // warps per gate/up CTA
-constexpr int kGuMaxCG = 2;             // column groups per pass of either GEMV (registers)
+constexpr int kGuMaxCG = 4;             // column groups per pass of either GEMV (registers)
 constexpr int kDnWarps = 8;             // warps per down CTA
 constexpr int kBarArea = 1024;          // mbarriers: 1 + warps x stages, 8 B each
 constexpr int kMaxSmem = 227 * 1024;    // dynamic shared memory per CTA on sm_100
@@ -254,6 +254,7 @@ struct GuCtx {
   int* status;
   uint64_t pol;
   int nst, jb, ntile, nbx, nbF, ks, kp, s, row0, n, G0, lane, act;
+  int xt0;          // first tile (of the warp's K slice) whose activations are staged
   bool strip_ok;
 };
 
@@ -290,7 +291,7 @@ __device__ __forceinline__ void gu_prefetch(const GuCtx& c) {
 // computes.  False if a wait timed out.
 template <int QT, int NCG>
 __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)[NCG][2],
-                                          const GuCtx& c, uint32_t& parity) {
+                                          const GuCtx& c, uint32_t& parity, int q0, int q1) {
   using Tr = QTraits<QT>;
   constexpr int U = Ring<QT>::kGuU;
   constexpr int TB = Tr::kTileBytes;
@@ -298,10 +299,13 @@ __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)
   constexpr int STAGE = 2 * SB;
   const int nstage = (c.ntile + U - 1) / U;
   const int cs = c.nbx * kXRec;
-  const uint8_t* xq = c.xs + c.lane * 16 + c.jb * 2 * kXRec;
-  const uint8_t* cq = c.xs + 512 + (c.lane & 3) * 16 + c.jb * 2 * kXRec;
-  int slot = 0;
-  for (int q = 0; q < nstage; ++q) {
+  // activation records of the staged blocks: tile t of the warp's K slice is
+  // at records 2 (jb + t - xt0) and + 1 of each column group
+  const int rec0 = 2 * (c.jb + q0 * U - c.xt0);
+  const uint8_t* xq = c.xs + c.lane * 16 + rec0 * kXRec;
+  const uint8_t* cq = c.xs + 512 + (c.lane & 3) * 16 + rec0 * kXRec;
+  int slot = q0 % c.nst;
+  for (int q = q0; q < q1; ++q) {
     if (!mbar_wait(&c.bars[slot], (parity >> slot) & 1u)) return false;
     parity ^= 1u << slot;
     const int nt = min(U, c.ntile - q * U);
@@ -349,17 +353,54 @@ __device__ __forceinline__ bool gu_stream(float2 (&accg)[NCG][2], float2 (&accu)
 // One chunk of NCG column groups: stream, split-K reduction across the
 // warps of a strip (rank order), SiLU(gate) * up epilogue into hidden
 // fragments.  Called uniformly by every warp of the CTA.
+// What a chunk needs to (re)build its activation records: with pt < the
+// tiles of K, the records are staged one K phase of pt tiles at a time (more
+// column groups than the whole of K would leave room for), the CTA meeting at
+// a barrier between phases; the weight rings stream on across the barrier.
+struct GuBuild {
+  const float* x;
+  const int32_t* x_rows;
+  const float* x_row_max;
+  float* rs;
+  float* rmax;
+  int x_div, ncg, d, pt;
+};
+
+template <int QT>
+__device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rmax,
+                                              const float* __restrict__ x,
+                                              const int32_t* __restrict__ x_rows, int x_div,
+                                              const float* __restrict__ x_row_max, int row0,
+                                              int c0, int n, int ncg, int d, int b0, int nbp,
+                                              int cgs);
+
 template <int QT, int NCG>
-__device__ __forceinline__ bool gu_chunk(const GuCtx& c, uint32_t& parity, int c0, bool ok) {
+__device__ __forceinline__ bool gu_chunk(GuCtx c, uint32_t& parity, int c0, bool ok,
+                                         const GuBuild& bd) {
+  constexpr int U = Ring<QT>::kGuU;
   float2 accg[NCG][2], accu[NCG][2];
 #pragma unroll
   for (int cg = 0; cg < NCG; ++cg)
 #pragma unroll
     for (int i = 0; i < 2; ++i) accg[cg][i] = accu[cg][i] = make_float2(0.f, 0.f);
-  if (c.strip_ok && ok) {
-    if (!gu_stream<QT, NCG>(accg, accu, c, parity)) {
-      set_status(c.status, MOE_STATUS_TIMEOUT);
-      ok = false;
+  const int JT = bd.d / 64;
+  const int nstage = (c.ntile + U - 1) / U;
+  for (int t0 = 0; t0 < JT; t0 += bd.pt) {
+    const int t1 = min(JT, t0 + bd.pt);
+    if (t0 > 0) __syncthreads();   // every warp is done with the previous phase's records
+    build_x_stage<QT>(const_cast<uint8_t*>(c.xs), bd.rs, bd.rmax, bd.x, bd.x_rows, bd.x_div,
+                      bd.x_row_max, c.row0, c0, c.n, bd.ncg, bd.d, 2 * t0, 2 * (t1 - t0),
+                      c.nbx);
+    __syncthreads();
+    c.xt0 = t0;
+    // one phase covers all of K (any K split), or phases of whole stages (no split)
+    const int q0 = t0 == 0 && t1 == JT ? 0 : t0 / U;
+    const int q1 = t0 == 0 && t1 == JT ? nstage : (t1 + U - 1) / U;
+    if (c.strip_ok && ok) {
+      if (!gu_stream<QT, NCG>(accg, accu, c, parity, q0, q1)) {
+        set_status(c.status, MOE_STATUS_TIMEOUT);
+        ok = false;
+      }
     }
   }
   const int lane = c.lane;
@@ -452,17 +493,21 @@ __device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rma
                                               const float* __restrict__ x,
                                               const int32_t* __restrict__ x_rows, int x_div,
                                               const float* __restrict__ x_row_max, int row0,
-                                              int c0, int n, int ncg, int d) {
+                                              int c0, int n, int ncg, int d, int b0, int nbp,
+                                              int cgs) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int NT = kGuWarps * 32;
-  const int nb = d / 32;
+  const int nb = nbp;      // blocks b0 .. b0 + nbp - 1 of the rows (a K phase),
+                           // record (cg * cgs + b - b0) for column group cg
   const int nrows = 4 * ncg;
   auto src_of = [&](int rr) -> const float* {
     const int r = row0 + c0 + rr;
     const int sr = x_rows ? x_rows[r] / x_div : r;
     return x + (size_t)sr * d;
   };
-  if (x_row_max) {
+  if (b0 > 0) {
+    // a later K phase: the rows' maxima and scales are in shared memory already
+  } else if (x_row_max) {
     if (tid < nrows) {
       const int r = row0 + c0 + tid;
       rmax[tid] = c0 + tid < n ? x_row_max[x_rows ? x_rows[r] / x_div : r] : 0.f;
@@ -483,7 +528,7 @@ __device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rma
     }
   }
   __syncthreads();
-  if (tid < nrows) {
+  if (tid < nrows && b0 == 0) {
     const float m = rmax[tid];
     float inv = 1.f;
     if (m > 0.f && isfinite(m)) inv = ldexpf(1.f, ilogbf(m) - 14);
@@ -493,7 +538,7 @@ __device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rma
   for (int it = tid; it < nrows * nb; it += NT) {
     const int rr = it / nb, b = it - rr * nb;
     const int cg = rr >> 2, w = rr & 3;
-    uint8_t* rec = xs + (size_t)(cg * nb + b) * kXRec;
+    uint8_t* rec = xs + (size_t)(cg * cgs + b) * kXRec;
     float* cor = reinterpret_cast<float*>(rec + 512);
     if (c0 + rr >= n) {
 #pragma unroll
@@ -509,7 +554,7 @@ __device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rma
     const float m = rmax[rr];
     float scale = 1.f;
     if (m > 0.f && isfinite(m)) scale = ldexpf(1.f, 14 - ilogbf(m));
-    const float4* src = reinterpret_cast<const float4*>(src_of(rr)) + b * 8;
+    const float4* src = reinterpret_cast<const float4*>(src_of(rr)) + (b0 + b) * 8;
     float v[32];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -554,15 +599,15 @@ __device__ __forceinline__ void build_x_stage(uint8_t* xs, float* rs, float* rma
 // one expert.  Per chunk of up to cgp groups of 4 rows, every warp first starts
 // its weight ring, then the CTA builds the chunk's activation fragments.
 // ---------------------------------------------------------------------------
-template <int QT>
+template <int QT, int NCGM>
 __global__ void __launch_bounds__(kGuWarps * 32, 1)
 gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, size_t gu_stride,
               int act, int d, int F, const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
               const int* __restrict__ active, const int* __restrict__ goff,
               const int* __restrict__ citem, const float* __restrict__ x,
               const int32_t* __restrict__ x_rows, int x_div, const float* __restrict__ x_row_max,
-              uint8_t* __restrict__ hfrag, int ks, int cgp, int nst, int* __restrict__ done,
-              int* __restrict__ status) {
+              uint8_t* __restrict__ hfrag, int ks, int cgp, int nst, int pt,
+              int* __restrict__ done, int* __restrict__ status) {
   using Tr = QTraits<QT>;
   constexpr int TB = Tr::kTileBytes;
   constexpr int SMAX = Ring<QT>::kGuStages;
@@ -575,7 +620,7 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   // after the wait keeps the plan complete for it.
   pdl_wait();
   pdl_trigger();
-  const int xbytes = gu_x_stage_bytes(d, cgp);
+  const int xbytes = cgp * 2 * pt * kXRec;
   GuCtx c;
   c.xs = smem;
   c.bars = reinterpret_cast<uint64_t*>(smem + xbytes) + warp * SMAX;
@@ -599,7 +644,8 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   c.row0 = offsets[e];
   c.n = offsets[e + 1] - c.row0;
   c.G0 = goff[e];
-  c.nbx = d / 32;
+  c.nbx = 2 * pt;      // staged blocks per column group
+  c.xt0 = 0;
   c.nbF = F / 32;
   c.nst = nst;
   c.lane = lane;
@@ -617,10 +663,14 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
   uint32_t parity = 0u;
   const int ncg = min(cgp, (c.n - c0 + 3) / 4);
   gu_prefetch<QT>(c);
-  build_x_stage<QT>(smem, rs_s, rmax_s, x, x_rows, x_div, x_row_max, c.row0, c0, c.n, ncg, d);
-  __syncthreads();
-  if (ncg == 1) gu_chunk<QT, 1>(c, parity, c0, true);
-  else gu_chunk<QT, 2>(c, parity, c0, true);
+  const GuBuild bd = {x, x_rows, x_row_max, rs_s, rmax_s, x_div, ncg, d, pt};
+  // NCGM: the most column groups this instance handles (2 or 4; the
+  // 4-group accumulators need registers the smaller instance keeps free)
+  if (ncg == 1) gu_chunk<QT, 1>(c, parity, c0, true, bd);
+  else if constexpr (NCGM <= 2) gu_chunk<QT, 2>(c, parity, c0, true, bd);
+  else if (ncg == 2) gu_chunk<QT, 2>(c, parity, c0, true, bd);
+  else if (ncg == 3) gu_chunk<QT, 3>(c, parity, c0, true, bd);
+  else gu_chunk<QT, 4>(c, parity, c0, true, bd);
   // this CTA's hidden fragments of the chunk are complete: count it (the down
   // kernel's CTAs of the chunk start once all of its gate/up CTAs have)
   __threadfence();
@@ -630,10 +680,15 @@ gateup_kernel(const uint8_t* __restrict__ wg, const uint8_t* __restrict__ wu, si
 }
 
 // ---------------------------------------------------------------------------
-// down: CTA = 8 warps = 8 strips of 16 d-rows of one expert; K = F is short.
+// down: CTA = 8 warps of one expert chunk; warp w streams strips
+// s0 + w, s0 + w + 8, ... (spw of them, 16 d-rows each) back to back through
+// one continuous ring, so a CTA's prologue, its wait for the gate/up CTAs and
+// its first-copy latency are paid once for spw strips.  K = F is short (11
+// tiles at F = 704), which is why one strip per warp left the kernel
+// latency-bound.
 // ---------------------------------------------------------------------------
 struct DnCtx {
-  const uint8_t* base;
+  const uint8_t* mat;    // this expert's W_down
   uint8_t* ring;
   uint64_t* bars;
   const uint8_t* hs;
@@ -642,58 +697,102 @@ struct DnCtx {
   int* status;
   uint64_t pol;
   float scale;   // per-expert factor on the down projection (1 if none)
-  int nst, JT, nbF, s, d, row0, n, lane;
-  bool strip_ok;
+  int nst, JT, nbF, d, row0, n, lane;
+  int s0, sstep, ns;     // strips s0 + i * sstep, i < ns
 };
 
-// Stage q of this warp's W_down tiles into ring slot `slot` (lane 0).
+// Stage q of the warp's flattened stage sequence (stage j of strip i, with
+// nsps stages per strip) into ring slot `slot` (lane 0).
 template <int QT>
 __device__ __forceinline__ void dn_issue(const DnCtx& c, int q, int slot) {
   using Tr = QTraits<QT>;
   constexpr int U = Ring<QT>::kDnU;
   constexpr int TB = Tr::kTileBytes;
-  const int t0 = q * U;
+  const int nsps = (c.JT + U - 1) / U;
+  const int i = q / nsps, j = q - i * nsps;
+  const int t0 = j * U;
   const uint32_t bytes = (uint32_t)(min(U, c.JT - t0) * TB);
+  const uint8_t* src = c.mat + ((size_t)(c.s0 + i * c.sstep) * c.JT + t0) * TB;
   mbar_expect_tx(&c.bars[slot], bytes);
-  bulk_g2s(c.ring + slot * U * TB, c.base + (size_t)t0 * TB, bytes, &c.bars[slot], c.pol);
+  bulk_g2s(c.ring + slot * U * TB, src, bytes, &c.bars[slot], c.pol);
 }
 
-// First stages of a chunk; the weights do not depend on the gate/up kernel,
-// so the first chunk's are issued before waiting for it.
+// First stages; the weights do not depend on the gate/up kernel, so they are
+// issued before waiting for it.
 template <int QT>
 __device__ __forceinline__ void dn_prefetch(const DnCtx& c) {
   constexpr int U = Ring<QT>::kDnU;
-  const int nstage = (c.JT + U - 1) / U;
-  if (c.lane == 0 && c.strip_ok) {
+  const int total = c.ns * ((c.JT + U - 1) / U);
+  if (c.lane == 0 && total > 0) {
     fence_proxy_async_smem();
-    for (int q = 0; q < min(c.nst, nstage); ++q) dn_issue<QT>(c, q, q);
+    for (int q = 0; q < min(c.nst, total); ++q) dn_issue<QT>(c, q, q);
   }
 }
 
+// Epilogue of strip s: quad reduction, y rows of the chunk's tokens.
+template <int NCG>
+__device__ __forceinline__ void dn_store(const DnCtx& c, float2 (&acc)[NCG][2], int s, int c0) {
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      acc[cg][i].x += __shfl_xor_sync(0xffffffffu, acc[cg][i].x, 2);
+      acc[cg][i].y += __shfl_xor_sync(0xffffffffu, acc[cg][i].y, 2);
+    }
+  const int g = c.lane >> 2, t = c.lane & 3;
+  if (t < 2 && c.y != nullptr) {
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg) {
+#pragma unroll
+      for (int ci = 0; ci < 2; ++ci) {
+        const int tok = c0 + 4 * cg + 2 * t + ci;
+        if (tok >= c.n) continue;
+        const int r = c.row0 + tok;
+        const int orow = c.y_rows ? c.y_rows[r] : r;
+        float* yr = c.y + (size_t)orow * c.d + s * 16 + g;
+        yr[0] = (ci ? acc[cg][0].y : acc[cg][0].x) * (1.0f / kHScale) * c.scale;
+        yr[8] = (ci ? acc[cg][1].y : acc[cg][1].x) * (1.0f / kHScale) * c.scale;
+      }
+    }
+  }
+}
+
+// Streams the warp's ns strips; after each strip's last stage its rows are
+// stored and the accumulators restart.  After a timed-out wait no further
+// copy is issued, but every copy already issued is still waited for (each
+// wait bounded), so none is left in flight when the kernel returns.
 template <int QT, int NCG>
-__device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
-                                          uint32_t& parity) {
+__device__ __forceinline__ bool dn_stream(const DnCtx& c, uint32_t& parity, int c0) {
   using Tr = QTraits<QT>;
   constexpr int U = Ring<QT>::kDnU;
   constexpr int TB = Tr::kTileBytes;
   constexpr int STAGE = U * TB;
-  const int nstage = (c.JT + U - 1) / U;
+  const int nsps = (c.JT + U - 1) / U;
+  const int total = c.ns * nsps;
   const int cs = c.nbF * 512;
+  float2 acc[NCG][2];
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = make_float2(0.f, 0.f);
+  bool ok = true;
+  int slot = 0, j = 0, i = 0;
+  int issued = min(c.nst, total);          // stages issued so far (dn_prefetch)
   const uint8_t* xq = c.hs + c.lane * 16;
-  int slot = 0;
-  for (int q = 0; q < nstage; ++q) {
-    if (!mbar_wait(&c.bars[slot], (parity >> slot) & 1u)) return false;
+  for (int q = 0; q < issued; ++q) {
+    ok = __all_sync(0xffffffffu, mbar_wait(&c.bars[slot], (parity >> slot) & 1u)) && ok;
     parity ^= 1u << slot;
-    const int nt = min(U, c.JT - q * U);
+    const int nt = min(U, c.JT - j * U);
     const uint8_t* st = c.ring + slot * STAGE;
     TileRegs<QT> tw[U];
 #pragma unroll
     for (int u = 0; u < U; ++u)
       if (u < nt) lds_tile<QT>(tw[u], st + u * TB, c.lane);
     __syncwarp();
-    if (c.lane == 0 && q + c.nst < nstage) {
-      fence_proxy_async_smem();
-      dn_issue<QT>(c, q + c.nst, slot);
+    if (ok && q + c.nst < total) {
+      if (c.lane == 0) {
+        fence_proxy_async_smem();
+        dn_issue<QT>(c, q + c.nst, slot);
+      }
+      issued = q + c.nst + 1;
     }
     slot = (slot + 1 == c.nst) ? 0 : slot + 1;
 #pragma unroll
@@ -713,57 +812,27 @@ __device__ __forceinline__ bool dn_stream(float2 (&acc)[NCG][2], const DnCtx& c,
       }
     }
     xq += U * 1024;
-  }
-  return true;
-}
-
-template <int QT, int NCG>
-__device__ __forceinline__ bool dn_chunk(const DnCtx& c, uint32_t& parity, int c0, bool ok) {
-  float2 acc[NCG][2];
+    if (++j == nsps) {
+      if (ok) dn_store<NCG>(c, acc, c.s0 + i * c.sstep, c0);
 #pragma unroll
-  for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = make_float2(0.f, 0.f);
-  if (c.strip_ok && ok) {
-    if (!dn_stream<QT, NCG>(acc, c, parity)) {
-      set_status(c.status, MOE_STATUS_TIMEOUT);
-      ok = false;
-    }
-  }
-#pragma unroll
-  for (int cg = 0; cg < NCG; ++cg)
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      acc[cg][i].x += __shfl_xor_sync(0xffffffffu, acc[cg][i].x, 2);
-      acc[cg][i].y += __shfl_xor_sync(0xffffffffu, acc[cg][i].y, 2);
-    }
-  const int g = c.lane >> 2, t = c.lane & 3;
-  if (t < 2 && c.strip_ok) {
-#pragma unroll
-    for (int cg = 0; cg < NCG; ++cg) {
-#pragma unroll
-      for (int ci = 0; ci < 2; ++ci) {
-        const int tok = c0 + 4 * cg + 2 * t + ci;
-        if (tok >= c.n) continue;
-        const int r = c.row0 + tok;
-        const int orow = c.y_rows ? c.y_rows[r] : r;
-        float* yr = c.y + (size_t)orow * c.d + c.s * 16 + g;
-        yr[0] = (ci ? acc[cg][0].y : acc[cg][0].x) * (1.0f / kHScale) * c.scale;
-        yr[8] = (ci ? acc[cg][1].y : acc[cg][1].x) * (1.0f / kHScale) * c.scale;
-      }
+      for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = make_float2(0.f, 0.f);
+      j = 0;
+      ++i;
+      xq = c.hs + c.lane * 16;
     }
   }
   return ok;
 }
 
-template <int QT>
+template <int QT, int NCGM>
 __global__ void __launch_bounds__(kDnWarps * 32, 2)
 down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
             const int32_t* __restrict__ offsets, const int* __restrict__ n_active,
             const int* __restrict__ active, const int* __restrict__ goff,
             const int* __restrict__ citem, const uint8_t* __restrict__ hfrag, float* __restrict__ y,
             const int32_t* __restrict__ y_rows, const float* __restrict__ down_scale, int cgp,
-            int nst, const int* __restrict__ done, int gu_cpe, int* __restrict__ status) {
-  using Tr = QTraits<QT>;
-  constexpr int TB = Tr::kTileBytes;
+            int nst, int spw, const int* __restrict__ done, int gu_cpe,
+            int* __restrict__ status) {
   constexpr int SMAX = Ring<QT>::kDnStages;
   static_assert(kDnWarps * SMAX * 8 + 16 <= kBarArea, "barrier area");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -775,12 +844,14 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   int* ok_s = reinterpret_cast<int*>(smem + xbytes + kDnWarps * SMAX * 8);
   c.ring = smem + xbytes + kBarArea + warp * nst * dn_stage_bytes<QT>();
   const int strips = d / 16;
-  const int cpe = (strips + kDnWarps - 1) / kDnWarps;
+  const int per_cta = kDnWarps * spw;
+  const int cpe = (strips + per_cta - 1) / per_cta;
   const int item = blockIdx.x / cpe;      // the same chunk as the gate/up CTAs that wrote it
   int e, c0;
   if (!chunk_of(item, citem, 4 * cgp, e, c0)) return;
-  c.s = (blockIdx.x % cpe) * kDnWarps + warp;
-  c.strip_ok = c.s < strips;
+  c.s0 = (blockIdx.x % cpe) * per_cta + warp;
+  c.sstep = kDnWarps;
+  c.ns = c.s0 < strips ? min(spw, (strips - c.s0 + kDnWarps - 1) / kDnWarps) : 0;
   c.JT = F / 64;
   c.row0 = offsets[e];
   c.n = offsets[e + 1] - c.row0;
@@ -792,7 +863,7 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   c.y = y;
   c.y_rows = y_rows;
   c.status = status;
-  c.base = wd + (size_t)e * mat_bytes + (size_t)(c.strip_ok ? c.s : 0) * c.JT * TB;
+  c.mat = wd + (size_t)e * mat_bytes;
   c.scale = down_scale ? down_scale[e] : 1.0f;
   c.pol = evict_first_policy();
   if (lane == 0) {
@@ -808,18 +879,26 @@ down_kernel(const uint8_t* __restrict__ wd, size_t mat_bytes, int d, int F,
   // (gate/up lets this grid start only after its own wait for the plan).
   if (threadIdx.x == 0) *ok_s = wait_count(done + item, gu_cpe) ? 1 : 0;
   __syncthreads();
-  if (*ok_s == 0 && threadIdx.x == 0) set_status(status, MOE_STATUS_TIMEOUT);
+  const bool ok = *ok_s != 0;
+  if (!ok && threadIdx.x == 0) set_status(status, MOE_STATUS_TIMEOUT);
   pdl_trigger();
   const int ncg = min(cgp, (c.n - c0 + 3) / 4);
   // hidden fragments of the chunk's groups: plain loads (they were written by
-  // other CTAs' plain stores, ordered by the counter's release / acquire); the
-  // rings are streamed regardless of a timeout so every issued copy is consumed
+  // other CTAs' plain stores, ordered by the counter's release / acquire)
   const uint4* src = reinterpret_cast<const uint4*>(hfrag + (size_t)(G0 + c0 / 4) * c.nbF * 512);
   uint4* dst = reinterpret_cast<uint4*>(smem);
   for (int i = threadIdx.x; i < ncg * c.nbF * 32; i += kDnWarps * 32) dst[i] = src[i];
   __syncthreads();
-  if (ncg == 1) dn_chunk<QT, 1>(c, parity, c0, true);
-  else dn_chunk<QT, 2>(c, parity, c0, true);
+  // the rings are streamed regardless of a timeout so every issued copy is
+  // consumed; rows are stored only when both the wait and the stream succeeded
+  bool st;
+  if (!ok) c.y = nullptr;
+  if (ncg == 1) st = dn_stream<QT, 1>(c, parity, c0);
+  else if constexpr (NCGM <= 2) st = dn_stream<QT, 2>(c, parity, c0);
+  else if (ncg == 2) st = dn_stream<QT, 2>(c, parity, c0);
+  else if (ncg == 3) st = dn_stream<QT, 3>(c, parity, c0);
+  else st = dn_stream<QT, 4>(c, parity, c0);
+  if (!st) set_status(status, MOE_STATUS_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
@@ -888,9 +967,31 @@ int experts_workspace(int rows, int E, int d, int F, size_t* bytes) {
 
 // Launch shape of the two GEMV kernels for a call.
 struct ExpertsPlan {
-  int ks, cgp_gu, nst_gu, smem_gu, grid_gu, cpe_gu;
-  int cgp_dn, nst_dn, smem_dn, grid_dn;
+  int ks, cgp_gu, nst_gu, smem_gu, grid_gu, cpe_gu, pt_gu;
+  int cgp_dn, nst_dn, smem_dn, grid_dn, spw_dn;
 };
+
+// Strips per warp of the down kernel.  A strip is short (F / 64 tiles), so a
+// CTA's fixed cost (prologue, wait for gate/up, first-copy latency, about one
+// strip's streaming time) is amortised over spw strips; spw is chosen to
+// minimise rounds * (spw + 1) for the expected work items on two CTAs per SM.
+#ifndef MOE_DN_SPW
+#define MOE_DN_SPW 0
+#endif
+static int down_strips_per_warp(int rows, int est_active, int strips_d, int cgp) {
+  if (MOE_DN_SPW > 0) return MOE_DN_SPW;
+  // measured on B200: with fewer than about four CTAs per SM the down grid
+  // stops overlapping the gate/up tail (decode T=64: 4 strips per warp,
+  // 786 CTAs, 151 us per layer; 11 strips, 262 CTAs, 169 us; 1 strip, 159 us)
+  const long long items = std::max(est_active, (rows + 4 * cgp - 1) / (4 * cgp));
+  const long long min_ctas = 4LL * sm_count();
+  int best = 1;
+  for (int spw = 2; spw <= 8; ++spw) {
+    const long long cpe = (strips_d + kDnWarps * spw - 1) / (kDnWarps * spw);
+    if (items * cpe >= min_ctas) best = spw;
+  }
+  return best;
+}
 
 template <int QT>
 static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
@@ -916,20 +1017,32 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   const int spc = kGuWarps / p.ks;
   p.cpe_gu = (strips_f + spc - 1) / spc;
   // gate/up: stages for the tiles a warp streams (clamped), then the largest
-  // column-group count that fits; fewer stages before fewer groups
+  // column-group count whose activation records fit beside the rings -- for
+  // all of K, or (without a K split) for one K phase of pt tiles, a whole
+  // number of stages, staged phase by phase
   const int gu_u = Ring<QT>::kGuU;
   p.nst_gu = std::max(1, std::min(Ring<QT>::kGuStages, ((JT + p.ks - 1) / p.ks + gu_u - 1) / gu_u));
-  for (;;) {
-    const int ring = kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
-    const int fit = (kMaxSmem - kBarArea - ring) / gu_x_stage_bytes(d, 1);
-    p.cgp_gu = std::min(std::min(want_cg, kGuMaxCG), fit);
-    if (p.cgp_gu >= std::min(want_cg, kGuMaxCG) || p.nst_gu <= 2) break;
-    --p.nst_gu;
+  const int ring = kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
+  const int avail = kMaxSmem - kBarArea - ring;
+  const int want = std::min(want_cg, kGuMaxCG);
+  p.cgp_gu = 0;
+  p.pt_gu = JT;
+  for (int cg = want; cg >= 1 && p.cgp_gu == 0; --cg) {
+    // the split-K reduction (cg KB per warp) lives in the rings
+    if (p.ks > 1 && p.nst_gu * gu_stage_bytes<QT>() < cg * 1024) continue;
+    if (cg * 2 * JT * kXRec <= avail) {
+      p.cgp_gu = cg;
+      p.pt_gu = JT;
+    } else if (p.ks == 1) {
+      const int pt = avail / (cg * 2 * kXRec) / gu_u * gu_u;   // tiles per phase
+      if (pt >= gu_u && cg > 2) {
+        p.cgp_gu = cg;
+        p.pt_gu = pt;
+      }
+    }
   }
   if (p.cgp_gu < 1) return false;
-  // the split-K reduction (cgp KB per warp) lives in the rings
-  if (p.ks > 1 && p.nst_gu * gu_stage_bytes<QT>() < p.cgp_gu * 1024) return false;
-  p.smem_gu = gu_x_stage_bytes(d, p.cgp_gu) + kBarArea + kGuWarps * p.nst_gu * gu_stage_bytes<QT>();
+  p.smem_gu = p.cgp_gu * 2 * p.pt_gu * kXRec + kBarArea + ring;
   const int dn_u = Ring<QT>::kDnU;
   p.nst_dn = std::max(1, std::min(Ring<QT>::kDnStages, (F / 64 + dn_u - 1) / dn_u));
   const int ring_dn = kDnWarps * p.nst_dn * dn_stage_bytes<QT>();
@@ -940,7 +1053,8 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   // work items: chunks of 4 * cgp rows, at most rows / (4 cgp) + one per expert
   const int items = std::min(max_groups(rows, E), rows / (4 * p.cgp_gu) + est_active);
   p.grid_gu = items * p.cpe_gu;
-  p.grid_dn = items * ((strips_d + kDnWarps - 1) / kDnWarps);
+  p.spw_dn = down_strips_per_warp(rows, est_active, strips_d, p.cgp_gu);
+  p.grid_dn = items * ((strips_d + kDnWarps * p.spw_dn - 1) / (kDnWarps * p.spw_dn));
   return true;
 }
 
@@ -959,12 +1073,17 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   int dev = 0;
   MOE_CUDA(cudaGetDevice(&dev));
   if (!((attr_set >> (dev & 63)) & 1ull)) {
-    MOE_CUDA(cudaFuncSetAttribute(gateup_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    MOE_CUDA(cudaFuncSetAttribute(gateup_kernel<QT, 2>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    MOE_CUDA(cudaFuncSetAttribute(gateup_kernel<QT, 4>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+    MOE_CUDA(cudaFuncSetAttribute(down_kernel<QT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kMaxSmem));
-    MOE_CUDA(cudaFuncSetAttribute(down_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    MOE_CUDA(cudaFuncSetAttribute(down_kernel<QT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   kMaxSmem));
     attr_set |= 1ull << (dev & 63);
   }
+  const bool wide = p.cgp_gu > 2;
   const int mg = max_groups(rows, E);
   if (!planned) {
     ::moe::ProfScope _prof(MOE_K_PLAN, s);
@@ -978,18 +1097,22 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
   const float* down_scale = opts ? opts->down_scale : nullptr;
   {
     ::moe::ProfScope _prof(MOE_K_GATEUP, s);
-    MOE_CUDA(launch_pdl(gateup_kernel<QT>, dim3(p.grid_gu), dim3(kGuWarps * 32), p.smem_gu, s,
+    MOE_CUDA(launch_pdl(wide ? gateup_kernel<QT, 4> : gateup_kernel<QT, 2>, dim3(p.grid_gu),
+                        dim3(kGuWarps * 32), p.smem_gu, s,
                         w_gate, w_up, gu_stride, act, d, F, offsets, (const int*)w.n_active,
                         (const int*)w.active, (const int*)w.goff, (const int*)w.coff, x, x_rows,
-                        x_div, x_row_max, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, w.done, w.status));
+                        x_div, x_row_max, w.hfrag, p.ks, p.cgp_gu, p.nst_gu, p.pt_gu, w.done,
+                        w.status));
   }
   MOE_CHECK(check_launch("gateup"));
   {
     ::moe::ProfScope _prof(MOE_K_DOWN, s);
-    MOE_CUDA(launch_pdl(down_kernel<QT>, dim3(p.grid_dn), dim3(kDnWarps * 32), p.smem_dn, s,
+    MOE_CUDA(launch_pdl(wide ? down_kernel<QT, 4> : down_kernel<QT, 2>, dim3(p.grid_dn),
+                        dim3(kDnWarps * 32), p.smem_dn, s,
                         w_down, mat_bytes, d, F, offsets, (const int*)w.n_active,
                         (const int*)w.active, (const int*)w.goff, (const int*)w.coff,
                         (const uint8_t*)w.hfrag, y, y_rows, down_scale, p.cgp_dn, p.nst_dn,
+                        p.spw_dn,
                         (const int*)w.done, p.cpe_gu, w.status));
   }
   return check_launch("down");
