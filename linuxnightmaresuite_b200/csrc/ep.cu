@@ -159,6 +159,20 @@ __device__ __forceinline__ bool wait_flag_sys(const int* p, int target) {
   return false;
 }
 
+// One row of n4 float4s copied by one warp with 8 loads in flight per lane
+// (the destination may be another GPU's window: posted stores over NVLink).
+__device__ __forceinline__ void copy_row_warp(float4* dst, const float4* src, int n4, int lane) {
+  for (int v = lane; v < n4; v += 32 * 8) {
+    float4 t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (v + 32 * u < n4) t[u] = src[v + 32 * u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (v + 32 * u < n4) dst[v + 32 * u] = t[u];
+  }
+}
+
 struct EpArgs {
   uint8_t* const* peers;   // W window bases (device array; own window included)
   uint8_t* win;            // this rank's window
@@ -197,7 +211,7 @@ ep_send_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm, in
     const float4* src = reinterpret_cast<const float4*>(x + (size_t)(perm[i] / k) * a.d);
     float4* dst = reinterpret_cast<float4*>(
         reinterpret_cast<float*>(a.peers[o] + a.off.recv_x) + ((size_t)a.rank * a.cap + j) * a.d);
-    for (int v = lane; v < a.d / 4; v += 32) dst[v] = __ldg(src + v);
+    copy_row_warp(dst, src, a.d / 4, lane);
   }
   if (blockIdx.x == 0) {
     for (int v = threadIdx.x; v < a.W * (a.El + 1); v += blockDim.x) {
@@ -304,7 +318,7 @@ ep_return_kernel(EpArgs a) {
         reinterpret_cast<const float*>(a.win + a.off.recv_x) + ((size_t)s * a.cap + i) * a.d);
     float4* dst = reinterpret_cast<float4*>(
         reinterpret_cast<float*>(a.peers[s] + a.off.ret_y) + (size_t)(base + i) * a.d);
-    for (int v = lane; v < a.d / 4; v += 32) dst[v] = src[v];
+    copy_row_warp(dst, src, a.d / 4, lane);
   }
   ep_finish(a, reinterpret_cast<int*>(a.win + a.off.counters) + 1, a.off.ret_flag);
 }
