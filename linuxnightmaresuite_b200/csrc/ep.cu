@@ -492,7 +492,7 @@ int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* con
     experts_plan_arrays(L.exp_ws, R, El, w->d, w->F, &n_active, &active, &goff, &coff, &done,
                         &mg);
     const int rpc = experts_rows_per_chunk(w->qtype, experts_down_qtype(w->qtype, w->opts), R,
-                                           El, w->d, w->F);
+                                           El, w->d, w->F, P);
     {
       ::moe::ProfScope _prof(MOE_K_EP_RECV, s);
       ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, coff,

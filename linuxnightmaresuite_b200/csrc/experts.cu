@@ -994,13 +994,19 @@ static int down_strips_per_warp(int rows, int est_active, int strips_d, int cgp)
 }
 
 template <int QT>
-static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
-  const int est_active = rows < E ? rows : E;
+// rows bounds the call (grids, buffers); hint (when below it) is the rows it
+// is expected to see, which picks column groups and the K split -- an
+// expert-parallel owner is planned for up to every rank's rows but usually
+// receives its own share.
+static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p, int hint = 0) {
+  const int bound_active = rows < E ? rows : E;
+  const int hrows = hint > 0 && hint < rows ? hint : rows;
+  const int est_active = hrows < E ? hrows : E;
   const int strips_f = F / 16, strips_d = d / 16;
   const int JT = d / 64;
   const int target = sm_count() * kGuWarps;  // one full CTA per SM
   // column groups per pass: about twice the mean rows of an expert
-  const int mean_rows = (rows + est_active - 1) / est_active;
+  const int mean_rows = (hrows + est_active - 1) / est_active;
   const int want_cg = std::max(1, std::min(kMaxCG, (2 * mean_rows + 3) / 4));
   // split K over 2, 4 or 8 warps of a strip until the chunks' strips fill the
   // GPU with one CTA per SM (every CTA builds its chunk's activations for all
@@ -1009,7 +1015,7 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
 #define MOE_KS_BY_ITEMS 1
 #endif
   const int cg_est = std::min(want_cg, kGuMaxCG);
-  const int items_est = MOE_KS_BY_ITEMS ? std::max(est_active, (rows + 4 * cg_est - 1) / (4 * cg_est))
+  const int items_est = MOE_KS_BY_ITEMS ? std::max(est_active, (hrows + 4 * cg_est - 1) / (4 * cg_est))
                                         : est_active;
   p.ks = 1;
   while (p.ks < 8 && (long long)items_est * strips_f * p.ks < target && JT / (2 * p.ks) >= 2)
@@ -1051,9 +1057,9 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p) {
   if ((kMaxSmem - kBarArea - ring_dn) / x_stage_bytes(F, 1) < p.cgp_dn) return false;
   p.smem_dn = x_stage_bytes(F, p.cgp_dn) + kBarArea + ring_dn;
   // work items: chunks of 4 * cgp rows, at most rows / (4 cgp) + one per expert
-  const int items = std::min(max_groups(rows, E), rows / (4 * p.cgp_gu) + est_active);
+  const int items = std::min(max_groups(rows, E), rows / (4 * p.cgp_gu) + bound_active);
   p.grid_gu = items * p.cpe_gu;
-  p.spw_dn = down_strips_per_warp(rows, est_active, strips_d, p.cgp_gu);
+  p.spw_dn = down_strips_per_warp(hrows, est_active, strips_d, p.cgp_gu);
   p.grid_dn = items * ((strips_d + kDnWarps * p.spw_dn - 1) / (kDnWarps * p.spw_dn));
   return true;
 }
@@ -1064,10 +1070,10 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
                           const int32_t* offsets, int E, int rows, const float* x,
                           const int32_t* x_rows, int x_div, const float* x_row_max, bool planned,
                           int d, int F, float* y, const int32_t* y_rows, const ExpertsWs& w,
-                          const moe_expert_opts* opts, cudaStream_t s) {
+                          const moe_expert_opts* opts, int rows_hint, cudaStream_t s) {
   using Tr = QTraits<QT>;
   ExpertsPlan p;
-  MOE_REQUIRE(plan_experts<QT>(rows, E, d, F, p), MOE_ERR_UNSUPPORTED,
+  MOE_REQUIRE(plan_experts<QT>(rows, E, d, F, p, rows_hint), MOE_ERR_UNSUPPORTED,
               "d=%d / F=%d too large for the staged activation buffers", d, F);
   static unsigned long long attr_set = 0;  // per template instance, bit per device
   int dev = 0;
@@ -1120,11 +1126,12 @@ static int launch_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint
 
 // Plan arrays inside an experts workspace, for a dispatch that writes them.
 // Rows per work item (chunk) of the GEMV kernels for a call's shape.
-int experts_rows_per_chunk(int qtype, int dn_qtype, int rows, int E, int d, int F) {
+int experts_rows_per_chunk(int qtype, int dn_qtype, int rows, int E, int d, int F,
+                           int rows_hint) {
   if (!experts_packed(qtype, dn_qtype)) return raw_rows_per_chunk(d, F);
   ExpertsPlan p;
-  const bool ok = qtype == MOE_Q4_0 ? plan_experts<MOE_Q4_0>(rows, E, d, F, p)
-                                    : plan_experts<MOE_Q8_0>(rows, E, d, F, p);
+  const bool ok = qtype == MOE_Q4_0 ? plan_experts<MOE_Q4_0>(rows, E, d, F, p, rows_hint)
+                                    : plan_experts<MOE_Q8_0>(rows, E, d, F, p, rows_hint);
   return ok ? 4 * p.cgp_gu : 4;
 }
 
@@ -1212,9 +1219,9 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
               w.bytes);
   if (qtype == MOE_Q4_0)
     return launch_experts<MOE_Q4_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
-                                    x_row_max, planned, d, F, y, y_rows, w, opts, s);
+                                    x_row_max, planned, d, F, y, y_rows, w, opts, rows_hint, s);
   return launch_experts<MOE_Q8_0>(w_gate, w_up, w_down, offsets, E, rows, x, x_rows, x_div,
-                                  x_row_max, planned, d, F, y, y_rows, w, opts, s);
+                                  x_row_max, planned, d, F, y, y_rows, w, opts, rows_hint, s);
 }
 
 }  // namespace moe

@@ -23,7 +23,9 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
                 int x_div, int d, int F, float* y, const int32_t* y_rows, void* ws,
                 size_t ws_bytes, cudaStream_t s, int* status, const float* x_row_max,
                 bool planned, int rows_hint, const moe_expert_opts* opts);
-int experts_rows_per_chunk(int qtype, int dn_qtype, int rows, int E, int d, int F);
+// rows per work item of the GEMV path; rows_hint as run_experts'
+int experts_rows_per_chunk(int qtype, int dn_qtype, int rows, int E, int d, int F,
+                           int rows_hint = 0);
 int experts_down_qtype(int qtype, const moe_expert_opts* opts);
 int experts_workspace(int rows, int E, int d, int F, size_t* bytes);
 int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes);
