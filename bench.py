@@ -242,8 +242,9 @@ def run_reference(args):
         return
     wl = WORKLOADS[args.workload]
     n = min(wl.tokens, wl.cpu_tokens)
-    times, dq = cpu_layer_timing(wl, args.seed, n, max(args.steps, 1), max(args.warmup, 0))
-    ms = 1e3 * float(np.mean(times)) * wl.layers
+    # at least 2 warm-up runs and the median of at least 5
+    times, dq = cpu_layer_timing(wl, args.seed, n, max(args.steps, 5), max(args.warmup, 2))
+    ms = 1e3 * float(np.median(times)) * wl.layers
     value = n / (ms / 1e3)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
@@ -255,7 +256,9 @@ def run_reference(args):
                    "dequant_s_untimed": dq},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
                          "sample": f"first {n} of {wl.tokens} tokens per step, weights "
-                                   f"pre-dequantised, physical cores"},
+                                   f"pre-dequantised, physical cores, median of "
+                                   f"{max(args.steps, 5)} runs after {max(args.warmup, 2)} "
+                                   f"warm-up"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

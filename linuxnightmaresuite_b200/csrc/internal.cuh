@@ -6,9 +6,25 @@
 namespace moe {
 
 // router.cu
+// The dispatch of one token's k pairs, done by the router's selection CTA
+// (the outputs of launch_dispatch_planned).
+struct SmallDispatch {
+  int32_t* offsets;
+  int32_t* perm;
+  int32_t* inv;
+  int* status;
+  int* n_active;
+  int* active;
+  int* goff;
+  int* coff;
+  int* done;
+  int max_groups, rpc;
+};
+bool router_fuses_dispatch(int T, int E, int k);
 int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
                   int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
-                  size_t workspace_bytes, cudaStream_t stream, float* row_max);
+                  size_t workspace_bytes, cudaStream_t stream, float* row_max,
+                  const SmallDispatch* sd = nullptr);
 
 // dispatch.cu
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,

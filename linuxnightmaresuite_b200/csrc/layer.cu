@@ -97,20 +97,26 @@ int moe_layer_forward_ex(const moe_layer_weights* w, const float* x, const float
   int32_t* ids = ids_out ? ids_out : L.ids;
   float* wts = weights_out ? weights_out : L.wts;
   const int P = T * w->k;
-  // the router's per-row maxima double as the experts' activation scaling,
-  // so they are only taken from the router when it reads the experts' input
-  MOE_CHECK(launch_router(router_x ? router_x : x, w->gate_w, w->bias, T, w->d, w->E, w->k,
-                          w->router_layout, w->mode, ids, wts, L.router_ws, L.router_bytes, s,
-                          router_x ? nullptr : L.row_max));
-  const float* row_max = router_x ? nullptr : L.row_max;
   int *n_active, *active, *goff, *coff, *done, mg;
   experts_plan_arrays(L.exp_ws, P, w->E, w->d, w->F, &n_active, &active, &goff, &coff, &done,
                       &mg);
   const int rpc = experts_rows_per_chunk(w->qtype, experts_down_qtype(w->qtype, w->opts), P,
                                          w->E, w->d, w->F);
-  MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
-                                    n_active, active, goff, coff, done, mg, rpc, L.disp_scratch,
-                                    s));
+  // one token: the router's selection CTA also sorts its k pairs and writes
+  // the plan (no dispatch kernel)
+  SmallDispatch sd = {L.offsets, L.perm, L.inv, L.status, n_active, active, goff, coff, done,
+                      mg, rpc};
+  const bool fused = router_fuses_dispatch(T, w->E, w->k);
+  // the router's per-row maxima double as the experts' activation scaling,
+  // so they are only taken from the router when it reads the experts' input
+  MOE_CHECK(launch_router(router_x ? router_x : x, w->gate_w, w->bias, T, w->d, w->E, w->k,
+                          w->router_layout, w->mode, ids, wts, L.router_ws, L.router_bytes, s,
+                          router_x ? nullptr : L.row_max, fused ? &sd : nullptr));
+  const float* row_max = router_x ? nullptr : L.row_max;
+  if (!fused)
+    MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
+                                      n_active, active, goff, coff, done, mg, rpc,
+                                      L.disp_scratch, s));
   MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
                         w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
                         row_max, true, 0, w->opts));

@@ -23,7 +23,7 @@
 #include <algorithm>
 #include <mutex>
 
-#include "moe_common.cuh"
+#include "internal.cuh"
 
 namespace moe {
 
@@ -462,6 +462,91 @@ router_select_kernel(const float* __restrict__ part, const float* __restrict__ p
   }
 }
 
+// One token (decode at T = 1): the selection as router_select_kernel, then the
+// dispatch of its k pairs in the same CTA -- a stable sort by expert of k
+// values, the offsets and the grouped experts' plan -- which saves the
+// dispatch kernel's launch and dependency on the layer's critical path.  The
+// result equals dispatch_kernel's for the same ids.
+template <int NJ>
+__global__ void __launch_bounds__(kSelMaxThreads)
+router_select_dispatch_kernel(const float* __restrict__ part, const float* __restrict__ pmax,
+                              int nds, const float* __restrict__ bias, int E, int k, int mode,
+                              int32_t* __restrict__ ids, float* __restrict__ weights,
+                              float* __restrict__ row_max, SmallDispatch sd) {
+  __shared__ float red[kSelMaxThreads / 128][kMaxE];
+  __shared__ float lg[kMaxE];
+  __shared__ int sel[kMaxK];
+  __shared__ int sh[33];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int Q = blockDim.x / 128;
+  const int q = tid / 128;
+  const int s0 = q * nds / Q, s1 = (q + 1) * nds / Q;
+  const size_t stride = (size_t)E;
+  for (int e = tid % 128; e < E; e += 128) {
+    const float* p = part + e;
+    float acc = 0.f;
+    int s = s0;
+    for (; s + 8 <= s1; s += 8) {
+      float v8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v8[u] = p[(size_t)(s + u) * stride];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += v8[u];
+    }
+    for (; s < s1; ++s) acc += p[(size_t)s * stride];
+    red[q][e] = acc;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    float acc = red[0][e];
+    for (int qq = 1; qq < Q; ++qq) acc += red[qq][e];
+    if (bias) acc += bias[e];
+    lg[e] = acc;
+  }
+  if (row_max && tid >= 128 * (Q - 1) && tid < 128 * (Q - 1) + 32) {
+    float m = 0.f;
+    for (int s = lane; s < nds; s += 32) m = fmaxf(m, pmax[s]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) row_max[0] = m;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    float v[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int e = lane + 32 * j;
+      v[j] = e < E ? lg[e] : 0.f;
+    }
+    select_warp<NJ>(v, E, k, mode, red[0], ids, weights);
+    __syncwarp();
+    if (lane < k) sel[lane] = ids[lane];
+  }
+  __syncthreads();
+  // stable counting sort of the k pairs by expert
+  if (tid < k) {
+    const int ej = sel[tid];
+    int rank = 0;
+    for (int i = 0; i < k; ++i) rank += (sel[i] < ej || (sel[i] == ej && i < tid)) ? 1 : 0;
+    sd.perm[rank] = tid;
+    sd.inv[tid] = rank;
+  }
+  int n = 0, below = 0;
+  if (tid < E) {
+    for (int i = 0; i < k; ++i) {
+      n += sel[i] == tid ? 1 : 0;
+      below += sel[i] < tid ? 1 : 0;
+    }
+    sd.offsets[tid] = below;
+  }
+  if (tid == 0) sd.offsets[E] = k;
+  if (sd.n_active)
+    write_expert_plan(n, tid, E, sd.rpc, sd.max_groups, sh, sd.n_active, sd.active, sd.goff,
+                      sd.coff, sd.done, sd.status);
+}
+
 // Workspace of moe_router: the status word, the partial logits and the
 // partial row maxima.
 static size_t router_ws(int T, int d, int E) {
@@ -474,7 +559,8 @@ static size_t router_ws(int T, int d, int E) {
 static int launch_router_passes(const float* x, const float* gate_w, const float* bias, int T,
                                 int d, int E, int k, int layout, int mode, int32_t* ids,
                                 float* weights, float* part, float* pmax, float* row_max,
-                                cudaStream_t s, size_t max_parts = ~(size_t)0) {
+                                cudaStream_t s, size_t max_parts = ~(size_t)0,
+                                const SmallDispatch* sd = nullptr) {
   const RouterPlan p = router_plan(T, d, E, max_parts);
   const size_t red = (size_t)kRouterWarps * p.tt * 128 * sizeof(float);
   {
@@ -525,6 +611,20 @@ static int launch_router_passes(const float* x, const float* gate_w, const float
     const dim3 grid2(T), block2(128 * Q);
     const float* pc = part;
     const float* pmc = pm;
+    if (sd) {
+      // one token: selection and dispatch in one CTA of at least E threads
+      const dim3 b1(128 * std::max(Q, (E + 127) / 128));
+      if (E <= 32)
+        MOE_CUDA(launch_pdl(router_select_dispatch_kernel<1>, dim3(1), b1, 0, s, pc, pmc, p.nds,
+                            bias, E, k, mode, ids, weights, row_max, *sd));
+      else if (E <= 128)
+        MOE_CUDA(launch_pdl(router_select_dispatch_kernel<4>, dim3(1), b1, 0, s, pc, pmc, p.nds,
+                            bias, E, k, mode, ids, weights, row_max, *sd));
+      else
+        MOE_CUDA(launch_pdl(router_select_dispatch_kernel<kMaxE / 32>, dim3(1), b1, 0, s, pc,
+                            pmc, p.nds, bias, E, k, mode, ids, weights, row_max, *sd));
+      return check_launch("router_select_dispatch");
+    }
     if (E <= 32)
       MOE_CUDA(launch_pdl(router_select_kernel<1>, grid2, block2, 0, s, pc, pmc, p.nds, bias, T,
                           E, k, mode, ids, weights, row_max));
@@ -560,8 +660,11 @@ static int check_router_args(const float* x, const float* gate_w, int T, int d, 
 // activation prep of the grouped experts).
 int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
                   int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
-                  size_t workspace_bytes, cudaStream_t stream, float* row_max) {
+                  size_t workspace_bytes, cudaStream_t stream, float* row_max,
+                  const SmallDispatch* sd) {
   MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
+  MOE_REQUIRE(!sd || router_fuses_dispatch(T, E, k), MOE_ERR_INVALID,
+              "the fused dispatch serves one token");
   if (T == 0) return MOE_OK;
   MOE_CHECK(check_router_args(x, gate_w, T, d, E, k, layout, mode, ids, weights));
   MOE_REQUIRE(workspace, MOE_ERR_INVALID, "null workspace");
@@ -573,7 +676,11 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
   float* pmax = reinterpret_cast<float*>(
       base + align_up(router_part_floats(p, T, E) * sizeof(float), 256));
   return launch_router_passes(x, gate_w, bias, T, d, E, k, layout, mode, ids, weights, part,
-                              pmax, row_max, stream);
+                              pmax, row_max, stream, ~(size_t)0, sd);
+}
+
+bool router_fuses_dispatch(int T, int E, int k) {
+  return T == 1 && E <= kSelMaxThreads && k <= kMaxK;
 }
 
 }  // namespace moe
@@ -591,7 +698,8 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
                int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
                size_t workspace_bytes, moe_stream_t stream) {
   return moe::launch_router(x, gate_w, bias, T, d, E, k, layout, mode, ids, weights, workspace,
-                            workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr);
+                            workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr,
+                            nullptr);
 }
 
 }  // extern "C"
