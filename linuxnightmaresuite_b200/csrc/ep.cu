@@ -494,9 +494,11 @@ int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* con
     const int rpc = experts_rows_per_chunk(w->qtype, experts_down_qtype(w->qtype, w->opts), R,
                                            El, w->d, w->F, P);
     {
+      // a programmatic dependent of the send: it reads nothing of it before
+      // the per-source flags (its own included) say the rows and counts are in
       ::moe::ProfScope _prof(MOE_K_EP_RECV, s);
-      ep_recv_plan_kernel<<<1, 1024, 0, s>>>(a, L.loff, L.row_map, n_active, active, goff, coff,
-                                             done, mg, rpc, L.status);
+      MOE_CUDA(launch_pdl(ep_recv_plan_kernel, dim3(1), dim3(1024), 0, s, a, L.loff, L.row_map,
+                          n_active, active, goff, coff, done, mg, rpc, L.status));
     }
     MOE_CHECK(check_launch("ep_recv_plan"));
     float* recv = reinterpret_cast<float*>(a.win + a.off.recv_x);
@@ -524,8 +526,9 @@ int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* con
   }
   if (phases & MOE_EP_PHASE_COMBINE) {
     {
+      // likewise after the return: only the owners' flags are read
       ::moe::ProfScope _prof(MOE_K_EP_WAIT, s);
-      ep_wait_kernel<<<1, 32, 0, s>>>(a, L.status);
+      MOE_CUDA(launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, s, a, L.status));
     }
     MOE_CHECK(check_launch("ep_wait"));
     MOE_CHECK(launch_combine(reinterpret_cast<const float*>(a.win + a.off.ret_y), L.inv, L.wts,

@@ -993,12 +993,19 @@ static int down_strips_per_warp(int rows, int est_active, int strips_d, int cgp)
   return best;
 }
 
-template <int QT>
 // rows bounds the call (grids, buffers); hint (when below it) is the rows it
 // is expected to see, which picks column groups and the K split -- an
 // expert-parallel owner is planned for up to every rank's rows but usually
 // receives its own share.
+template <int QT>
 static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p, int hint = 0) {
+  // K-phased activation staging (items wider than all of K leaves room for,
+  // at a CTA barrier per phase) only from this many expected rows per expert;
+  // below, narrower single-phase items
+#ifndef MOE_GU_PHASE_MIN_ROWS
+#define MOE_GU_PHASE_MIN_ROWS 12
+#endif
+  constexpr int kGuPhaseMinRows = MOE_GU_PHASE_MIN_ROWS;
   const int bound_active = rows < E ? rows : E;
   const int hrows = hint > 0 && hint < rows ? hint : rows;
   const int est_active = hrows < E ? hrows : E;
@@ -1039,7 +1046,7 @@ static bool plan_experts(int rows, int E, int d, int F, ExpertsPlan& p, int hint
     if (cg * 2 * JT * kXRec <= avail) {
       p.cgp_gu = cg;
       p.pt_gu = JT;
-    } else if (p.ks == 1) {
+    } else if (p.ks == 1 && mean_rows >= kGuPhaseMinRows) {
       const int pt = avail / (cg * 2 * kXRec) / gu_u * gu_u;   // tiles per phase
       if (pt >= gu_u && cg > 2) {
         p.cgp_gu = cg;
