@@ -181,7 +181,10 @@ struct EpArgs {
 };
 
 // Completion of a multi-CTA send: the last CTA to finish raises every peer's
-// flag (slot `rank` of the flag array at `flag_off`) to the epoch.
+// flag (slot `rank` of the flag array at `flag_off`) to the epoch.  Each CTA's
+// rows are visible system-wide (its system fence) before it counts itself,
+// so the last CTA needs only a GPU-scope fence to order the flags after the
+// other CTAs' counts (whose rows are then already visible to the peers).
 __device__ __forceinline__ void ep_finish(const EpArgs& a, int* ctr, size_t flag_off) {
   __threadfence_system();
   __syncthreads();
@@ -189,7 +192,7 @@ __device__ __forceinline__ void ep_finish(const EpArgs& a, int* ctr, size_t flag
     const int prev = atomicAdd(ctr, 1);
     if (prev == (int)(gridDim.x * gridDim.y) - 1) {
       *ctr = 0;
-      __threadfence_system();
+      __threadfence();
       for (int o = 0; o < a.W; ++o)
         st_release_sys(reinterpret_cast<int*>(a.peers[o] + flag_off) + a.rank, a.epoch);
     }
