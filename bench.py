@@ -351,11 +351,13 @@ def ncu_traffic(workload: str, kernel: str):
 
 
 class Built:
-    """A workload ready to step on this rank."""
+    """A workload ready to step on this rank.  host_io: the step takes pinned
+    host tensors itself (its kernels read x and write the output over the bus)."""
 
-    def __init__(self, wl, step, x_np, T, datas, status, close, routing_stats):
+    def __init__(self, wl, step, x_np, T, datas, status, close, routing_stats, host_io=False):
         self.wl, self.step, self.x_np, self.T, self.datas = wl, step, x_np, T, datas
         self.status, self.close, self.routing_stats = status, close, routing_stats
+        self.host_io = host_io
 
 
 def build(wl: Workload, seed: int, rank: int, world: int, dev) -> Built:
@@ -427,7 +429,7 @@ def build(wl: Workload, seed: int, rank: int, world: int, dev) -> Built:
     data.w_gate = data.w_up = data.w_down = None
     torch.cuda.synchronize()
     return Built(wl, step, x_np, T, [data], lambda: int(layer.device_status()), close,
-                 routing_stats)
+                 routing_stats, host_io=world == 1)
 
 
 def measure(wl: Workload, args, steps: int, warmup: int, rank: int, world: int, local: int,
@@ -501,10 +503,16 @@ def measure(wl: Workload, args, steps: int, warmup: int, rank: int, world: int, 
     x_dev = torch.empty_like(x)
     e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    def e2e_step():
+        if b.host_io:   # the layer reads x and writes out in host memory itself
+            b.step(x_host, out_host)
+        else:
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(b.step(x_dev, out), non_blocking=True)
+
     for _ in range(2):
         pre_step()
-        x_dev.copy_(x_host, non_blocking=True)
-        out_host.copy_(b.step(x_dev, out), non_blocking=True)
+        e2e_step()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -512,9 +520,7 @@ def measure(wl: Workload, args, steps: int, warmup: int, rank: int, world: int, 
         for i in range(steps):
             pre_step()
             e_starts[i].record()
-            x_dev.copy_(x_host, non_blocking=True)
-            res = b.step(x_dev, out)
-            out_host.copy_(res, non_blocking=True)
+            e2e_step()
             e_ends[i].record()
         torch.cuda.synchronize()
     e2e_ms = float(np.mean([s.elapsed_time(e) for s, e in zip(e_starts, e_ends)]))

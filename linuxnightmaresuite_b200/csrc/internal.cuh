@@ -24,7 +24,7 @@ bool router_fuses_dispatch(int T, int E, int k);
 int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
                   int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
                   size_t workspace_bytes, cudaStream_t stream, float* row_max,
-                  const SmallDispatch* sd = nullptr);
+                  const SmallDispatch* sd = nullptr, float* xcopy = nullptr);
 
 // dispatch.cu
 int launch_dispatch_planned(const int32_t* ids, int T, int k, int E, int32_t* offsets,

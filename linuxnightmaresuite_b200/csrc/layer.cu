@@ -27,8 +27,24 @@ struct LayerWs {
   int32_t* s_off;
   float* s_y;
   float* row_max;
+  float* xdev;      // device copy of x when the caller's x is in host memory
   size_t bytes;
 };
+
+// Where a pointer lives: pinned (page-locked, device-mapped) host memory is
+// read and written by device code through the same pointer; pageable host
+// memory cannot be.
+enum { kMemDevice = 0, kMemPinnedHost = 1, kMemPageable = 2 };
+static int memory_kind(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kMemDevice;
+  }
+  if (a.type == cudaMemoryTypeHost) return kMemPinnedHost;
+  if (a.type == cudaMemoryTypeUnregistered) return kMemPageable;
+  return kMemDevice;
+}
 
 static LayerWs carve_layer(void* ws, const moe_layer_weights* w, int T) {
   Carve c{static_cast<uint8_t*>(ws), 0, 0};
@@ -52,6 +68,7 @@ static LayerWs carve_layer(void* ws, const moe_layer_weights* w, int T) {
   L.s_off = c.take<int32_t>(2);
   L.s_y = w->s_gate ? c.take<float>((size_t)T * w->d) : nullptr;
   L.row_max = c.take<float>(T > 0 ? T : 1);
+  L.xdev = c.take<float>((size_t)(T > 0 ? T : 1) * w->d);
   L.bytes = align_up(c.used, 256);
   return L;
 }
@@ -107,17 +124,32 @@ int moe_layer_forward_ex(const moe_layer_weights* w, const float* x, const float
   SmallDispatch sd = {L.offsets, L.perm, L.inv, L.status, n_active, active, goff, coff, done,
                       mg, rpc};
   const bool fused = router_fuses_dispatch(T, w->E, w->k);
+  // x (and out) may be pinned host memory: the router's first pass then
+  // reads x over the bus and leaves the device copy every later kernel reads
+  // (no separate host-to-device copy); out is written in place by the combine
+  const int xk = memory_kind(x);
+  MOE_REQUIRE(xk != kMemPageable && memory_kind(out) != kMemPageable, MOE_ERR_INVALID,
+              "x and out must be device or pinned host memory");
+  const bool x_host = xk == kMemPinnedHost;
+  const float* xe = x;
+  float* xcopy = nullptr;
+  if (x_host) {
+    xe = L.xdev;
+    if (router_x) MOE_CUDA(cudaMemcpyAsync(L.xdev, x, (size_t)T * w->d * sizeof(float),
+                                           cudaMemcpyDefault, s));
+    else xcopy = L.xdev;
+  }
   // the router's per-row maxima double as the experts' activation scaling,
   // so they are only taken from the router when it reads the experts' input
   MOE_CHECK(launch_router(router_x ? router_x : x, w->gate_w, w->bias, T, w->d, w->E, w->k,
                           w->router_layout, w->mode, ids, wts, L.router_ws, L.router_bytes, s,
-                          router_x ? nullptr : L.row_max, fused ? &sd : nullptr));
+                          router_x ? nullptr : L.row_max, fused ? &sd : nullptr, xcopy));
   const float* row_max = router_x ? nullptr : L.row_max;
   if (!fused)
     MOE_CHECK(launch_dispatch_planned(ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
                                       n_active, active, goff, coff, done, mg, rpc,
                                       L.disp_scratch, s));
-  MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, x, L.perm,
+  MOE_CHECK(run_experts(w->w_gate, w->w_up, w->w_down, w->qtype, L.offsets, w->E, P, xe, L.perm,
                         w->k, w->d, w->F, L.y, nullptr, L.exp_ws, L.exp_bytes, s, L.status,
                         row_max, true, 0, w->opts));
   if (w->s_gate) {
@@ -127,7 +159,7 @@ int moe_layer_forward_ex(const moe_layer_weights* w, const float* x, const float
     }
     MOE_CHECK(check_launch("fill_offsets"));
     const moe_expert_opts so = shared_expert_opts(w->opts);
-    MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
+    MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, xe,
                           nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.exp_ws, L.exp_bytes, s,
                           L.status, row_max, false, 0, &so));
   }

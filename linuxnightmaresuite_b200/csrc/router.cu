@@ -86,7 +86,7 @@ template <int TT>
 __global__ void __launch_bounds__(kRouterThreads)
 router_gemv_kernel(const float* __restrict__ x, const float* __restrict__ G, int T, int d, int E,
                    int layout, int rows_per_slice, float* __restrict__ part,
-                   float* __restrict__ pmax) {
+                   float* __restrict__ pmax, float* __restrict__ xcopy) {
   // pass 2 may start (and wait) while this grid runs
   pdl_trigger();
   __shared__ __align__(16) float xs[kRouterChunk][TT];   // x chunk, token-minor
@@ -111,8 +111,13 @@ router_gemv_kernel(const float* __restrict__ x, const float* __restrict__ G, int
       for (int v = tid; v < TT * (kRouterChunk / 4); v += kRouterThreads) {
         const int tl = v % TT, q = v / TT;
         float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (tl < nt && 4 * q < rows)
+        if (tl < nt && 4 * q < rows) {
           f = __ldg(reinterpret_cast<const float4*>(x + (size_t)(t0 + tl) * d + i0) + q);
+          // x in host memory: this pass's reads are the layer's only ones,
+          // and it leaves the device copy the later kernels read
+          if (xcopy && eg == 0)
+            reinterpret_cast<float4*>(xcopy + (size_t)(t0 + tl) * d + i0)[q] = f;
+        }
         xs[4 * q + 0][tl] = f.x;
         xs[4 * q + 1][tl] = f.y;
         xs[4 * q + 2][tl] = f.z;
@@ -305,7 +310,7 @@ __device__ __forceinline__ void select_warp(float (&v)[NJ], int E, int k, int mo
 __global__ void __launch_bounds__(kRgThreads)
 router_gemm_kernel(const float* __restrict__ x, const float* __restrict__ G, int T, int d, int E,
                    int layout, int rows_per_slice, float* __restrict__ part,
-                   float* __restrict__ pmax) {
+                   float* __restrict__ pmax, float* __restrict__ xcopy) {
   pdl_trigger();
   __shared__ __align__(16) float xs[2][kRgK][kRgTT + 8];
   __shared__ __align__(16) float gs[2][kRgK][kRgTE];
@@ -321,6 +326,8 @@ router_gemm_kernel(const float* __restrict__ x, const float* __restrict__ G, int
       const int t = t0 + xt, i = i0 + xk;
       xr = (t < T && i < r1) ? __ldg(reinterpret_cast<const float4*>(x + (size_t)t * d + i))
                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (xcopy && blockIdx.z == 0 && t < T && i < r1)   // device copy of host x
+        *reinterpret_cast<float4*>(xcopy + (size_t)t * d + i) = xr;
       xm = fmaxf(xm, fmaxf(fmaxf(fabsf(xr.x), fabsf(xr.y)), fmaxf(fabsf(xr.z), fabsf(xr.w))));
     }
 #pragma unroll
@@ -560,7 +567,7 @@ static int launch_router_passes(const float* x, const float* gate_w, const float
                                 int d, int E, int k, int layout, int mode, int32_t* ids,
                                 float* weights, float* part, float* pmax, float* row_max,
                                 cudaStream_t s, size_t max_parts = ~(size_t)0,
-                                const SmallDispatch* sd = nullptr) {
+                                const SmallDispatch* sd = nullptr, float* xcopy = nullptr) {
   const RouterPlan p = router_plan(T, d, E, max_parts);
   const size_t red = (size_t)kRouterWarps * p.tt * 128 * sizeof(float);
   {
@@ -582,25 +589,26 @@ static int launch_router_passes(const float* x, const float* gate_w, const float
   if (p.gemm) {
     ::moe::ProfScope _prof(MOE_K_ROUTER, s);
     const dim3 g3(p.nds, p.tiles, (E + kRgTE - 1) / kRgTE);
-    router_gemm_kernel<<<g3, kRgThreads, 0, s>>>(x, gate_w, T, d, E, layout, p.rows, part, pm);
+    router_gemm_kernel<<<g3, kRgThreads, 0, s>>>(x, gate_w, T, d, E, layout, p.rows, part, pm,
+                                                  xcopy);
   } else {
     ::moe::ProfScope _prof(MOE_K_ROUTER, s);
     switch (p.tt) {
       case 16:
         router_gemv_kernel<16><<<grid, kRouterThreads, red, s>>>(x, gate_w, T, d, E, layout,
-                                                                 p.rows, part, pm);
+                                                                 p.rows, part, pm, xcopy);
         break;
       case 8:
         router_gemv_kernel<8><<<grid, kRouterThreads, red, s>>>(x, gate_w, T, d, E, layout,
-                                                                p.rows, part, pm);
+                                                                p.rows, part, pm, xcopy);
         break;
       case 4:
         router_gemv_kernel<4><<<grid, kRouterThreads, red, s>>>(x, gate_w, T, d, E, layout,
-                                                                p.rows, part, pm);
+                                                                p.rows, part, pm, xcopy);
         break;
       default:
         router_gemv_kernel<1><<<grid, kRouterThreads, red, s>>>(x, gate_w, T, d, E, layout,
-                                                                p.rows, part, pm);
+                                                                p.rows, part, pm, xcopy);
     }
   }
   MOE_CHECK(check_launch("router_gemv"));
@@ -661,7 +669,7 @@ static int check_router_args(const float* x, const float* gate_w, int T, int d, 
 int launch_router(const float* x, const float* gate_w, const float* bias, int T, int d, int E,
                   int k, int layout, int mode, int32_t* ids, float* weights, void* workspace,
                   size_t workspace_bytes, cudaStream_t stream, float* row_max,
-                  const SmallDispatch* sd) {
+                  const SmallDispatch* sd, float* xcopy) {
   MOE_REQUIRE(T >= 0, MOE_ERR_INVALID, "T must be >= 0");
   MOE_REQUIRE(!sd || router_fuses_dispatch(T, E, k), MOE_ERR_INVALID,
               "the fused dispatch serves one token");
@@ -676,7 +684,7 @@ int launch_router(const float* x, const float* gate_w, const float* bias, int T,
   float* pmax = reinterpret_cast<float*>(
       base + align_up(router_part_floats(p, T, E) * sizeof(float), 256));
   return launch_router_passes(x, gate_w, bias, T, d, E, k, layout, mode, ids, weights, part,
-                              pmax, row_max, stream, ~(size_t)0, sd);
+                              pmax, row_max, stream, ~(size_t)0, sd, xcopy);
 }
 
 bool router_fuses_dispatch(int T, int E, int k) {
@@ -699,7 +707,7 @@ int moe_router(const float* x, const float* gate_w, const float* bias, int T, in
                size_t workspace_bytes, moe_stream_t stream) {
   return moe::launch_router(x, gate_w, bias, T, d, E, k, layout, mode, ids, weights, workspace,
                             workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr,
-                            nullptr);
+                            nullptr, nullptr);
 }
 
 }  // extern "C"

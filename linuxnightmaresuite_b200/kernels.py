@@ -67,9 +67,10 @@ def _ptr(t: Optional[torch.Tensor]):
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
-def _need(t: torch.Tensor, dtype, name: str) -> torch.Tensor:
-    if not isinstance(t, torch.Tensor) or not t.is_cuda:
-        raise TypeError(f"{name} must be a CUDA tensor")
+def _need(t: torch.Tensor, dtype, name: str, pinned_ok: bool = False) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not (t.is_cuda or (pinned_ok and t.is_pinned())):
+        raise TypeError(f"{name} must be a CUDA tensor" + (" or pinned host memory"
+                                                          if pinned_ok else ""))
     if t.dtype != dtype:
         raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
     if not t.is_contiguous():
@@ -288,16 +289,22 @@ def layer_forward(lw: LayerWeights, x: torch.Tensor, out: Optional[torch.Tensor]
                   ids: Optional[torch.Tensor] = None,
                   weights: Optional[torch.Tensor] = None,
                   router_x: Optional[torch.Tensor] = None) -> torch.Tensor:
-    _need(x, torch.float32, "x")
+    """x and out may be pinned host tensors: the layer then reads x and writes
+    out over the bus from its own kernels (no separate copies)."""
+    _need(x, torch.float32, "x", pinned_ok=True)
+    if out is not None:
+        _need(out, torch.float32, "out", pinned_ok=True)
     if router_x is not None:
         _need(router_x, torch.float32, "router_x")
         if router_x.shape != x.shape:
             raise ValueError("router_x must have the shape of x")
     T = x.shape[0]
     if out is None:
-        out = torch.empty_like(x)
+        out = torch.empty_like(x) if x.is_cuda else torch.empty(x.shape, dtype=x.dtype,
+                                                                 pin_memory=True)
+    dev = x.device if x.is_cuda else torch.device("cuda", torch.cuda.current_device())
     if ws is None:
-        ws = workspace(lw.workspace_bytes(T), x.device)
+        ws = workspace(lw.workspace_bytes(T), dev)
         ws[:256].zero_()
     call("moe_layer_forward_ex", ctypes.byref(lw.c), _ptr(x), _ptr(router_x), T, _ptr(out),
          _ptr(residual), _ptr(ids), _ptr(weights), _ptr(ws), ws.numel(), _stream())

@@ -283,13 +283,17 @@ class MoELayer:
     def forward_batch(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
                       out: Optional[torch.Tensor] = None, return_routing: bool = False,
                       router_x: Optional[torch.Tensor] = None):
-        """(T, d) tokens on the device; ``router_x`` (T, d) is what the router
-        reads when it differs from the experts' input (gemma4)."""
+        """(T, d) tokens on the device, or in pinned host memory (with ``out``
+        then also pinned host memory or on the device): the layer's kernels
+        read and write host tensors over the bus themselves.  ``router_x``
+        (T, d) is what the router reads when it differs from the experts'
+        input (gemma4)."""
         T = x.shape[0]
         ids = weights = None
         if return_routing:
-            ids = torch.empty((T, self.router.top_k), dtype=torch.int32, device=x.device)
-            weights = torch.empty((T, self.router.top_k), dtype=torch.float32, device=x.device)
+            dev = self.router.device
+            ids = torch.empty((T, self.router.top_k), dtype=torch.int32, device=dev)
+            weights = torch.empty((T, self.router.top_k), dtype=torch.float32, device=dev)
         out = K.layer_forward(self.weights, x, out=out, residual=residual,
                               ws=self._workspace(T), ids=ids, weights=weights, router_x=router_x)
         return (out, ids, weights) if return_routing else out
