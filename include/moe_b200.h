@@ -288,7 +288,12 @@ int moe_layer_workspace_bytes(const moe_layer_weights* w, int T, size_t* bytes);
 
 /* MoELayer.forward (moe_forward.py:154-174) for T tokens:
  * router -> dispatch -> grouped experts -> combine (+ shared expert).
- *   out (T, d) f32; must not alias x.
+ *   x (T, d) f32 in device memory or in pinned (page-locked) host memory: the
+ *   router's first pass then reads it over the bus and leaves a device copy in
+ *   the workspace for the later kernels (no separate host-to-device copy).
+ *   Pageable host memory is rejected (MOE_ERR_INVALID).
+ *   out (T, d) f32, device or pinned host memory (written in place by the
+ *   combine); must not alias x.
  *   residual (T, d) or NULL: added to the output (the transformer residual,
  *   moe_forward.py:359 `x = x + ffn_out`); may alias out.
  *   ids_out / weights_out (T, k) or NULL: receive the routing decisions.

@@ -73,12 +73,25 @@ class MoEEngineAdapter:
     # ------------------------------------------------------------- calls
     def moe_ffn(self, xn, layer_idx: int, weights=None) -> np.ndarray:
         """GPUStreamEngine._moe_ffn: xn (dim,) or (1, dim) host f32 ->
-        (1, dim) f32 (softmax over all experts -> top-k -> renormalised)."""
+        (1, dim) f32 (softmax over all experts -> top-k -> renormalised).
+        The token and the result go through pinned host buffers that the
+        layer's kernels read and write themselves."""
         lay = self._routed_layer(layer_idx)
-        x = torch.from_numpy(np.ascontiguousarray(np.asarray(xn, dtype=np.float32)
-                                                  .reshape(1, -1))).to(self.device)
+        d = self._dim(lay)
+        xin, xout = self._pinned(d)
+        xin.numpy()[0] = np.asarray(xn, dtype=np.float32).reshape(-1)
+        with torch.cuda.device(self.device):
+            lay.forward_batch(xin, out=xout)
+            torch.cuda.current_stream().synchronize()
         self.calls += 1
-        return lay.forward_batch(x).cpu().numpy().reshape(1, -1)
+        return xout.numpy().copy()
+
+    def _pinned(self, d: int):
+        buf = getattr(self, "_pin", None)
+        if buf is None or buf[0].shape[1] != d:
+            self._pin = buf = (torch.empty((1, d), dtype=torch.float32, pin_memory=True),
+                               torch.empty((1, d), dtype=torch.float32, pin_memory=True))
+        return buf
 
     def moe_ffn_gpu(self, xn_ptr: int, layer_idx: int, weights=None, out_ptr: Optional[int] = None):
         """GPUStreamEngine._moe_ffn_gpu: reads dim f32 at device address
