@@ -429,7 +429,7 @@ def build(wl: Workload, seed: int, rank: int, world: int, dev) -> Built:
     data.w_gate = data.w_up = data.w_down = None
     torch.cuda.synchronize()
     return Built(wl, step, x_np, T, [data], lambda: int(layer.device_status()), close,
-                 routing_stats, host_io=world == 1)
+                 routing_stats, host_io=True)
 
 
 def measure(wl: Workload, args, steps: int, warmup: int, rank: int, world: int, local: int,

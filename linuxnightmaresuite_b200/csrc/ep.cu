@@ -354,6 +354,7 @@ struct EpWs {
   int32_t* row_map;
   uint8_t* exp_ws;
   size_t exp_bytes;
+  float* xdev;         // device copy of x when the caller's x is in host memory
   int32_t* s_off;      // shared expert: [0, T]
   float* s_y;          // shared expert output (T, d)
   uint8_t* s_ws;       // shared expert workspace (its own plan and buffers)
@@ -380,6 +381,7 @@ static EpWs carve_ep(void* ws, const moe_layer_weights* w, int W, int T) {
   L.row_map = c.take<int32_t>(R);
   experts_workspace_hint(R, (int)P, El, w->d, w->F, &L.exp_bytes);
   L.exp_ws = c.take<uint8_t>(L.exp_bytes);
+  L.xdev = c.take<float>((size_t)T * w->d);
   L.s_off = c.take<int32_t>(2);
   L.s_y = w->s_gate ? c.take<float>((size_t)T * w->d) : nullptr;
   L.s_bytes = 0;
@@ -477,15 +479,22 @@ int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* con
   a.cap = P;
   a.d = w->d;
   a.epoch = epoch;
+  // x may be pinned host memory: the router's first pass reads it over the
+  // bus and leaves the device copy the send (and the shared expert) read
+  const int xk = memory_kind(x);
+  MOE_REQUIRE(xk != kMemPageable && memory_kind(out) != kMemPageable, MOE_ERR_INVALID,
+              "x and out must be device or pinned host memory");
+  const float* xe = xk == kMemPinnedHost ? L.xdev : x;
   if (phases & MOE_EP_PHASE_SEND) {
     MOE_CHECK(launch_router(x, w->gate_w, w->bias, T, w->d, w->E, w->k, w->router_layout,
-                            w->mode, L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr));
+                            w->mode, L.ids, L.wts, L.router_ws, L.router_bytes, s, nullptr,
+                            nullptr, xk == kMemPinnedHost ? L.xdev : nullptr));
     MOE_CHECK(launch_dispatch_planned(L.ids, T, w->k, w->E, L.offsets, L.perm, L.inv, L.status,
                                       nullptr, nullptr, nullptr, nullptr, nullptr, 0, 1,
                                       L.disp_scratch, s));
     {
       ::moe::ProfScope _prof(MOE_K_EP_SEND, s);
-      ep_send_kernel<<<(P + 7) / 8, 256, 0, s>>>(x, L.perm, w->k, L.offsets, P, a);
+      ep_send_kernel<<<(P + 7) / 8, 256, 0, s>>>(xe, L.perm, w->k, L.offsets, P, a);
     }
     MOE_CHECK(check_launch("ep_send"));
   }
@@ -522,7 +531,7 @@ int moe_ep_forward_phases(const moe_layer_weights* w, int W, int rank, void* con
       }
       MOE_CHECK(check_launch("ep_fill_two"));
       const moe_expert_opts so = shared_expert_opts(w->opts);
-      MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, x,
+      MOE_CHECK(run_experts(w->s_gate, w->s_up, w->s_down, w->shared_qtype, L.s_off, 1, T, xe,
                             nullptr, 1, w->d, w->Fs, L.s_y, nullptr, L.s_ws, L.s_bytes, s,
                             L.status, nullptr, false, T, &so));
     }

@@ -52,6 +52,21 @@ void experts_plan_arrays(void* ws, int rows, int E, int d, int F, int** n_active
 int launch_combine(const float* y, const int32_t* inv_perm, const float* w, const float* shared,
                    const float* residual, int T, int k, int d, float* out, cudaStream_t s);
 
+// Where a pointer lives: pinned (page-locked, device-mapped) host memory is
+// read and written by device code through the same pointer; pageable host
+// memory cannot be.
+enum { kMemDevice = 0, kMemPinnedHost = 1, kMemPageable = 2 };
+inline int memory_kind(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return kMemDevice;
+  }
+  if (a.type == cudaMemoryTypeHost) return kMemPinnedHost;
+  if (a.type == cudaMemoryTypeUnregistered) return kMemPageable;
+  return kMemDevice;
+}
+
 // The shared expert's options: the routed experts' activation, one matrix
 // per stack, no down scale.
 inline moe_expert_opts shared_expert_opts(const moe_expert_opts* routed) {

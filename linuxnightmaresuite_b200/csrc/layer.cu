@@ -31,21 +31,6 @@ struct LayerWs {
   size_t bytes;
 };
 
-// Where a pointer lives: pinned (page-locked, device-mapped) host memory is
-// read and written by device code through the same pointer; pageable host
-// memory cannot be.
-enum { kMemDevice = 0, kMemPinnedHost = 1, kMemPageable = 2 };
-static int memory_kind(const void* p) {
-  cudaPointerAttributes a;
-  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-    (void)cudaGetLastError();
-    return kMemDevice;
-  }
-  if (a.type == cudaMemoryTypeHost) return kMemPinnedHost;
-  if (a.type == cudaMemoryTypeUnregistered) return kMemPageable;
-  return kMemDevice;
-}
-
 static LayerWs carve_layer(void* ws, const moe_layer_weights* w, int T) {
   Carve c{static_cast<uint8_t*>(ws), 0, 0};
   LayerWs L;

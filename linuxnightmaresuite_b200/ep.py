@@ -233,13 +233,17 @@ class EPMoELayer:
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                 residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One expert-parallel step for this rank's tokens x (T, d); every rank
-        calls it with the same T.  Device work only."""
+        calls it with the same T.  x and out may be pinned host tensors (the
+        layer's kernels read and write them over the bus)."""
         K, ex = self.K, self.exchange
-        K._need(x, torch.float32, "x")
+        K._need(x, torch.float32, "x", pinned_ok=True)
+        if out is not None:
+            K._need(out, torch.float32, "out", pinned_ok=True)
         T = int(x.shape[0])
         ex.ensure(self.lw, T)
         if out is None:
-            out = torch.empty_like(x)
+            out = torch.empty_like(x) if x.is_cuda else torch.empty(x.shape, dtype=x.dtype,
+                                                                     pin_memory=True)
         ex.epoch += 1
         self._lib.call("moe_ep_forward", ctypes.byref(self.lw.c), self.world, self.rank,
                        ctypes.c_void_p(ex.peers.data_ptr()), ctypes.c_void_p(ex.window),
@@ -340,12 +344,13 @@ class EPLocalRanks:
             raise ValueError(f"{len(xs)} token blocks for {W} ranks")
         T = int(xs[0].shape[0])
         for x in xs:
-            K._need(x, torch.float32, "x")
+            K._need(x, torch.float32, "x", pinned_ok=True)
             if int(x.shape[0]) != T:
                 raise ValueError("every rank must bring the same number of tokens")
         self._ensure(T)
         if outs is None:
-            outs = [torch.empty_like(x) for x in xs]
+            outs = [torch.empty_like(x) if x.is_cuda else
+                    torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs]
         res = residuals if residuals is not None else [None] * W
         self.epoch += 1
         for phase in (_lib.MOE_EP_PHASE_SEND, _lib.MOE_EP_PHASE_SERVE, _lib.MOE_EP_PHASE_COMBINE):

@@ -8,6 +8,7 @@ import torch
 
 from linuxnightmaresuite_b200 import moe_forward as M
 from linuxnightmaresuite_b200 import synth
+from linuxnightmaresuite_b200.ep import EPLocalRanks
 
 pytestmark = pytest.mark.gpu
 
@@ -41,3 +42,22 @@ def test_pageable_host_tokens_rejected():
                                    cfg.top_k, mode=cfg.route_mode, device=dev)
     with pytest.raises(TypeError):
         layer.forward_batch(torch.from_numpy(np.ascontiguousarray(data.x[:4])))
+
+
+def test_expert_parallel_host_tokens_match_device_tokens():
+    """The expert-parallel layer (its ranks emulated on one GPU): pinned host
+    tokens and outputs give the device tensors' result bit for bit."""
+    dev = torch.device("cuda:0")
+    W, T = 2, 16
+    cfg = synth.MoEConfig("host_io_ep", 512, 16, 4, 256, T * W, synth.QTYPE_Q8_0, 0.002)
+    data = synth.make_layer_device(cfg, 5, T * W, 0, cfg.n_experts, dev)
+    ep = EPLocalRanks(data.gate_w, data.w_gate, data.w_up, data.w_down, cfg.qtype, cfg.top_k, W,
+                      mode=cfg.route_mode, bias=data.bias, device=dev)
+    xs = [np.ascontiguousarray(data.x[r * T:(r + 1) * T]) for r in range(W)]
+    ref = [o.cpu().numpy() for o in ep.forward([torch.from_numpy(x).to(dev) for x in xs])]
+    got = ep.forward([torch.from_numpy(x).pin_memory() for x in xs])
+    torch.cuda.synchronize()
+    for g, r in zip(got, ref):
+        assert not g.is_cuda
+        np.testing.assert_array_equal(g.numpy(), r)
+    assert ep.device_status() == [0] * W
