@@ -68,13 +68,25 @@ enum { MOE_ACT_SWIGLU = 0, MOE_ACT_GEGLU_TANH = 1 };
  *                   (F, d) matrix, stride = two matrices
  *                   (nightmare_stream.py:3361-3441)
  *   down_scale      (E_local,) f32 per-expert factor on the down projection
- *                   (ffn_down_exps.scale, nightmare_stream.py:4307-4330), or NULL */
+ *                   (ffn_down_exps.scale, nightmare_stream.py:4307-4330), or NULL
+ *   kernels         MOE_KERNELS_*: which kernel family runs packed Q4_0 / Q8_0
+ *                   experts; 0 = chosen from the routed rows per active expert
+ *   chunk_rows      block-scale family: rows per work unit (8, 16, 32 or 64;
+ *                   0 = chosen from the routed rows per active expert) */
 typedef struct moe_expert_opts {
   int act;
   int down_qtype;
   size_t gate_up_stride;
   const float* down_scale;
+  int kernels;
+  int chunk_rows;
 } moe_expert_opts;
+
+/* Kernel families for packed experts: mma.sync GEMVs (a few rows per expert),
+ * block-scale tcgen05 GEMMs (exact integer weights, per-block scaling; mid-size
+ * groups), split-operand tcgen05 GEMMs (large groups). */
+enum { MOE_KERNELS_AUTO = 0, MOE_KERNELS_GEMV = 1, MOE_KERNELS_BLOCKSCALE = 2,
+       MOE_KERNELS_SPLIT_GEMM = 3 };
 
 enum { MOE_ROUTE_TOPK_SOFTMAX = 0, MOE_ROUTE_SOFTMAX_TOPK_RENORM = 1 };
 

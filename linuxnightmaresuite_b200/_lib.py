@@ -27,6 +27,7 @@ MOE_Q4_K = 12
 MOE_Q6_K = 14
 MOE_ACT_SWIGLU = 0
 MOE_ACT_GEGLU_TANH = 1
+MOE_KERNELS_AUTO, MOE_KERNELS_GEMV, MOE_KERNELS_BLOCKSCALE, MOE_KERNELS_SPLIT_GEMM = 0, 1, 2, 3
 MOE_ROUTE_TOPK_SOFTMAX = 0
 MOE_ROUTE_SOFTMAX_TOPK_RENORM = 1
 MOE_ROUTER_D_E = 0
@@ -45,7 +46,8 @@ cf = ctypes.c_float
 
 class MoEExpertOpts(ctypes.Structure):
     """Mirror of ``moe_expert_opts``."""
-    _fields_ = [("act", ci), ("down_qtype", ci), ("gate_up_stride", csz), ("down_scale", vp)]
+    _fields_ = [("act", ci), ("down_qtype", ci), ("gate_up_stride", csz), ("down_scale", vp),
+                ("kernels", ci), ("chunk_rows", ci)]
 
 
 class MoELayerWeights(ctypes.Structure):

@@ -940,23 +940,59 @@ int run_experts_tc(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_
                    const int32_t* y_rows, void* ws, size_t ws_bytes, int* status,
                    const moe_expert_opts* opts, cudaStream_t s);
 
-// Rows per active expert from which the tcgen05 GEMM path is used.
+size_t bs_workspace(int rows, int E, int d, int F);
+bool bs_supported(int rows, int E, int d, int F);
+int run_experts_bs(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_down, int qtype,
+                   const int32_t* offsets, int E, int rows, const float* x, const int32_t* x_rows,
+                   int x_div, const float* x_row_max, int d, int F, float* y,
+                   const int32_t* y_rows, void* ws, size_t ws_bytes, int* status,
+                   const moe_expert_opts* opts, int rb, cudaStream_t s);
+
+// Routed rows per active expert from which the split-operand tcgen05 GEMMs
+// are used, and from which the block-scale tcgen05 GEMMs are (below that).
 #ifndef MOE_TC_MIN_MEAN_ROWS
 #define MOE_TC_MIN_MEAN_ROWS 64
 #endif
+#ifndef MOE_BS_MIN_MEAN_ROWS
+#define MOE_BS_MIN_MEAN_ROWS MOE_TC_MIN_MEAN_ROWS
+#endif
 constexpr int kTcMinMeanRows = MOE_TC_MIN_MEAN_ROWS;
+constexpr int kBsMinMeanRows = MOE_BS_MIN_MEAN_ROWS;
+
+static int mean_rows_per_expert(int rows, int E) {
+  const int active = rows < E ? rows : E;
+  return active > 0 ? rows / active : 0;
+}
 
 static bool use_tc(int rows, int E, int d, int F) {
-  const int active = rows < E ? rows : E;
-  return active > 0 && rows / active >= kTcMinMeanRows && tc_supported(rows, E, d, F);
+  return mean_rows_per_expert(rows, E) >= kTcMinMeanRows && tc_supported(rows, E, d, F);
+}
+
+// The kernel family of a call with `hint` expected rows (opts may pin it).
+static int expert_family(int rows, int hint, int E, int d, int F, const moe_expert_opts* opts) {
+  if (opts && opts->kernels != MOE_KERNELS_AUTO) return opts->kernels;
+  if (use_tc(hint, E, d, F)) return MOE_KERNELS_SPLIT_GEMM;
+  if (mean_rows_per_expert(hint, E) >= kBsMinMeanRows && bs_supported(rows, E, d, F))
+    return MOE_KERNELS_BLOCKSCALE;
+  return MOE_KERNELS_GEMV;
+}
+
+// Block-scale chunk rows: about the busiest expert's rows at this mean, so
+// most experts take one chunk (each chunk streams its expert's weights once).
+static int bs_chunk_rows(int hint, int E, const moe_expert_opts* opts) {
+  if (opts && opts->chunk_rows) return opts->chunk_rows;
+  const int m = mean_rows_per_expert(hint, E);
+  return m <= 5 ? 8 : m <= 10 ? 16 : m <= 22 ? 32 : 64;
 }
 
 // rows: the most rows a call may see (buffers); rows_hint: the rows it is
-// expected to see, which picks the GEMV or the tensor-core path.
+// expected to see, which picks the kernel family.  Every family's buffers are
+// included, so options may pin any of them.
 int experts_workspace_hint(int rows, int rows_hint, int E, int d, int F, size_t* bytes) {
   size_t a = carve_experts(nullptr, rows, E, d, F).bytes;
-  if (use_tc(rows_hint > 0 ? rows_hint : rows, E, d, F))
-    a = std::max(a, tc_workspace(rows, E, d, F));
+  if (bs_supported(rows, E, d, F)) a = std::max(a, bs_workspace(rows, E, d, F));
+  if (tc_supported(rows, E, d, F)) a = std::max(a, tc_workspace(rows, E, d, F));
+  (void)rows_hint;
   *bytes = a;
   return MOE_OK;
 }
@@ -1217,9 +1253,16 @@ int run_experts(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_dow
   MOE_REQUIRE(x_div > 0, MOE_ERR_INVALID, "x_rows_div must be positive");
   MOE_REQUIRE(((uintptr_t)w_gate | (uintptr_t)w_up | (uintptr_t)w_down | (uintptr_t)x) % 16 == 0,
               MOE_ERR_INVALID, "weights and activations must be 16-byte aligned");
-  if (use_tc(rows_hint > 0 ? rows_hint : rows, E, d, F))
+  const int hint = rows_hint > 0 ? rows_hint : rows;
+  const int family = expert_family(rows, hint, E, d, F, opts);
+  if (family == MOE_KERNELS_SPLIT_GEMM)
     return run_experts_tc(w_gate, w_up, w_down, qtype, offsets, E, rows, x, x_rows, x_div,
                           x_row_max, d, F, y, y_rows, ws, ws_bytes, status, opts, s);
+  if (family == MOE_KERNELS_BLOCKSCALE)
+    return run_experts_bs(w_gate, w_up, w_down, qtype, offsets, E, rows, x, x_rows, x_div,
+                          x_row_max, d, F, y, y_rows, ws, ws_bytes, status, opts,
+                          bs_chunk_rows(hint, E, opts), s);
+  MOE_REQUIRE(family == MOE_KERNELS_GEMV, MOE_ERR_INVALID, "unknown kernel family %d", family);
   ExpertsWs w = carve_experts(ws, rows, E, d, F);
   if (status) w.status = status;
   MOE_REQUIRE(ws_bytes >= w.bytes, MOE_ERR_WORKSPACE, "experts workspace %zu < %zu", ws_bytes,

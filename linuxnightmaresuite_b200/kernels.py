@@ -22,6 +22,10 @@ QTYPE_Q4_K = _lib.MOE_Q4_K
 QTYPE_Q6_K = _lib.MOE_Q6_K
 ACT_SWIGLU = _lib.MOE_ACT_SWIGLU
 ACT_GEGLU_TANH = _lib.MOE_ACT_GEGLU_TANH
+KERNELS_AUTO = _lib.MOE_KERNELS_AUTO
+KERNELS_GEMV = _lib.MOE_KERNELS_GEMV
+KERNELS_BLOCKSCALE = _lib.MOE_KERNELS_BLOCKSCALE
+KERNELS_SPLIT_GEMM = _lib.MOE_KERNELS_SPLIT_GEMM
 # GGML type -> (weights per block, bytes per block), dequant_fast.py:723-754
 BLOCK_GEOMETRY = {QTYPE_F32: (1, 4), QTYPE_Q4_0: (32, 18), QTYPE_Q5_1: (32, 24),
                   QTYPE_Q8_0: (32, 34), QTYPE_Q4_K: (256, 144), QTYPE_Q6_K: (256, 210)}
@@ -44,15 +48,18 @@ def packed_path(qtype: int, down_qtype: int) -> bool:
 
 class ExpertOpts:
     """Expert variant (``moe_expert_opts``): activation, down matrix type,
-    gate/up stride of a fused stack, per-expert down scale (device f32)."""
+    gate/up stride of a fused stack, per-expert down scale (device f32), and
+    the kernel family (``KERNELS_*``, 0 = automatic) with its chunk rows."""
 
     def __init__(self, act: int = ACT_SWIGLU, down_qtype: int = 0, gate_up_stride: int = 0,
-                 down_scale: Optional[torch.Tensor] = None):
+                 down_scale: Optional[torch.Tensor] = None, kernels: int = 0,
+                 chunk_rows: int = 0):
         if down_scale is not None:
             _need(down_scale, torch.float32, "down_scale")
         self.down_scale = down_scale
         self.c = _lib.MoEExpertOpts(act, down_qtype, gate_up_stride,
-                                    0 if down_scale is None else down_scale.data_ptr())
+                                    0 if down_scale is None else down_scale.data_ptr(),
+                                    kernels, chunk_rows)
 
     @property
     def ref(self):
