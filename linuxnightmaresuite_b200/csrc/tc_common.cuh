@@ -192,11 +192,13 @@ __device__ __forceinline__ void store_packed_half(const PackedHalf<QT>& p, int l
   }
 }
 
-// lane 0 waits, the warp follows its verdict
+// Every lane polls (the phase, once complete, stays complete until the next
+// one can start) and the warp follows the vote; measured faster on B200 than
+// lane 0 polling while the other lanes wait on a shuffle (prefill gate/up
+// 1.08 -> 1.03 ms).
 __device__ __forceinline__ bool warp_mbar_wait(uint64_t* bar, uint32_t parity, int lane) {
-  bool ok = true;
-  if (lane == 0) ok = mbar_wait(bar, parity);
-  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  (void)lane;
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity) ? 1 : 0) != 0;
 }
 
 __device__ __forceinline__ void tc_fail(volatile int* flag, int* status) {
