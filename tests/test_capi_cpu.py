@@ -68,3 +68,18 @@ def test_argument_validation_without_gpu(lib):
     assert sz.value == 128 * 704 * 88 * 18
     assert lib.moe_experts_workspace_bytes(512, 128, 2816, 704, ctypes.byref(sz)) == 0
     assert sz.value > 0
+
+
+def test_expert_opts_mirror_matches_header():
+    """The ctypes mirror of moe_expert_opts has the header's fields in order,
+    and the kernel-family constants match the header's enum."""
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    body = re.search(r"typedef struct moe_expert_opts \{(.*?)\} moe_expert_opts;", src, re.S)
+    fields = re.findall(r"(\w+)\s*;", body.group(1))
+    assert fields == [f[0] for f in _lib.MoEExpertOpts._fields_]
+    enum = re.search(r"enum \{ (MOE_KERNELS_AUTO[^}]*)\}", src, re.S).group(1)
+    for name, value in re.findall(r"(MOE_KERNELS_\w+)\s*=\s*(\d+)", enum):
+        assert getattr(_lib, name) == int(value), name
+    from linuxnightmaresuite_b200 import kernels as K
+    o = K.ExpertOpts(kernels=K.KERNELS_BLOCKSCALE, chunk_rows=16)
+    assert (o.c.kernels, o.c.chunk_rows, o.c.act) == (_lib.MOE_KERNELS_BLOCKSCALE, 16, 0)
