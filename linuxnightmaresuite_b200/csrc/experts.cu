@@ -949,7 +949,10 @@ int run_experts_bs(const uint8_t* w_gate, const uint8_t* w_up, const uint8_t* w_
                    const moe_expert_opts* opts, int rb, cudaStream_t s);
 
 // Routed rows per active expert from which the split-operand tcgen05 GEMMs
-// are used, and from which the block-scale tcgen05 GEMMs are (below that).
+// are used, and from which the block-scale tcgen05 GEMMs would be (below
+// that).  The block-scale threshold defaults to the split one, so automatic
+// selection never picks them: measured on B200 they trail the GEMVs at every
+// group size tried (4-32 rows per expert); options can still pin them.
 #ifndef MOE_TC_MIN_MEAN_ROWS
 #define MOE_TC_MIN_MEAN_ROWS 64
 #endif
