@@ -281,7 +281,7 @@ struct StripStage {
 template <int QT, int MODE, int STAGES, int STAGE_BYTES, int B_OFF, int B_PLANE>
 __device__ __forceinline__ void tc_producer_role(const TcArgs& args, int strip, int lane,
                                                  int my_tiles, int ksteps, uint8_t* stage_base,
-                                                 uint64_t* full_b, uint64_t* empty,
+                                                 uint64_t* full, uint64_t* empty,
                                                  volatile int* flag) {
   using Tr = QTraits<QT>;
   const int total = my_tiles * ksteps;
@@ -343,7 +343,7 @@ __device__ __forceinline__ void tc_producer_role(const TcArgs& args, int strip, 
             fence_proxy_async_smem();   // generic stores -> visible to the tensor core
           }
           __syncwarp();
-          if (lane == 0) mbar_arrive(&full_b[j]);
+          if (lane == 0) mbar_arrive(&full[j]);
           // the next loads go out after the fence, which would otherwise wait for them
           if (it + STAGES < total) {
             load_next(p[j]);
@@ -386,8 +386,7 @@ tc_gateup_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
   uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kGuStages * kGuStageBytes);
-  uint64_t* full_b = full_a + kGuStages;
-  uint64_t* empty = full_b + kGuStages;
+  uint64_t* empty = full_a + kGuStages;
   uint64_t* pfull = empty + kGuStages;    // [2] partial written
   uint64_t* pempty = pfull + 2;           // [2] partial added to the registers
   uint64_t* sfull = pempty + 2;           // [2] corrections of a tile written
@@ -406,8 +405,8 @@ tc_gateup_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGuStages; ++s) {
-      mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], kGuProducers);
+      // one barrier per stage: the TMA thread's byte count and every producer
+      mbar_init(&full_a[s], 1 + kGuProducers);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -458,7 +457,7 @@ tc_gateup_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
             // the promoters' reads of this partial (and of S) precede the MMAs
             tc_fence_after();
           }
-          if (!mbar_wait(&full_b[s], phase) || !mbar_wait(&full_a[s], phase)) {
+          if (!mbar_wait(&full_a[s], phase)) {
             tc_fail(flag, args.status);
             ok = false;
             break;
@@ -491,7 +490,7 @@ tc_gateup_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
     }
   } else if (warp < kGuProm0) {
     tc_producer_role<QT, 0, kGuStages, kGuStageBytes, 2 * kATile, kGuBTile>(
-        args, warp - 2, lane, my_tiles, ksteps, stage_base, full_b, empty, flag);
+        args, warp - 2, lane, my_tiles, ksteps, stage_base, full_a, empty, flag);
   } else {
     // promoters: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (tile rows)
     // and owns gate columns [32 hh, 32 hh + 32) and the matching up columns
@@ -596,8 +595,7 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
       (reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
   uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kTcStages * kStageBytes);
-  uint64_t* full_b = full_a + kTcStages;
-  uint64_t* empty = full_b + kTcStages;
+  uint64_t* empty = full_a + kTcStages;
   uint64_t* tfull = empty + kTcStages;    // accumulators written
   uint64_t* tempty = tfull + 1;           // accumulators read out
   uint64_t* drain = tempty + 1;           // the issuer's last MMAs
@@ -616,8 +614,7 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], kTcProducers);
+      mbar_init(&full_a[s], 1 + kTcProducers);
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
@@ -655,10 +652,10 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
         // the epilogue's tensor-memory reads of the previous tile precede these MMAs
         tc_fence_after();
         for (int kk = 0; kk < ksteps && ok; ++kk) {
-          // the weight tile (producer warps) usually completes after the TMA copy;
-          // the barriers order the producers' proxy-fenced stores and the TMA
-          // bytes before the MMAs' shared-memory reads
-          if (!mbar_wait(&full_b[s], phase) || !mbar_wait(&full_a[s], phase)) {
+          // the stage's one barrier (the TMA bytes and every weight producer)
+          // orders the producers' proxy-fenced stores and the TMA bytes before
+          // the MMAs' shared-memory reads
+          if (!mbar_wait(&full_a[s], phase)) {
             tc_fail(flag, args.status);
             ok = false;
             break;
@@ -687,7 +684,7 @@ tc_down_kernel(const __grid_constant__ CUtensorMap amap, const TcArgs args) {
     }
   } else if (warp < kTcEpi0) {
     tc_producer_role<QT, 1, kTcStages, kStageBytes, 2 * kATile, kBTile>(
-        args, warp - kTcProd0, lane, my_tiles, ksteps, stage_base, full_b, empty, flag);
+        args, warp - kTcProd0, lane, my_tiles, ksteps, stage_base, full_a, empty, flag);
   } else {
     // epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31 (= tile rows)
     const int q = warp & 3;
